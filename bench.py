@@ -1,0 +1,450 @@
+#!/usr/bin/env python3
+"""Benchmark of libtinycublas_b200 on its headline workload (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--dtype f16|bf16]
+
+Workload: the Llama-3.1-8B-shaped prefill projection set at 512 tokens, issued as
+ggml-cuda issues it: cublasGemmEx(T, N, m = out features, n = 512, k = in features, fp16 weights
+N(0, 0.02^2), fp16 activations N(0, 1), f32 C, COMPUTE_32F). One step = the 8 projections Q 4096->4096,
+K 4096->1024, V 4096->1024, O 4096->4096, gate and up 4096->14336, down 14336->4096, lm_head
+4096->128256 (761.2 GFLOP). Synthetic seeded data of those shapes; weights are random, not a checkpoint.
+Inputs are larger than L2 (1.9 GB touched per step), so no flush is needed between steps.
+
+At N > 1 (torchrun, one process per GPU, NCCL): every projection is N-sharded along m (the weight's
+output features); each rank computes its m/N rows, an NCCL all-gather on a second stream replicates C
+(overlapped with the next projection), and a gather kernel lays the blocks out as the column-major C.
+Total work is fixed, so scaling is "strong".
+
+Keys beyond the base contract: roofline (dominant kernel = the lm_head GEMM), cpu_baseline (the
+oracle's multithreaded fp16 GEMM on the host, a stand-in for ggml-cpu), e2e (the same step through the
+public API with host buffers: H2D of the step's activations and D2H of the last token's logits), per
+projection figures, and decode (n <= 8) HBM bandwidth figures.
+
+--impl reference runs the same step through the reference's own libtinycublas (its cublas.c and gemm.cu,
+compiled from source for sm_100a by oracle/build_ref.sh): the reference's implementation of this path
+is GPU code, so it is timed on the same B200.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+TOKENS = 512
+HIDDEN, KV, FFN, VOCAB = 4096, 1024, 14336, 128256
+# (name, m = out features, k = in features, which activation feeds it)
+PROJECTIONS = [
+    ("q", HIDDEN, HIDDEN, "x"), ("k", KV, HIDDEN, "x"), ("v", KV, HIDDEN, "x"), ("o", HIDDEN, HIDDEN, "x"),
+    ("gate", FFN, HIDDEN, "x"), ("up", FFN, HIDDEN, "x"), ("down", HIDDEN, FFN, "h"), ("lm_head", VOCAB, HIDDEN, "x"),
+]
+STEP_FLOP = sum(2.0 * m * TOKENS * k for _, m, k, _ in PROJECTIONS)
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d["bf16_tflops_sustained"], "source": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 100 ms while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.samples = []
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def mark(self, begin: bool):
+        if begin:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = [s for t, s in self.samples if self.t0 is None or (self.t0 - 0.15 <= t <= (self.t1 or t) + 0.15)]
+        if not rows:
+            rows = [s for _, s in self.samples]
+        sm, smax, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            p = [x.strip() for x in r.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sm.append(float(p[1]))
+                smax = max(smax, float(p[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, p[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(torch, rank, world, dtype, seed=1234):
+    """Weights (this rank's m/world rows of each projection, stored k x m: op T, lda = k) and activations."""
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    acts = {
+        "x": (torch.randn(TOKENS, HIDDEN, device="cuda", generator=g)).to(dtype).contiguous(),  # B: k x n, ldb = k
+        "h": (torch.randn(TOKENS, FFN, device="cuda", generator=g)).to(dtype).contiguous(),
+    }
+    layers = []
+    for name, m, k, src in PROJECTIONS:
+        mp = m // world
+        w = torch.empty(mp, k, device="cuda", dtype=dtype)  # row r of w = output feature r: k contiguous
+        gw = torch.Generator(device="cuda")
+        gw.manual_seed(seed * 131 + sum(map(ord, name)) * 7 + rank)
+        w.copy_(torch.randn(mp, k, device="cuda", generator=gw) * 0.02)
+        c = torch.empty(mp * TOKENS if world > 1 else m * TOKENS, device="cuda", dtype=torch.float32)
+        layers.append({"name": name, "m": m, "mp": mp, "k": k, "src": src, "w": w, "c_local": c})
+    return acts, layers
+
+
+def gemm_call(h, cb, layer, act, ctype, out_ptr, ldc):
+    k, mp = layer["k"], layer["mp"]
+    return h.gemm_ex(cb.CUBLAS_OP_T, cb.CUBLAS_OP_N, mp, TOKENS, k, 1.0, layer["w"].data_ptr(), ctype, k,
+                     act.data_ptr(), ctype, k, 0.0, out_ptr, cb.CUDA_R_32F, ldc, cb.CUBLAS_COMPUTE_32F)
+
+
+def run_cpu_baseline():
+    """The oracle's fp16 GEMM on the host cores, on a bounded sample of the workload: the Q, K, V and O
+    projections of one step (41.9 GFLOP)."""
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(5)
+    x = O.to_bits(rng.normal(0, 1, HIDDEN * TOKENS).astype(np.float32), O.F16)
+    total, t = 0.0, 0.0
+    for name, m, k, _ in PROJECTIONS[:4]:
+        w = O.to_bits(rng.normal(0, 0.02, m * k).astype(np.float32), O.F16)
+        c = np.empty(m * TOKENS, np.float32)
+        t0 = time.perf_counter()
+        O.cpu_gemm_f16_tn(m, TOKENS, k, w, k, x, k, c, m, 0)
+        t += time.perf_counter() - t0
+        total += 2.0 * m * TOKENS * k
+    cores = O.max_threads()
+    return {"value": round(total / t / 1e12, 5), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": "Q, K, V, O projections of one step (41.9 GFLOP), fp16 in, f32 out, oracle/gemm_oracle.c "
+                      "orc_cpu_gemm_f16_tn (F16C + AVX2 FMA + OpenMP; stand-in for ggml-cpu, absent from the tree)",
+            "seconds": round(t, 3)}
+
+
+def decode_figures(torch, lib, cb, dtype_code, dtype):
+    """Config 4: n in {1, 2, 4, 8} against the four weight shapes, HBM GB/s of the skinny kernel.
+    Weight copies rotate so that the bytes touched per pass exceed twice L2."""
+    out = {}
+    h = lib.handle()
+    s = torch.cuda.current_stream()
+    h.set_stream(s.cuda_stream)
+    for (m, k) in [(4096, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]:
+        wbytes = m * k * 2
+        copies = max(1, min(16, (300 << 20) // wbytes + 1))
+        ws = [torch.randn(m, k, device="cuda").mul_(0.02).to(dtype) for _ in range(copies)]
+        for n in (1, 2, 4, 8):
+            x = torch.randn(n, k, device="cuda").to(dtype)
+            c = torch.empty(m * n, device="cuda")
+            reps = max(4 * copies, 20)
+
+            def one(i):
+                return h.gemm_ex(1, 0, m, n, k, 1.0, ws[i % copies].data_ptr(), dtype_code, k, x.data_ptr(),
+                                 dtype_code, k, 0.0, c.data_ptr(), cb.CUDA_R_32F, m, cb.CUBLAS_COMPUTE_32F)
+            for i in range(copies):
+                one(i)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(s)
+            for i in range(reps):
+                one(i)
+            e1.record(s)
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            byts = m * k * 2 + n * k * 2 + m * n * 4
+            out[f"{m}x{k}_n{n}"] = {"us": round(us, 2), "GB/s": round(byts / us / 1e3, 1)}
+        del ws
+    h.close()
+    return out
+
+
+def run(args):
+    import torch
+    import torch.distributed as dist
+    from macuda_b200 import cublas as cb
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
+    if args.impl == "reference":
+        from oracle import oracle as O
+        lib = O.reference_library()
+        if lib is None:
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libtinycublas_ref.so was not built "
+                                  "(needs the reference tree at build time)"}))
+            return 0
+        if world > 1:  # the reference is single-GPU: rank 0 alone runs it
+            dist.barrier()
+            if rank != 0:
+                dist.destroy_process_group()
+                return 0
+            world = 1
+    else:
+        lib = cb.library()
+    dtype = torch.float16 if args.dtype == "f16" else torch.bfloat16
+    ctype = cb.CUDA_R_16F if args.dtype == "f16" else cb.CUDA_R_16BF
+    acts, layers = make_inputs(torch, rank, world, dtype)
+    stream = torch.cuda.Stream()
+    comm = torch.cuda.Stream() if world > 1 else None
+    h = lib.handle()
+    h.set_stream(stream.cuda_stream)
+    full = {}
+    if world > 1:
+        for L in layers:
+            full[L["name"]] = {"gathered": torch.empty(L["m"] * TOKENS, device="cuda"),
+                               "c": torch.empty(L["m"] * TOKENS, device="cuda")}
+    done_ev = [torch.cuda.Event() for _ in layers]
+    gemm_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in layers]
+    per_gemm_ms = [0.0] * len(layers)
+    launches_per_step = len(layers) * (2 if world > 1 else 1)
+
+    def step(timed_gemms=False):
+        for i, L in enumerate(layers):
+            act = acts[L["src"]]
+            ldc = L["mp"] if world > 1 else L["m"]
+            if timed_gemms:
+                gemm_ev[i][0].record(stream)
+            st = gemm_call(h, cb, L, act, ctype, L["c_local"].data_ptr(), ldc)
+            if timed_gemms:
+                gemm_ev[i][1].record(stream)
+            if st != 0:
+                raise RuntimeError(f"{L['name']}: cublasGemmEx status {st}")
+            if world > 1:
+                done_ev[i].record(stream)
+                comm.wait_event(done_ev[i])
+                with torch.cuda.stream(comm):
+                    dist.all_gather_into_tensor(full[L["name"]]["gathered"], L["c_local"])
+                    lib.lib.tb200_gather_row_blocks(full[L["name"]]["gathered"].data_ptr(), world, L["mp"], TOKENS, 4,
+                                                    full[L["name"]]["c"].data_ptr(), L["m"], comm.cuda_stream)
+        if world > 1:
+            stream.wait_stream(comm)
+
+    # warm-up
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local) if not args.no_clocks else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.mark(True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    if clocks:
+        clocks.mark(False)
+    if world > 1:
+        dist.barrier()
+    ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clock_info = clocks.stop() if clocks else None
+
+    # per-projection device times, measured inside a separate pass of the same steps
+    reps = max(3, min(args.steps, 50))
+    for _ in range(reps):
+        step(timed_gemms=True)
+        torch.cuda.synchronize()
+        for i in range(len(layers)):
+            per_gemm_ms[i] += gemm_ev[i][0].elapsed_time(gemm_ev[i][1]) / reps
+    value = STEP_FLOP / (ms * 1e-3) / 1e12
+
+    pk = peaks()
+    dom = layers.index(next(L for L in layers if L["name"] == "lm_head"))
+    L = layers[dom]
+    dom_flop = 2.0 * L["mp"] * TOKENS * L["k"]
+    dom_tflops = dom_flop / (per_gemm_ms[dom] * 1e-3) / 1e12
+    traffic = None
+    prof = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if os.path.exists(prof) and world == 1 and args.impl == "ours":
+        try:
+            with open(prof) as f:
+                traffic = json.load(f).get("lm_head_dram_bytes")
+        except Exception:
+            traffic = None
+    roofline = {"bound": "tensor", "achieved": round(dom_tflops, 2), "peak": pk["bf16_tflops_sustained"],
+                "unit": "TFLOP/s", "frac": round(dom_tflops / pk["bf16_tflops_sustained"], 4), "traffic": traffic,
+                "kernel": "lm_head GEMM (%d x %d x %d)" % (L["mp"], TOKENS, L["k"]),
+                "peak_source": pk["source"] + " bf16 sustained (cuBLAS 8192^3, MEASURED_PEAKS.json)",
+                "frac_of_burst": round(dom_tflops / pk["bf16_tflops"], 4),
+                "algorithmic_bytes": L["mp"] * L["k"] * 2 + TOKENS * L["k"] * 2 + L["mp"] * TOKENS * 4}
+
+    shapes = {Lx["name"]: {"m": Lx["mp"], "n": TOKENS, "k": Lx["k"], "us": round(per_gemm_ms[i] * 1e3, 2),
+                           "TFLOP/s": round(2.0 * Lx["mp"] * TOKENS * Lx["k"] / (per_gemm_ms[i] * 1e-3) / 1e12, 1)}
+              for i, Lx in enumerate(layers)}
+
+    # e2e through the public API with host buffers: each step copies its activations from pinned host
+    # memory (double-buffered on a copy stream, overlapping the previous step) and reads back the last
+    # token's logits
+    e2e = None
+    if world == 1:
+        hx = [acts["x"].cpu().pin_memory(), acts["h"].cpu().pin_memory()]
+        dev_bufs = [[torch.empty_like(acts["x"]), torch.empty_like(acts["h"])] for _ in range(2)]
+        logits = torch.empty(VOCAB, dtype=torch.float32).pin_memory()
+        copy = torch.cuda.Stream()
+        ready = [torch.cuda.Event() for _ in range(2)]
+        free = [torch.cuda.Event() for _ in range(2)]
+        lm = layers[dom]
+        n_e2e = max(3, min(args.steps, 100))
+
+        def e2e_step(i):
+            b = i % 2
+            with torch.cuda.stream(copy):
+                copy.wait_event(free[b])
+                dev_bufs[b][0].copy_(hx[0], non_blocking=True)
+                dev_bufs[b][1].copy_(hx[1], non_blocking=True)
+                ready[b].record(copy)
+            stream.wait_event(ready[b])
+            for L2 in layers:
+                act = dev_bufs[b][0] if L2["src"] == "x" else dev_bufs[b][1]
+                st = gemm_call(h, cb, L2, act, ctype, L2["c_local"].data_ptr(), L2["m"])
+                if st != 0:
+                    raise RuntimeError("e2e gemm failed")
+            free[b].record(stream)
+            with torch.cuda.stream(stream):
+                logits.copy_(lm["c_local"][(TOKENS - 1) * lm["m"]:TOKENS * lm["m"]], non_blocking=True)
+
+        for i in range(3):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        f0.record(stream)
+        t_wall = time.perf_counter()
+        for i in range(n_e2e):
+            e2e_step(i)
+        f1.record(stream)
+        torch.cuda.synchronize()
+        t_wall = time.perf_counter() - t_wall
+        e2e_ms = f0.elapsed_time(f1) / n_e2e
+        e2e = {"value": round(STEP_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+               "h2d_bytes_per_step": int(hx[0].numel() * 2 + hx[1].numel() * 2), "d2h_bytes_per_step": VOCAB * 4,
+               "ms_per_step": round(e2e_ms, 4), "wall_ms_per_step": round(t_wall * 1e3 / n_e2e, 4), "steps": n_e2e}
+
+    cpu = None
+    if rank == 0 and world == 1 and args.impl == "ours" and not args.no_cpu_baseline:
+        try:
+            cpu = run_cpu_baseline()
+        except Exception as ex:  # the baseline is reported, never required
+            cpu = {"error": str(ex)[:200]}
+
+    decode = None
+    if rank == 0 and world == 1 and not args.no_decode:
+        decode = decode_figures(torch, lib, cb, ctype, dtype)
+
+    h.close()
+    if rank == 0:
+        line = {
+            "metric": "GEMM TFLOP/s (Llama-3.1-8B prefill projection set, 512 tokens, fp16 -> f32, ggml's T,N call)",
+            "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": args.dtype, "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) activations; no checkpoint)",
+            "config": {"workload": "llama3.1-8b prefill projections q,k,v,o,gate,up,down,lm_head @ 512 tokens "
+                                   "(BASELINE configs[1])", "tokens": TOKENS, "step_gflop": round(STEP_FLOP / 1e9, 1),
+                       "parallelism": f"N-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (1.9 GB per step); no flush"},
+            "frac_of_peak": round(value / pk["bf16_tflops_sustained"], 4),
+            "roofline": roofline, "shapes": shapes, "gpu_launches": launches_per_step * args.steps,
+        }
+        if args.impl == "reference":
+            line["impl"] = "reference"
+            line["cpu_baseline"] = {"value": line["value"], "unit": "TFLOP/s", "cores": 0, "kind": "reference",
+                                    "sample": "the whole step through the reference's own libtinycublas (cublas.c + "
+                                              "gemm.cu compiled from source for sm_100a) on one B200; the reference's "
+                                              "implementation of this path is GPU code, it has no CPU implementation"}
+            line["e2e"] = {"value": line["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+            line["gpu_launches"] = None
+        else:
+            line["cpu_baseline"] = cpu
+            line["e2e"] = e2e
+        if clock_info:
+            line["clocks"] = clock_info
+        if decode:
+            line["decode"] = decode
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    return run(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

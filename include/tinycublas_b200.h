@@ -1,0 +1,147 @@
+/* tinycublas_b200.h - the C ABI of libtinycublas_b200.so, the B200 (sm_100a) GEMM library.
+ *
+ * The library exports the cuBLAS v2 entry points that llama.cpp's ggml-cuda calls, with the exact
+ * signatures of CUDA 12.9's cublas_v2.h, so it links in place of libcublas (or of macuda's
+ * libtinycublas) without a source change on the caller's side. Every declaration below names the
+ * reference interface it replaces, as path:line inside the Davinchy/macuda tree.
+ *
+ * Conventions shared by every GEMM entry point (the cuBLAS ones):
+ *   C = alpha * op(A) * op(B) + beta * C, column-major, op(X) = X or X^T.
+ *   A, B, C and pointer arrays are caller-owned DEVICE memory; alpha and beta are HOST pointers read
+ *   in the compute type (half under CUBLAS_COMPUTE_16F*, float otherwise).
+ *   Launches are asynchronous on the handle's stream. No entry point synchronises the host, reads
+ *   device memory back, or allocates on the GEMM path, so every call can be captured in a CUDA graph.
+ *
+ * Status codes:
+ *   CUBLAS_STATUS_SUCCESS            launched (or nothing to do: m, n or batch is 0)
+ *   CUBLAS_STATUS_NOT_INITIALIZED    NULL handle
+ *   CUBLAS_STATUS_INVALID_VALUE      negative sizes, a leading dimension below its minimum, an
+ *                                    operation other than N or T
+ *   CUBLAS_STATUS_NOT_SUPPORTED      a type / compute-type combination outside the contract
+ *                                    (reference cuda-shim/libtinycublas/cublas.c:118-134)
+ *   CUBLAS_STATUS_EXECUTION_FAILED   the CUDA launch failed
+ */
+#ifndef TINYCUBLAS_B200_H
+#define TINYCUBLAS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+#include <cublas_v2.h> /* cuBLAS types: cublasHandle_t, cublasStatus_t, cublasOperation_t, ... */
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- handle lifecycle ------------------------------------------------------------------------- */
+
+/* replaces cuda-shim/libtinycublas/cublas.c:242-244. Allocates the handle on the host only; it
+ * binds the legacy default stream and records the current device. Touches no device memory. */
+cublasStatus_t cublasCreate_v2(cublasHandle_t *handle);
+
+/* replaces cublas.c:245-247. Frees the handle and any workspace the library allocated for it. */
+cublasStatus_t cublasDestroy_v2(cublasHandle_t handle);
+
+/* replaces cublas.c:248. NULL selects the legacy default stream. */
+cublasStatus_t cublasSetStream_v2(cublasHandle_t handle, cudaStream_t stream);
+
+/* replaces cublas.c:249. Unlike the reference (which stores and ignores it), the mode is honoured:
+ * CUBLAS_TF32_TENSOR_OP_MATH lets fp32 GEMMs run on the TF32 tensor cores; the default and
+ * CUBLAS_PEDANTIC_MATH keep them in fp32. */
+cublasStatus_t cublasSetMathMode(cublasHandle_t handle, cublasMath_t mode);
+
+/* replaces cublas.c:288 (a no-op there). Records a caller-owned device workspace; this library's
+ * kernels do not need one, so the pointer is kept only for cublasGetWorkspace-style introspection. */
+cublasStatus_t cublasSetWorkspace_v2(cublasHandle_t handle, void *workspace, size_t workspaceSizeInBytes);
+
+/* replaces cublas.c:286-287 */
+const char *cublasGetStatusString(cublasStatus_t status);
+
+/* ---- GEMM ------------------------------------------------------------------------------------ */
+
+/* replaces cublas.c:250-253. fp32 GEMM: fp32 FMA by default, TF32 tensor cores under
+ * CUBLAS_TF32_TENSOR_OP_MATH (the reference always used TF32, cuda-shim/libtinycublas/gemm.cu:143-221). */
+cublasStatus_t cublasSgemm_v2(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb,
+                              int m, int n, int k, const float *alpha, const float *A, int lda,
+                              const float *B, int ldb, const float *beta, float *C, int ldc);
+
+/* replaces cublas.c:254-259. In/out types f32, f16, bf16; fp32 accumulation always (also under
+ * CUBLAS_COMPUTE_16F, which reads alpha/beta as half and requires an f16 C, as cuBLAS does). */
+cublasStatus_t cublasGemmEx(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb,
+                            int m, int n, int k, const void *alpha, const void *A, cudaDataType Atype, int lda,
+                            const void *B, cudaDataType Btype, int ldb, const void *beta, void *C,
+                            cudaDataType Ctype, int ldc, cublasComputeType_t computeType, cublasGemmAlgo_t algo);
+
+/* replaces cublas.c:261-280. Strides in elements of the respective type; a stride of 0 broadcasts
+ * one matrix to the whole batch. One launch for the whole batch. */
+cublasStatus_t cublasGemmStridedBatchedEx(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb,
+                                          int m, int n, int k, const void *alpha, const void *A, cudaDataType Atype,
+                                          int lda, long long int strideA, const void *B, cudaDataType Btype, int ldb,
+                                          long long int strideB, const void *beta, void *C, cudaDataType Ctype,
+                                          int ldc, long long int strideC, int batchCount,
+                                          cublasComputeType_t computeType, cublasGemmAlgo_t algo);
+
+/* replaces cublas.c:308-313 (and its helper `batched`, cublas.c:292-303). The pointer arrays are
+ * read ON THE DEVICE by the kernel: no device-to-host copy, no stream synchronisation, one launch. */
+cublasStatus_t cublasGemmBatchedEx(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb,
+                                   int m, int n, int k, const void *alpha, const void *const Aarray[],
+                                   cudaDataType Atype, int lda, const void *const Barray[], cudaDataType Btype,
+                                   int ldb, const void *beta, void *const Carray[], cudaDataType Ctype, int ldc,
+                                   int batchCount, cublasComputeType_t computeType, cublasGemmAlgo_t algo);
+
+/* replaces cublas.c:289-291 */
+cublasStatus_t cublasSgemmStridedBatched(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb,
+                                         int m, int n, int k, const float *alpha, const float *A, int lda,
+                                         long long int strideA, const float *B, int ldb, long long int strideB,
+                                         const float *beta, float *C, int ldc, long long int strideC, int batchCount);
+
+/* replaces cublas.c:304-307 */
+cublasStatus_t cublasSgemmBatched(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb,
+                                  int m, int n, int k, const float *alpha, const float *const Aarray[], int lda,
+                                  const float *const Barray[], int ldb, const float *beta, float *const Carray[],
+                                  int ldc, int batchCount);
+
+/* replaces cublas.c:314-333 and the kernel gemm.cu:41-49. X * A = alpha * B in place in B, with A
+ * upper-triangular, non-unit, not transposed (the case ggml's solve_tri issues); other cases return
+ * NOT_SUPPORTED, as in the reference. Pointer arrays read on the device, one launch. */
+cublasStatus_t cublasStrsmBatched(cublasHandle_t handle, cublasSideMode_t side, cublasFillMode_t uplo,
+                                  cublasOperation_t trans, cublasDiagType_t diag, int m, int n, const float *alpha,
+                                  const float *const A[], int lda, float *const B[], int ldb, int batchCount);
+
+/* ---- library extensions (no cuBLAS counterpart) ------------------------------------------------ */
+
+/* Which kernel family a GEMM of this shape and type goes to on a device with `num_sms` SMs, without
+ * launching anything. Mirrors the role of the reference's test hook tinycublas_splitk_plan
+ * (cublas.c:69-78): a pure function the host-only tests pin row by row.
+ * Returns one of the TB200_KERNEL_* values; *tile_n receives the tensor-core tile width (0 if none). */
+enum { TB200_KERNEL_NONE = 0, TB200_KERNEL_SIMT = 1, TB200_KERNEL_SKINNY = 2, TB200_KERNEL_TC = 3 };
+int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_type, int out_type,
+               int tf32, int ptr_array, int aligned, int num_sms, int *tile_n);
+
+/* The persistent tensor-core kernel's tile width choice (64, 128 or 256) for an m x n x batch GEMM on
+ * `num_sms` SMs. Pure function, pinned by host-only tests. */
+int tb200_tc_tile_n(int m, int n, int batch, int num_sms);
+
+/* Last error a kernel of this library recorded on the current device (0 = none): a bounded wait in
+ * the tensor-core pipeline that gave up (1), or an internal inconsistency (2). Reading it clears it.
+ * Synchronises the current device. */
+int tb200_device_error(void);
+
+/* Gather the row blocks of an N-sharded GEMM into C: `parts` holds P column-major blocks, block r of
+ * size rows x n with leading dimension rows (the NCCL all-gather output); block r lands in rows
+ * [r*rows, (r+1)*rows) of C (ldc). elem_bytes is 2 or 4. Asynchronous on `stream`. */
+cublasStatus_t tb200_gather_row_blocks(const void *parts, int P, int rows, int n, int elem_bytes, void *C,
+                                       int ldc, cudaStream_t stream);
+
+/* HBM probes, the counterparts of gemm.cu:421-431: stream n4 16-byte writes of v, or n4 16-byte
+ * reads folded into *sink. Asynchronous on `stream`. */
+cublasStatus_t tb200_bw_write(void *p, long long n4, float v, cudaStream_t stream);
+cublasStatus_t tb200_bw_read(const void *p, long long n4, float *sink, cudaStream_t stream);
+
+/* Build identification: "tinycublas_b200 <git describe> sm_100a". */
+const char *tb200_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

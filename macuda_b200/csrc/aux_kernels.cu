@@ -1,0 +1,116 @@
+// aux_kernels.cu - the small kernels beside the GEMMs: batched triangular solve, the row-block
+// gather used after an N-sharded GEMM's all-gather, HBM bandwidth probes, and device queries.
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include "tb200_internal.h"
+#include "../../include/tinycublas_b200.h"
+
+namespace {
+
+// X * A = alpha * B, in place in B (X overwrites B), A n x n upper-triangular non-unit (lda),
+// B rows x n (ldb), column-major; one thread per row of X, forward substitution over the columns.
+// The case ggml's solve_tri issues through cublasStrsmBatched (reference gemm.cu:41-49); here one
+// launch covers the whole batch and the pointer arrays are read on the device.
+__global__ void tb200_trsm_rupn_kernel(const float *const *Aarr, float *const *Barr, int rows, int n, int lda, int ldb,
+                                       float alpha, int z0) {
+  const int b = blockIdx.y + z0;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows) return;
+  const float *A = Aarr[b];
+  float *X = Barr[b];
+  for (int j = 0; j < n; ++j) {
+    float acc = alpha * X[i + (long long)j * ldb];
+    for (int l = 0; l < j; ++l) acc = fmaf(-X[i + (long long)l * ldb], A[l + (long long)j * lda], acc);
+    X[i + (long long)j * ldb] = acc / A[j + (long long)j * lda];
+  }
+}
+
+// parts: P blocks of rows x n, each column-major with ld = rows, back to back; block r goes to rows
+// [r*rows, (r+1)*rows) of C. Consecutive threads walk rows, so reads and writes coalesce.
+template <typename E>
+__global__ void tb200_gather_rows_kernel(const E *parts, int P, int rows, int n, E *C, int ldc) {
+  const long long total = (long long)P * rows * n;
+  for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
+    const long long per = (long long)rows * n;
+    const int r = (int)(e / per);
+    const long long w = e - (long long)r * per;
+    const int col = (int)(w / rows), i = (int)(w - (long long)col * rows);
+    C[(long long)r * rows + i + (long long)col * ldc] = parts[e];
+  }
+}
+
+__global__ void tb200_bw_write_kernel(float4 *p, long long n4, float v) {
+  const float4 val = make_float4(v, v, v, v);
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x)
+    p[i] = val;
+}
+
+__global__ void tb200_bw_read_kernel(const float4 *p, long long n4, float *sink) {
+  float acc = 0.f;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+    const float4 x = __ldcs(p + i);
+    acc += x.x + x.y + x.z + x.w;
+  }
+  if (acc == 1.234567e30f) *sink = acc;  // keeps the loads; practically never true
+}
+
+}  // namespace
+
+extern "C" int tb200_num_sms(void) {
+  static int cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 0 || dev >= 64) return 148;
+  if (!cache[dev]) {
+    int v = 0;
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || v <= 0) v = 148;
+    cache[dev] = v;
+  }
+  return cache[dev];
+}
+
+extern "C" int tb200_launch_trsm_rupn(const float *const *A, float *const *B, int rows, int n, int lda, int ldb,
+                                      float alpha, int batch, cudaStream_t s) {
+  const unsigned gx = (unsigned)((rows + 127) / 128);
+  for (int z0 = 0; z0 < batch; z0 += 65535) {
+    const unsigned gy = (unsigned)(batch - z0 < 65535 ? batch - z0 : 65535);
+    tb200_trsm_rupn_kernel<<<dim3(gx, gy, 1), 128, 0, s>>>(A, B, rows, n, lda, ldb, alpha, z0);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+  }
+  return 0;
+}
+
+static unsigned grid_for(long long work, int threads) {
+  long long g = (work + threads - 1) / threads;
+  const long long cap = (long long)tb200_num_sms() * 8;
+  if (g > cap) g = cap;
+  return (unsigned)(g < 1 ? 1 : g);
+}
+
+extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_gather_row_blocks(const void *parts, int P, int rows, int n, int elem_bytes, void *C,
+                                                  int ldc, cudaStream_t stream) {
+  if (P <= 0 || rows < 0 || n < 0 || ldc < P * rows || (elem_bytes != 2 && elem_bytes != 4))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (rows == 0 || n == 0) return CUBLAS_STATUS_SUCCESS;
+  const long long total = (long long)P * rows * n;
+  const unsigned g = grid_for(total, 256);
+  if (elem_bytes == 4)
+    tb200_gather_rows_kernel<float><<<g, 256, 0, stream>>>((const float *)parts, P, rows, n, (float *)C, ldc);
+  else
+    tb200_gather_rows_kernel<unsigned short>
+        <<<g, 256, 0, stream>>>((const unsigned short *)parts, P, rows, n, (unsigned short *)C, ldc);
+  return cudaGetLastError() == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_bw_write(void *p, long long n4, float v, cudaStream_t stream) {
+  if (n4 <= 0) return CUBLAS_STATUS_SUCCESS;
+  tb200_bw_write_kernel<<<grid_for(n4, 256), 256, 0, stream>>>((float4 *)p, n4, v);
+  return cudaGetLastError() == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_bw_read(const void *p, long long n4, float *sink, cudaStream_t stream) {
+  if (n4 <= 0) return CUBLAS_STATUS_SUCCESS;
+  tb200_bw_read_kernel<<<grid_for(n4, 256), 256, 0, stream>>>((const float4 *)p, n4, sink);
+  return cudaGetLastError() == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}

@@ -1,0 +1,182 @@
+// gemm_skinny.cu - decode-shaped GEMMs (n <= 8) with the weight under op T: a bandwidth-bound path.
+//
+// C (m x n, n <= 8) = alpha * A^T B + beta * C with A stored k x m (each output row's k weights are
+// contiguous) and B stored k x n. Every byte of A is read exactly once, so the kernel is bound by
+// HBM bandwidth; its job is to keep enough 128-bit loads in flight and to keep the arithmetic off
+// the critical path. Replaces the reference's split-K tc2k kernels (cuda-shim/libtinycublas/
+// gemm.cu:317-348, :408-415) and their plan (cublas.c:69-78) for these shapes.
+//
+// Decomposition: one CTA per 16 output rows (and batch element), 8 warps splitting k in 32-wide
+// chunks (warp w takes chunks w, w+8, ...). Per chunk a lane (g = lane/4, c = lane%4) issues two
+// 16-byte loads of A (rows g and g+8, k = 8c..8c+7) and one 16-byte load of B (column g), and the
+// warp multiplies them on the tensor cores with two mma.m16n8k16 (fp32 accumulate). The k order
+// inside a chunk is permuted identically for A and B, which leaves every dot product unchanged and
+// lets the fragments come straight from 128-bit loads. The 8 warps' partial tiles are summed in
+// shared memory in warp order, so the result is deterministic, needs no global workspace, no
+// counters and no second launch (the reference's split-K needed all three, and its per-handle
+// workspace raced across streams: splitk-20260923/burst-3090.out).
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include "tb200_internal.h"
+#include "tb200_device.cuh"
+
+using namespace tb200;
+
+namespace {
+
+constexpr int SK_WARPS = 8;
+constexpr int SK_T = SK_WARPS * 32;
+constexpr int SK_ROWS = 16;
+constexpr int SK_UNROLL = 4;
+
+__device__ __forceinline__ uint4 ld_stream_v4(const void *p) {  // read once: no L1 allocation
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint4 ld_cached_v4(const void *p) { return __ldg((const uint4 *)p); }
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1);
+template <>
+__device__ __forceinline__ void mma16816<__half>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                                 uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gemm_t g, int z0) {
+  __shared__ float red[SK_WARPS][SK_ROWS][8];
+  const int b = blockIdx.y + z0;
+  const T *A = g.Aarr ? (const T *)g.Aarr[b] : (const T *)g.A + (long long)b * g.sA;
+  const T *B = g.Barr ? (const T *)g.Barr[b] : (const T *)g.B + (long long)b * g.sB;
+  const int osz = g.out_type == 0 ? 4 : 2;
+  char *C = g.Carr ? (char *)g.Carr[b] : (char *)g.C + (long long)b * g.sC * osz;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gi = lane >> 2, ci = lane & 3;
+  const int row0 = blockIdx.x * SK_ROWS;
+  const int ra = row0 + gi, rb = row0 + gi + 8;
+  const bool ok_a = ra < g.m, ok_b = rb < g.m, ok_col = gi < g.n;
+  // rows past m and columns past n read row/column 0 (always valid) and are discarded
+  const T *pa = A + (long long)(ok_a ? ra : 0) * g.lda + 8 * ci;
+  const T *pb = A + (long long)(ok_b ? rb : 0) * g.lda + 8 * ci;
+  const T *pB = B + (long long)(ok_col ? gi : 0) * g.ldb + 8 * ci;
+  float d[4] = {0.f, 0.f, 0.f, 0.f};
+  const int nchunks = g.k >> 5;  // whole 32-wide chunks; the host guarantees k % 8 == 0
+  const bool vec = (((uintptr_t)A | (uintptr_t)B) & 15) == 0;  // pointer-array elements may be unaligned
+  if (vec) {
+    int j = warp;
+    for (; j + (SK_UNROLL - 1) * SK_WARPS < nchunks; j += SK_UNROLL * SK_WARPS) {
+      uint4 va[SK_UNROLL], vb[SK_UNROLL], vB[SK_UNROLL];
+#pragma unroll
+      for (int u = 0; u < SK_UNROLL; ++u) {
+        const long long off = (long long)(j + u * SK_WARPS) * 32;
+        va[u] = ld_stream_v4(pa + off);
+        vb[u] = ld_stream_v4(pb + off);
+        vB[u] = ld_cached_v4(pB + off);
+      }
+#pragma unroll
+      for (int u = 0; u < SK_UNROLL; ++u) {
+        if (!ok_col) vB[u] = make_uint4(0, 0, 0, 0);
+        mma16816<T>(d, va[u].x, vb[u].x, va[u].y, vb[u].y, vB[u].x, vB[u].y);
+        mma16816<T>(d, va[u].z, vb[u].z, va[u].w, vb[u].w, vB[u].z, vB[u].w);
+      }
+    }
+    for (; j < nchunks; j += SK_WARPS) {
+      const long long off = (long long)j * 32;
+      uint4 va = ld_stream_v4(pa + off), vb = ld_stream_v4(pb + off), vB = ld_cached_v4(pB + off);
+      if (!ok_col) vB = make_uint4(0, 0, 0, 0);
+      mma16816<T>(d, va.x, vb.x, va.y, vb.y, vB.x, vB.y);
+      mma16816<T>(d, va.z, vb.z, va.w, vb.w, vB.z, vB.w);
+    }
+    // tail of k % 32 (a multiple of 8): lanes whose 8-wide group lies inside k load it, others zero
+    const int kt = nchunks * 32;
+    if (warp == 0 && kt < g.k) {
+      const bool in = kt + 8 * ci < g.k;
+      uint4 va = in ? ld_stream_v4(pa + kt) : make_uint4(0, 0, 0, 0);
+      uint4 vb = in ? ld_stream_v4(pb + kt) : make_uint4(0, 0, 0, 0);
+      uint4 vB = (in && ok_col) ? ld_cached_v4(pB + kt) : make_uint4(0, 0, 0, 0);
+      mma16816<T>(d, va.x, vb.x, va.y, vb.y, vB.x, vB.y);
+      mma16816<T>(d, va.z, vb.z, va.w, vb.w, vB.z, vB.w);
+    }
+  } else {
+    // unaligned pointer-array element: scalar fp32 dot products, same reduction below
+    float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
+    const int c0 = 2 * ci;
+    for (int kk = warp; kk < g.k; kk += SK_WARPS) {
+      const float x0 = ok_a ? to_f32(A[(long long)ra * g.lda + kk]) : 0.f;
+      const float x1 = ok_b ? to_f32(A[(long long)rb * g.lda + kk]) : 0.f;
+      const float y0 = c0 < g.n ? to_f32(B[(long long)c0 * g.ldb + kk]) : 0.f;
+      const float y1 = c0 + 1 < g.n ? to_f32(B[(long long)(c0 + 1) * g.ldb + kk]) : 0.f;
+      acc[0][0] = fmaf(x0, y0, acc[0][0]);
+      acc[0][1] = fmaf(x0, y1, acc[0][1]);
+      acc[1][0] = fmaf(x1, y0, acc[1][0]);
+      acc[1][1] = fmaf(x1, y1, acc[1][1]);
+    }
+    d[0] = acc[0][0]; d[1] = acc[0][1]; d[2] = acc[1][0]; d[3] = acc[1][1];
+  }
+  // accumulator fragment: d0, d1 = (row g, cols 2c, 2c+1); d2, d3 = (row g+8, same cols)
+  red[warp][gi][2 * ci] = d[0];
+  red[warp][gi][2 * ci + 1] = d[1];
+  red[warp][gi + 8][2 * ci] = d[2];
+  red[warp][gi + 8][2 * ci + 1] = d[3];
+  __syncthreads();
+  if (threadIdx.x < SK_ROWS * 8) {
+    const int r = threadIdx.x & 15, col = threadIdx.x >> 4;
+    const int row = row0 + r;
+    if (row < g.m && col < g.n) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < SK_WARPS; ++w) sum += red[w][r][col];
+      const long long idx = row + (long long)col * g.ldc;
+      float v = g.alpha * sum;
+      if (g.beta != 0.f) v += g.beta * load_out(C, idx, g.out_type);
+      store_out(C, idx, v, g.out_type);
+    }
+  }
+}
+
+}  // namespace
+
+extern "C" int tb200_skinny_ok(const tb200_gemm_t *g) {
+  if (g->in_type != TB200_F16 && g->in_type != TB200_BF16) return 0;
+  if (g->n > 8 || g->opA != 1 || g->opB != 0 || g->k % 8 != 0) return 0;
+  if (g->lda % 8 || g->ldb % 8) return 0;
+  if (!g->Aarr && ((((uintptr_t)g->A) | ((uintptr_t)g->B)) & 15)) return 0;
+  if (!g->Aarr && g->batch > 1 && ((g->sA % 8) || (g->sB % 8))) return 0;
+  return 1;
+}
+
+extern "C" int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s) {
+  if (!tb200_skinny_ok(g)) return tb200_launch_simt(g, s);
+  const long long gx = (g->m + SK_ROWS - 1) / SK_ROWS;
+  if (gx > 0x7fffffffLL) return (int)cudaErrorInvalidConfiguration;
+  for (int z0 = 0; z0 < g->batch; z0 += 65535) {
+    const unsigned gy = (unsigned)(g->batch - z0 < 65535 ? g->batch - z0 : 65535);
+    if (tb200_trace())
+      fprintf(stderr, "[trace] launch tb200_gemm_skinny grid=(%lld,%u,1) block=(%d,1,1) m=%d n=%d k=%d out=%d\n", gx, gy,
+              SK_T, g->m, g->n, g->k, g->out_type);
+    dim3 grid((unsigned)gx, gy, 1);
+    if (g->in_type == TB200_F16) tb200_gemm_skinny_kernel<__half><<<grid, SK_T, 0, s>>>(*g, z0);
+    else tb200_gemm_skinny_kernel<__nv_bfloat16><<<grid, SK_T, 0, s>>>(*g, z0);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+  }
+  return 0;
+}

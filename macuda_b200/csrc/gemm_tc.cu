@@ -1,0 +1,441 @@
+// gemm_tc.cu - the persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+// C = alpha * op(A) op(B) + beta * C, column-major, f16/bf16 inputs (kind::f16) or f32 inputs on the
+// TF32 path (kind::tf32), fp32 accumulation in tensor memory, f32/f16/bf16 C. Replaces the
+// reference's wmma + cp.async template tinyblas_gemm_tc2 and its 24 entry points
+// (cuda-shim/libtinycublas/gemm.cu:241-415) and the first-cut tinyblas_gemm_f16_tc / f32_tc
+// (gemm.cu:61-221) for every aligned operand.
+//
+// Shape of one CTA (one per SM, persistent over output tiles of 128 x BN):
+//   warp 0      TMA producer: one thread streams A and B k-blocks (128-byte rows, 128B swizzle)
+//               into a STAGES-deep shared-memory ring, signalling full[s] by transaction count.
+//   warp 1      owns tensor memory (allocates 2*BN columns: two accumulators) and one thread issues
+//               tcgen05.mma for each k-block, then tcgen05.commit frees the smem stage (empty[s]);
+//               after a tile's last k-block a commit publishes the accumulator (tfull[a]).
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time from the accumulator, apply
+//               alpha/beta, convert, store straight to column-major C (consecutive lanes hold
+//               consecutive rows, so every store instruction of a warp is contiguous), then release
+//               the accumulator (tempty[a]) so the MMA warp can start the tile after next.
+// The two accumulators let the epilogue of tile i overlap the main loop of tile i+1.
+//
+// Operand layouts (no transposes materialised): op(A) is K-major when A is stored k x m (op T, the
+// ggml call) and MN-major when stored m x k (op N); op(B) is K-major when B is stored k x n (op N)
+// and MN-major when stored n x k (op T). Both majors are fed to the tensor core through the
+// instruction descriptor's major bits and matching smem descriptors. Strided batches use rank-3
+// tensor maps (batch = third coordinate); a stride of 0 broadcasts through a rank-2 map.
+//
+// No TMA multicast anywhere: every CTA loads its own tiles, and L2 absorbs the reuse.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+#include <stdio.h>
+#include "tb200_internal.h"
+#include "tb200_device.cuh"
+
+using namespace tb200;
+
+__device__ int g_tb200_err;  // error word: 1 = a pipeline wait gave up
+
+namespace {
+
+constexpr int TC_BM = 128;
+constexpr int TC_THREADS = 192;
+constexpr uint64_t WAIT_BUDGET_NS = 2000000000ull;  // 2 s: far beyond any legitimate wait
+constexpr uint64_t DRAIN_BUDGET_NS = 200000000ull;
+
+struct TcParams {
+  int m, n, k, batch;
+  int num_kb;
+  int m_tiles, n_tiles;
+  long long tiles_per_batch, total_tiles;
+  int group_m;
+  float alpha, beta;
+  void *C;
+  int ldc;
+  long long sC;
+  int out_type;
+  int a_mn, b_mn;            // 1 = MN-major smem tile (m or n contiguous)
+  int a_batched, b_batched;  // rank-3 tensor map
+  uint32_t idesc;
+  uint32_t a_lbo, a_sbo, a_kstep;
+  uint32_t b_lbo, b_sbo, b_kstep;
+  int epr;   // elements per 128-byte row: 64 for 16-bit, 32 for f32
+  int bk;    // k elements per stage (= epr)
+};
+
+template <int BN>
+struct TcCfg {
+  static constexpr int A_BYTES = TC_BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES_RAW = 196608 / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+};
+
+__device__ __forceinline__ void decode_tile(const TcParams &p, long long t, int &b, int &mt, int &nt) {
+  b = (int)(t / p.tiles_per_batch);
+  long long r = t - (long long)b * p.tiles_per_batch;
+  const long long group_tiles = (long long)p.group_m * p.n_tiles;
+  const int g = (int)(r / group_tiles);
+  const int first_m = g * p.group_m;
+  int gm = p.m_tiles - first_m;
+  if (gm > p.group_m) gm = p.group_m;
+  const int local = (int)(r - (long long)g * group_tiles);
+  mt = first_m + local % gm;
+  nt = local / gm;
+}
+
+template <int KIND, int BN>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tb200_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const TcParams p) {
+  using Cfg = TcCfg<BN>;
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment of the shared-window offset: the 128B swizzle atom is 8 rows x 128 bytes
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint8_t *smA = smem;
+  uint8_t *smB = smem + STAGES * Cfg::A_BYTES;
+  uint64_t *bars = (uint64_t *)(smem + STAGES * Cfg::STAGE_BYTES);
+  uint64_t *full = bars;
+  uint64_t *empty = bars + STAGES;
+  uint64_t *tfull = bars + 2 * STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *drain = tempty + 2;
+  uint32_t *tmem_slot = (uint32_t *)(drain + 1);
+  volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      uint32_t issued = 0, issued_par = 0;  // per stage: a fill is outstanding, and its phase parity
+      const uint32_t tx = (uint32_t)Cfg::STAGE_BYTES;
+      for (long long t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
+        int b, mt, nt;
+        decode_tile(p, t, b, mt, nt);
+        const int m0 = mt * TC_BM, n0 = nt * BN;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, WAIT_BUDGET_NS)) break;
+          mbar_arrive_expect_tx(&full[s], tx);
+          const int k0 = kb * p.bk;
+          uint8_t *dA = smA + s * Cfg::A_BYTES;
+          uint8_t *dB = smB + s * Cfg::B_BYTES;
+          if (!p.a_mn) {
+            if (p.a_batched) tma_load_3d(dA, &tmA, &full[s], k0, m0, b);
+            else tma_load_2d(dA, &tmA, &full[s], k0, m0);
+          } else {
+            for (int j = 0; j < TC_BM / p.epr; ++j) {
+              uint8_t *d = dA + j * p.bk * 128;
+              if (p.a_batched) tma_load_3d(d, &tmA, &full[s], m0 + j * p.epr, k0, b);
+              else tma_load_2d(d, &tmA, &full[s], m0 + j * p.epr, k0);
+            }
+          }
+          if (!p.b_mn) {
+            if (p.b_batched) tma_load_3d(dB, &tmB, &full[s], k0, n0, b);
+            else tma_load_2d(dB, &tmB, &full[s], k0, n0);
+          } else {
+            for (int j = 0; j < BN / p.epr; ++j) {
+              uint8_t *d = dB + j * p.bk * 128;
+              if (p.b_batched) tma_load_3d(d, &tmB, &full[s], n0 + j * p.epr, k0, b);
+              else tma_load_2d(d, &tmB, &full[s], n0 + j * p.epr, k0);
+            }
+          }
+          issued |= 1u << s;
+          issued_par = (issued_par & ~(1u << s)) | (ph << s);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (*abort_flag) {  // let every copy still in flight land before the CTA's smem goes away
+        volatile int no_abort = 0;
+        for (int q = 0; q < STAGES; ++q)
+          if (issued & (1u << q)) (void)mbar_wait(&full[q], (issued_par >> q) & 1u, &no_abort, DRAIN_BUDGET_NS);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int acc = 0;
+      uint32_t aph = 0;
+      const uint32_t a_base = smem_u32(smA), b_base = smem_u32(smB);
+      for (long long t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, WAIT_BUDGET_NS)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(&full[s], ph, abort_flag, WAIT_BUDGET_NS)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = a_base + (uint32_t)(s * Cfg::A_BYTES);
+          const uint32_t sb = b_base + (uint32_t)(s * Cfg::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {  // BK / UMMA_K = 4 for both kinds (64/16, 32/8)
+            const uint64_t ad = smem_desc_sw128(sa + kk * p.a_kstep, p.a_lbo, p.a_sbo);
+            const uint64_t bd = smem_desc_sw128(sb + kk * p.b_kstep, p.b_lbo, p.b_sbo);
+            if (KIND == 0) umma_f16(d_tmem, ad, bd, p.idesc, (kb | kk) != 0);
+            else umma_tf32(d_tmem, ad, bd, p.idesc, (kb | kk) != 0);
+          }
+          umma_commit(&empty[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) aph ^= 1u;
+      }
+      // every MMA issued above has completed once this commit arrives
+      umma_commit(drain);
+      volatile int no_abort = 0;
+      (void)mbar_wait(drain, 0, &no_abort, DRAIN_BUDGET_NS);
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    int acc = 0;
+    uint32_t aph = 0;
+    const int osz = p.out_type == 0 ? 4 : 2;
+    for (long long t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      int b, mt, nt;
+      decode_tile(p, t, b, mt, nt);
+      // one lane waits, the warp follows its verdict: tcgen05.ld below needs the whole warp converged
+      int got = 0;
+      if (lane == 0) got = mbar_wait(&tfull[acc], aph, abort_flag, WAIT_BUDGET_NS) ? 1 : 0;
+      got = __shfl_sync(0xffffffffu, got, 0);
+      if (!got) break;
+      tc_fence_after();
+      const int row = mt * TC_BM + quad * 32 + lane;
+      const int n0 = nt * BN;
+      char *Cb = (char *)p.C + (long long)b * p.sC * osz;
+      const bool row_ok = row < p.m;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+        tmem_ld_wait();
+        const int col0 = n0 + c * 32;
+        if (row_ok && col0 < p.n) {
+          const int ncols = p.n - col0 < 32 ? p.n - col0 : 32;
+          if (p.beta == 0.f) {
+            if (p.out_type == 0 && p.alpha == 1.f) {
+              float *dst = (float *)Cb + row + (long long)col0 * p.ldc;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols) dst[(long long)j * p.ldc] = __uint_as_float(r[j]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols)
+                  store_out(Cb, row + (long long)(col0 + j) * p.ldc, p.alpha * __uint_as_float(r[j]), p.out_type);
+            }
+          } else {
+            float old[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              old[j] = j < ncols ? load_out(Cb, row + (long long)(col0 + j) * p.ldc, p.out_type) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols)
+                store_out(Cb, row + (long long)(col0 + j) * p.ldc, p.alpha * __uint_as_float(r[j]) + p.beta * old[j],
+                          p.out_type);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) aph ^= 1u;
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_tb200_err, 1);
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static int tried = 0;
+  if (!fn && !tried) {
+    tried = 1;
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+  }
+  return fn;
+}
+
+// rank-2 (batch stride 0 or batch 1) or rank-3 tiled map with a 128-byte-wide, 128B-swizzled box
+bool make_map(CUtensorMap *tm, CUtensorMapDataType dt, int esz, const void *base, long long d0, long long d1,
+              long long ld, int batch, long long bstride, int box0, int box1, int *batched) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (!enc) return false;
+  const bool b3 = batch > 1 && bstride != 0;
+  cuuint64_t dims[3] = {(cuuint64_t)d0, (cuuint64_t)d1, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * esz), (cuuint64_t)(bstride * esz)};
+  cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(tm, dt, b3 ? 3 : 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  *batched = b3 ? 1 : 0;
+  return r == CUDA_SUCCESS;
+}
+
+template <int KIND, int BN>
+int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, int num_sms, cudaStream_t s) {
+  using Cfg = TcCfg<BN>;
+  auto kern = tb200_gemm_tc_kernel<KIND, BN>;
+  static int attr_done[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    attr_done[dev] = 1;
+  }
+  long long grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
+  if (tb200_trace())
+    fprintf(stderr, "[trace] launch tb200_gemm_tc<%s,%d> grid=(%lld,1,1) block=(%d,1,1) smem=%d stages=%d m=%d n=%d k=%d batch=%d\n",
+            KIND ? "tf32" : "f16", BN, grid, TC_THREADS, Cfg::SMEM_BYTES, Cfg::STAGES, p.m, p.n, p.k, p.batch);
+  kern<<<(unsigned)grid, TC_THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, p);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace
+
+extern "C" int tb200_tc_ok(const tb200_gemm_t *g) {
+  const int es = g->in_type == TB200_F32 ? 4 : 2;
+  if (g->Aarr || g->Barr || g->Carr) return 0;
+  if (g->k <= 0) return 0;
+  if (((long long)g->lda * es) % 16 || ((long long)g->ldb * es) % 16) return 0;
+  if (((uintptr_t)g->A & 15) || ((uintptr_t)g->B & 15)) return 0;
+  if (g->batch > 1 && (((g->sA * es) % 16) || ((g->sB * es) % 16))) return 0;
+  return 1;
+}
+
+extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int num_sms, cudaStream_t s) {
+  if (!tb200_tc_ok(g)) return tb200_launch_simt(g, s);
+  const bool f32in = g->in_type == TB200_F32;
+  const int es = f32in ? 4 : 2;
+  const int epr = 128 / es;
+  int bn = tile_n;
+  if (bn != 32 && bn != 64 && bn != 128 && bn != 256) bn = 128;
+  const int b_mn = g->opB == 1, a_mn = g->opA == 0;
+  if (b_mn && bn < epr) bn = epr;  // an MN-major B tile holds whole 128-byte rows
+  const CUtensorMapDataType dt =
+      f32in ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+            : (g->in_type == TB200_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+
+  TcParams p;
+  memset(&p, 0, sizeof p);
+  CUtensorMap ta, tb;
+  bool ok;
+  if (!a_mn) ok = make_map(&ta, dt, es, g->A, g->k, g->m, g->lda, g->batch, g->sA, epr, TC_BM, &p.a_batched);
+  else ok = make_map(&ta, dt, es, g->A, g->m, g->k, g->lda, g->batch, g->sA, epr, epr, &p.a_batched);
+  if (ok) {
+    if (!b_mn) ok = make_map(&tb, dt, es, g->B, g->k, g->n, g->ldb, g->batch, g->sB, epr, bn, &p.b_batched);
+    else ok = make_map(&tb, dt, es, g->B, g->n, g->k, g->ldb, g->batch, g->sB, epr, epr, &p.b_batched);
+  }
+  if (!ok) {
+    if (tb200_trace()) fprintf(stderr, "[trace] tensor map refused; SIMT kernel instead\n");
+    return tb200_launch_simt(g, s);
+  }
+  p.m = g->m; p.n = g->n; p.k = g->k; p.batch = g->batch;
+  p.epr = epr;
+  p.bk = epr;
+  p.num_kb = (g->k + p.bk - 1) / p.bk;
+  p.m_tiles = (g->m + TC_BM - 1) / TC_BM;
+  p.n_tiles = (g->n + bn - 1) / bn;
+  p.tiles_per_batch = (long long)p.m_tiles * p.n_tiles;
+  p.total_tiles = p.tiles_per_batch * g->batch;
+  p.group_m = 8;
+  p.alpha = g->alpha; p.beta = g->beta;
+  p.C = g->C; p.ldc = g->ldc; p.sC = g->sC; p.out_type = g->out_type;
+  p.a_mn = a_mn; p.b_mn = b_mn;
+  // K-major: 8-row core groups 1024 bytes apart, UMMA_K step = 32 bytes inside the swizzle atom.
+  // MN-major: 128-byte rows along m/n, 8 k-rows per 1024-byte atom (SBO), atoms along m/n one box
+  // (bk rows x 128 bytes) apart (LBO), UMMA_K step = UMMA_K rows of 128 bytes.
+  const uint32_t umma_k = 32 / es;
+  p.a_lbo = a_mn ? (uint32_t)(p.bk * 128) : 16u;
+  p.a_sbo = 1024u;
+  p.a_kstep = a_mn ? umma_k * 128u : 32u;
+  p.b_lbo = b_mn ? (uint32_t)(p.bk * 128) : 16u;
+  p.b_sbo = 1024u;
+  p.b_kstep = b_mn ? umma_k * 128u : 32u;
+  const uint32_t fmt = f32in ? 2u : (g->in_type == TB200_BF16 ? 1u : 0u);
+  p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
+            ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+
+  if (f32in) {
+    switch (bn) {
+      case 32: return launch_bn<1, 32>(ta, tb, p, num_sms, s);
+      case 64: return launch_bn<1, 64>(ta, tb, p, num_sms, s);
+      case 128: return launch_bn<1, 128>(ta, tb, p, num_sms, s);
+      default: return launch_bn<1, 256>(ta, tb, p, num_sms, s);
+    }
+  }
+  switch (bn) {
+    case 32: return launch_bn<0, 32>(ta, tb, p, num_sms, s);
+    case 64: return launch_bn<0, 64>(ta, tb, p, num_sms, s);
+    case 128: return launch_bn<0, 128>(ta, tb, p, num_sms, s);
+    default: return launch_bn<0, 256>(ta, tb, p, num_sms, s);
+  }
+}
+
+extern "C" __attribute__((visibility("default"))) int tb200_device_error(void) {
+  int v = 0, zero = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&v, g_tb200_err, sizeof v) != cudaSuccess) return -1;
+  cudaMemcpyToSymbol(g_tb200_err, &zero, sizeof zero);
+  return v;
+}

@@ -1,0 +1,49 @@
+/* tb200_internal.h - the seam between the C host layer (tinycublas.c) and the CUDA launchers (*.cu).
+ * Plain C types only; every launcher returns a cudaError_t as int and launches asynchronously. */
+#ifndef TB200_INTERNAL_H
+#define TB200_INTERNAL_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types, numbered as the reference's dtype_code (cuda-shim/libtinycublas/cublas.c:107) */
+enum { TB200_F32 = 0, TB200_F16 = 1, TB200_BF16 = 2 };
+
+/* One GEMM request, already validated: C = alpha * op(A) op(B) + beta * C, column-major.
+ * Exactly one of (A, Aarr) is used: Aarr != NULL means a device array of batch pointers. Strides are
+ * in elements of the operand's own type. */
+typedef struct {
+  int opA, opB;             /* 0 = N, 1 = T */
+  int m, n, k, batch;
+  float alpha, beta;
+  const void *A; int lda; long long sA; const void *const *Aarr;
+  const void *B; int ldb; long long sB; const void *const *Barr;
+  void *C; int ldc; long long sC; void *const *Carr;
+  int in_type, out_type;    /* TB200_F32 / F16 / BF16 */
+  int tf32;                 /* f32 inputs only: 1 = TF32 tensor cores allowed */
+} tb200_gemm_t;
+
+int tb200_launch_simt(const tb200_gemm_t *g, cudaStream_t s);
+int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s);
+int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int num_sms, cudaStream_t s);
+int tb200_launch_trsm_rupn(const float *const *A, float *const *B, int rows, int n, int lda, int ldb, float alpha,
+                           int batch, cudaStream_t s);
+
+/* properties of the current device, cached per device ordinal */
+int tb200_num_sms(void);
+
+/* eligibility rules shared by the planner and the launchers */
+int tb200_skinny_ok(const tb200_gemm_t *g);
+int tb200_tc_ok(const tb200_gemm_t *g);
+
+int tb200_trace(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,375 @@
+/* tinycublas.c - the cuBLAS v2 C ABI subset ggml-cuda calls, on the B200 kernels of this library.
+ *
+ * Host layer of libtinycublas_b200.so. It owns the handle, the type contract, the alpha/beta decoding
+ * and the choice of kernel; the CUDA launchers live in the .cu files behind tb200_internal.h. The
+ * file is compiled against CUDA's own cublas_v2.h, so the compiler checks every exported signature
+ * against the real cuBLAS prototypes, as the reference does (cuda-shim/libtinycublas/cublas.c:9).
+ *
+ * Differences from the reference's host layer (cuda-shim/libtinycublas/cublas.c), by design:
+ *   - pointer-array batches are read on the device (reference: device-to-host copy + stream sync +
+ *     one launch per element, cublas.c:292-303);
+ *   - nothing here allocates device memory or synchronises, so every call is graph-capturable
+ *     (the reference's split-K path bypassed capture, cublas.c:170);
+ *   - cublasSetMathMode is honoured for fp32 GEMMs (the reference stored it and always used TF32,
+ *     cublas.c:218, :249);
+ *   - the kernel plan reads the device's SM count (the reference hard-codes the RTX 5090's 170,
+ *     cublas.c:73, :151).
+ */
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+#include <cublas_v2.h>
+#include "tb200_internal.h"
+#include "../../include/tinycublas_b200.h"
+
+#ifndef TB200_GIT_DESCRIBE
+#define TB200_GIT_DESCRIBE "unknown"
+#endif
+
+struct tb200_handle {
+  cudaStream_t stream;
+  cublasMath_t math_mode;
+  int device;
+  void *user_ws;
+  size_t user_ws_bytes;
+};
+
+/* ---- environment knobs, read once (the reference's TINYCUBLAS_TC / TINYCUBLAS_GEMM bisect knobs,
+ * cublas.c:79-81, under this library's own names) ---- */
+static int env_flag(const char *name, int dflt) {
+  const char *e = getenv(name);
+  if (!e || !*e) return dflt;
+  return *e != '0';
+}
+int tb200_trace(void) {
+  static int v = -1;
+  if (v < 0) v = env_flag("TB200_TRACE", 0);
+  return v;
+}
+static int tc_enabled(void) {     /* TB200_TC=0: no tensor-core kernel, everything on the SIMT kernel */
+  static int v = -1;
+  if (v < 0) v = env_flag("TB200_TC", 1);
+  return v;
+}
+static int skinny_enabled(void) { /* TB200_SKINNY=0: decode shapes go to the tensor-core kernel */
+  static int v = -1;
+  if (v < 0) v = env_flag("TB200_SKINNY", 1);
+  return v;
+}
+
+/* ---- type contract: reference cublas.c:107-134, restated ---- */
+static int dtype_code(cudaDataType t) {
+  return t == CUDA_R_32F ? TB200_F32 : t == CUDA_R_16F ? TB200_F16 : t == CUDA_R_16BF ? TB200_BF16 : -1;
+}
+
+/* IEEE binary16 bits -> float, exact (every half is a float) */
+static float half_bits_to_float(uint16_t h) {
+  uint32_t sign = (uint32_t)(h >> 15) << 31, e = (h >> 10) & 0x1fu, f = h & 0x3ffu, bits;
+  if (e == 0x1f) {
+    bits = sign | 0x7f800000u | (f << 13);
+  } else if (e == 0) {
+    if (f == 0) {
+      bits = sign;
+    } else { /* subnormal: renormalise */
+      int shift = 0;
+      while (!(f & 0x400u)) { f <<= 1; shift++; }
+      f &= 0x3ffu;
+      bits = sign | ((uint32_t)(127 - 15 + 1 - shift) << 23) | (f << 13);
+    }
+  } else {
+    bits = sign | ((e + 127 - 15) << 23) | (f << 13);
+  }
+  float out;
+  memcpy(&out, &bits, 4);
+  return out;
+}
+
+static int is_c16(cublasComputeType_t ct) { return ct == CUBLAS_COMPUTE_16F || ct == CUBLAS_COMPUTE_16F_PEDANTIC; }
+
+/* alpha/beta live on the host in the compute type */
+static float read_scalar(const void *p, cublasComputeType_t ct) {
+  return is_c16(ct) ? half_bits_to_float(*(const uint16_t *)p) : *(const float *)p;
+}
+
+/* A and B of one type; a compute type cuBLAS defines for it; C as that compute type allows.
+ *   f32:  32F, 32F_PEDANTIC, 32F_FAST_TF32, 32F_FAST_16F, 32F_FAST_16BF
+ *   f16:  32F, 32F_PEDANTIC, or 16F / 16F_PEDANTIC with an f16 C
+ *   bf16: 32F, 32F_PEDANTIC
+ * Returns 0 and the codes, or -1 (NOT_SUPPORTED). *tf32 says whether an f32 GEMM may use TF32. */
+static int gemm_contract(cudaDataType At, cudaDataType Bt, cudaDataType Ct, cublasComputeType_t ct, int *in, int *out,
+                         int *tf32) {
+  *in = dtype_code(At);
+  *out = dtype_code(Ct);
+  *tf32 = 0;
+  if (*in < 0 || *out < 0 || dtype_code(Bt) != *in) return -1;
+  int c32 = ct == CUBLAS_COMPUTE_32F || ct == CUBLAS_COMPUTE_32F_PEDANTIC;
+  if (*in == TB200_F32) {
+    if (ct == CUBLAS_COMPUTE_32F_FAST_TF32 || ct == CUBLAS_COMPUTE_32F_FAST_16F || ct == CUBLAS_COMPUTE_32F_FAST_16BF) {
+      *tf32 = 1;
+      return 0;
+    }
+    return c32 ? 0 : -1;
+  }
+  if (*in == TB200_F16) return (c32 || (is_c16(ct) && *out == TB200_F16)) ? 0 : -1;
+  return c32 ? 0 : -1;
+}
+
+/* ---- planning ---- */
+static int esize(int t) { return t == TB200_F32 ? 4 : 2; }
+
+/* the persistent tensor-core kernel's tile width: fewest waves of 128 x BN tiles, weighted by how
+ * much of its peak a BN-wide UMMA reaches. A 128 x N x 16 UMMA needs N/2 tensor cycles and reads
+ * 4 KB of A plus N x 32 B of B from shared memory (128 B per cycle), so narrow tiles are bound by
+ * shared memory: efficiency ~ min(1, (N/2) / (32 + N/4)), derated slightly at N = 128 where the two
+ * are equal. */
+int tb200_tc_tile_n(int m, int n, int batch, int num_sms) {
+  static const int bns[4] = {256, 128, 64, 32};
+  static const double eff[4] = {1.0, 0.9, 0.62, 0.38};
+  if (num_sms <= 0) num_sms = 148;
+  int best = 256;
+  double best_cost = 1e300;
+  for (int i = 0; i < 4; i++) {
+    int bn = bns[i];
+    if (bn > 32 && n <= bn / 2) continue; /* a tile at least half full */
+    long long tiles = (long long)((m + 127) / 128) * ((n + bn - 1) / bn) * (long long)batch;
+    long long waves = (tiles + num_sms - 1) / num_sms;
+    double cost = (double)waves * bn / eff[i];
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = bn;
+    }
+  }
+  return best;
+}
+
+int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_type, int out_type, int tf32,
+               int ptr_array, int aligned, int num_sms, int *tile_n) {
+  (void)out_type;
+  if (tile_n) *tile_n = 0;
+  if (m <= 0 || n <= 0 || batch <= 0) return TB200_KERNEL_NONE;
+  if (k <= 0 || !tc_enabled()) return TB200_KERNEL_SIMT;
+  int sixteen = in_type == TB200_F16 || in_type == TB200_BF16;
+  if (sixteen && n <= 8 && transa == 1 && transb == 0 && k % 8 == 0 && aligned && skinny_enabled())
+    return TB200_KERNEL_SKINNY;
+  if ((sixteen || (in_type == TB200_F32 && tf32)) && aligned && !ptr_array) {
+    int bn = tb200_tc_tile_n(m, n, batch, num_sms);
+    if (tile_n) *tile_n = bn;
+    return TB200_KERNEL_TC;
+  }
+  return TB200_KERNEL_SIMT;
+}
+
+/* base pointers 16-byte aligned, leading dimensions and strides whole multiples of 16 bytes: what a
+ * TMA tensor map and 128-bit loads need */
+static int operands_aligned(const tb200_gemm_t *g) {
+  const long long es = esize(g->in_type);
+  if (((long long)g->lda * es) % 16 || ((long long)g->ldb * es) % 16) return 0;
+  if (g->Aarr || g->Barr) return 1; /* per-element pointers are checked by the kernels that read them */
+  if (((uintptr_t)g->A & 15) || ((uintptr_t)g->B & 15)) return 0;
+  if (g->batch > 1 && (((g->sA * es) % 16) || ((g->sB * es) % 16))) return 0;
+  return 1;
+}
+
+static const char *kernel_name(int kind) {
+  return kind == TB200_KERNEL_SKINNY ? "skinny" : kind == TB200_KERNEL_TC ? "tc" : kind == TB200_KERNEL_SIMT ? "simt" : "none";
+}
+
+static cublasStatus_t run_gemm(struct tb200_handle *h, tb200_gemm_t *g) {
+  int tile_n = 0;
+  int aligned = operands_aligned(g);
+  int ptr_array = g->Aarr != NULL;
+  int sms = tb200_num_sms();
+  int kind = tb200_plan(g->opA, g->opB, g->m, g->n, g->k, g->batch, g->in_type, g->out_type, g->tf32, ptr_array,
+                        aligned, sms, &tile_n);
+  if (kind == TB200_KERNEL_TC) { /* TB200_TC_BN=32|64|128|256 forces the tile width (tests, bisecting) */
+    const char *e = getenv("TB200_TC_BN");
+    int v = e ? atoi(e) : 0;
+    if (v == 32 || v == 64 || v == 128 || v == 256) tile_n = v;
+  }
+  if (tb200_trace())
+    fprintf(stderr, "[trace] gemm %s op=%c%c m=%d n=%d k=%d batch=%d in=%d out=%d tf32=%d ptr=%d aligned=%d BN=%d\n",
+            kernel_name(kind), g->opA ? 'T' : 'N', g->opB ? 'T' : 'N', g->m, g->n, g->k, g->batch, g->in_type,
+            g->out_type, g->tf32, ptr_array, aligned, tile_n);
+  int rc = 0;
+  switch (kind) {
+    case TB200_KERNEL_NONE: return CUBLAS_STATUS_SUCCESS;
+    case TB200_KERNEL_SKINNY: rc = tb200_launch_skinny(g, h->stream); break;
+    case TB200_KERNEL_TC: rc = tb200_launch_tc(g, tile_n, sms, h->stream); break;
+    default: rc = tb200_launch_simt(g, h->stream); break;
+  }
+  if (rc != 0) {
+    fprintf(stderr, "[tinycublas_b200] %s launch failed: %s\n", kernel_name(kind), cudaGetErrorString((cudaError_t)rc));
+    return CUBLAS_STATUS_EXECUTION_FAILED;
+  }
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+static int op_code(cublasOperation_t op) { return op == CUBLAS_OP_N ? 0 : op == CUBLAS_OP_T ? 1 : -1; }
+static int imax(int a, int b) { return a > b ? a : b; }
+
+/* cuBLAS's argument rules: non-negative sizes, leading dimensions at least the stored row count */
+static cublasStatus_t check_args(int oa, int ob, int m, int n, int k, int lda, int ldb, int ldc, int batch) {
+  if (oa < 0 || ob < 0) return CUBLAS_STATUS_INVALID_VALUE;
+  if (m < 0 || n < 0 || k < 0 || batch < 0) return CUBLAS_STATUS_INVALID_VALUE;
+  if (lda < imax(1, oa == 0 ? m : k)) return CUBLAS_STATUS_INVALID_VALUE;
+  if (ldb < imax(1, ob == 0 ? k : n)) return CUBLAS_STATUS_INVALID_VALUE;
+  if (ldc < imax(1, m)) return CUBLAS_STATUS_INVALID_VALUE;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+static cublasStatus_t gemm_common(cublasHandle_t handle, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                                  const void *alpha, const void *A, const void *const *Aarr, cudaDataType At, int lda,
+                                  long long sA, const void *B, const void *const *Barr, cudaDataType Bt, int ldb,
+                                  long long sB, const void *beta, void *C, void *const *Carr, cudaDataType Ct, int ldc,
+                                  long long sC, int batch, cublasComputeType_t ct) {
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  tb200_gemm_t g;
+  memset(&g, 0, sizeof g);
+  int tf32 = 0;
+  if (gemm_contract(At, Bt, Ct, ct, &g.in_type, &g.out_type, &tf32)) return CUBLAS_STATUS_NOT_SUPPORTED;
+  g.opA = op_code(ta);
+  g.opB = op_code(tb);
+  cublasStatus_t st = check_args(g.opA, g.opB, m, n, k, lda, ldb, ldc, batch);
+  if (st != CUBLAS_STATUS_SUCCESS) return st;
+  if (!alpha || !beta) return CUBLAS_STATUS_INVALID_VALUE;
+  if (m == 0 || n == 0 || batch == 0) return CUBLAS_STATUS_SUCCESS;
+  /* an f32 GEMM may use TF32 when the compute type says so or the handle's math mode asks for it */
+  if (g.in_type == TB200_F32)
+    g.tf32 = tf32 || (((int)h->math_mode & 0xf) == CUBLAS_TF32_TENSOR_OP_MATH && ct == CUBLAS_COMPUTE_32F);
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.batch = batch;
+  g.alpha = read_scalar(alpha, ct);
+  g.beta = read_scalar(beta, ct);
+  g.A = A; g.lda = lda; g.sA = sA; g.Aarr = Aarr;
+  g.B = B; g.ldb = ldb; g.sB = sB; g.Barr = Barr;
+  g.C = C; g.ldc = ldc; g.sC = sC; g.Carr = Carr;
+  return run_gemm(h, &g);
+}
+
+/* ---- exported ABI ---- */
+
+cublasStatus_t cublasCreate_v2(cublasHandle_t *handle) {
+  if (!handle) return CUBLAS_STATUS_INVALID_VALUE;
+  struct tb200_handle *h = (struct tb200_handle *)calloc(1, sizeof *h);
+  if (!h) return CUBLAS_STATUS_ALLOC_FAILED;
+  h->stream = NULL;
+  h->math_mode = CUBLAS_DEFAULT_MATH;
+  h->device = -1;
+  (void)cudaGetDevice(&h->device); /* no context is created by this query */
+  *handle = (cublasHandle_t)h;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasDestroy_v2(cublasHandle_t handle) {
+  free(handle);
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasSetStream_v2(cublasHandle_t handle, cudaStream_t stream) {
+  if (!handle) return CUBLAS_STATUS_NOT_INITIALIZED;
+  ((struct tb200_handle *)handle)->stream = stream;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasSetMathMode(cublasHandle_t handle, cublasMath_t mode) {
+  if (!handle) return CUBLAS_STATUS_NOT_INITIALIZED;
+  ((struct tb200_handle *)handle)->math_mode = mode;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+cublasStatus_t cublasSetWorkspace_v2(cublasHandle_t handle, void *workspace, size_t bytes) {
+  if (!handle) return CUBLAS_STATUS_NOT_INITIALIZED;
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  h->user_ws = workspace;
+  h->user_ws_bytes = bytes;
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+const char *cublasGetStatusString(cublasStatus_t s) {
+  switch (s) {
+    case CUBLAS_STATUS_SUCCESS: return "CUBLAS_STATUS_SUCCESS";
+    case CUBLAS_STATUS_NOT_INITIALIZED: return "CUBLAS_STATUS_NOT_INITIALIZED";
+    case CUBLAS_STATUS_ALLOC_FAILED: return "CUBLAS_STATUS_ALLOC_FAILED";
+    case CUBLAS_STATUS_INVALID_VALUE: return "CUBLAS_STATUS_INVALID_VALUE";
+    case CUBLAS_STATUS_NOT_SUPPORTED: return "CUBLAS_STATUS_NOT_SUPPORTED";
+    case CUBLAS_STATUS_EXECUTION_FAILED: return "CUBLAS_STATUS_EXECUTION_FAILED";
+    case CUBLAS_STATUS_INTERNAL_ERROR: return "CUBLAS_STATUS_INTERNAL_ERROR";
+    default: return "CUBLAS_STATUS_UNKNOWN_ERROR";
+  }
+}
+
+cublasStatus_t cublasSgemm_v2(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                              const float *alpha, const float *A, int lda, const float *B, int ldb, const float *beta,
+                              float *C, int ldc) {
+  return gemm_common(h, ta, tb, m, n, k, alpha, A, NULL, CUDA_R_32F, lda, 0, B, NULL, CUDA_R_32F, ldb, 0, beta, C, NULL,
+                     CUDA_R_32F, ldc, 0, 1, CUBLAS_COMPUTE_32F);
+}
+
+cublasStatus_t cublasGemmEx(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                            const void *alpha, const void *A, cudaDataType At, int lda, const void *B, cudaDataType Bt,
+                            int ldb, const void *beta, void *C, cudaDataType Ct, int ldc, cublasComputeType_t ct,
+                            cublasGemmAlgo_t algo) {
+  (void)algo;
+  return gemm_common(h, ta, tb, m, n, k, alpha, A, NULL, At, lda, 0, B, NULL, Bt, ldb, 0, beta, C, NULL, Ct, ldc, 0, 1,
+                     ct);
+}
+
+cublasStatus_t cublasGemmStridedBatchedEx(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n,
+                                          int k, const void *alpha, const void *A, cudaDataType At, int lda,
+                                          long long int sA, const void *B, cudaDataType Bt, int ldb, long long int sB,
+                                          const void *beta, void *C, cudaDataType Ct, int ldc, long long int sC,
+                                          int batch, cublasComputeType_t ct, cublasGemmAlgo_t algo) {
+  (void)algo;
+  return gemm_common(h, ta, tb, m, n, k, alpha, A, NULL, At, lda, sA, B, NULL, Bt, ldb, sB, beta, C, NULL, Ct, ldc, sC,
+                     batch, ct);
+}
+
+cublasStatus_t cublasGemmBatchedEx(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                                   const void *alpha, const void *const Aarray[], cudaDataType At, int lda,
+                                   const void *const Barray[], cudaDataType Bt, int ldb, const void *beta,
+                                   void *const Carray[], cudaDataType Ct, int ldc, int batch, cublasComputeType_t ct,
+                                   cublasGemmAlgo_t algo) {
+  (void)algo;
+  if (batch > 0 && (!Aarray || !Barray || !Carray)) return CUBLAS_STATUS_INVALID_VALUE;
+  return gemm_common(h, ta, tb, m, n, k, alpha, NULL, Aarray, At, lda, 0, NULL, Barray, Bt, ldb, 0, beta, NULL, Carray,
+                     Ct, ldc, 0, batch, ct);
+}
+
+cublasStatus_t cublasSgemmStridedBatched(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n,
+                                         int k, const float *alpha, const float *A, int lda, long long int sA,
+                                         const float *B, int ldb, long long int sB, const float *beta, float *C,
+                                         int ldc, long long int sC, int batch) {
+  return gemm_common(h, ta, tb, m, n, k, alpha, A, NULL, CUDA_R_32F, lda, sA, B, NULL, CUDA_R_32F, ldb, sB, beta, C,
+                     NULL, CUDA_R_32F, ldc, sC, batch, CUBLAS_COMPUTE_32F);
+}
+
+cublasStatus_t cublasSgemmBatched(cublasHandle_t h, cublasOperation_t ta, cublasOperation_t tb, int m, int n, int k,
+                                  const float *alpha, const float *const Aarray[], int lda, const float *const Barray[],
+                                  int ldb, const float *beta, float *const Carray[], int ldc, int batch) {
+  if (batch > 0 && (!Aarray || !Barray || !Carray)) return CUBLAS_STATUS_INVALID_VALUE;
+  return gemm_common(h, ta, tb, m, n, k, alpha, NULL, (const void *const *)Aarray, CUDA_R_32F, lda, 0, NULL,
+                     (const void *const *)Barray, CUDA_R_32F, ldb, 0, beta, NULL, (void *const *)Carray, CUDA_R_32F, ldc,
+                     0, batch, CUBLAS_COMPUTE_32F);
+}
+
+cublasStatus_t cublasStrsmBatched(cublasHandle_t handle, cublasSideMode_t side, cublasFillMode_t uplo,
+                                  cublasOperation_t trans, cublasDiagType_t diag, int m, int n, const float *alpha,
+                                  const float *const A[], int lda, float *const B[], int ldb, int batch) {
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (side != CUBLAS_SIDE_RIGHT || uplo != CUBLAS_FILL_MODE_UPPER || trans != CUBLAS_OP_N || diag != CUBLAS_DIAG_NON_UNIT)
+    return CUBLAS_STATUS_NOT_SUPPORTED;
+  if (m < 0 || n < 0 || batch < 0 || lda < imax(1, n) || ldb < imax(1, m) || !alpha) return CUBLAS_STATUS_INVALID_VALUE;
+  if (m == 0 || n == 0 || batch == 0) return CUBLAS_STATUS_SUCCESS;
+  if (!A || !B) return CUBLAS_STATUS_INVALID_VALUE;
+  if (tb200_trace()) fprintf(stderr, "[trace] trsm_rupn m=%d n=%d batch=%d\n", m, n, batch);
+  int rc = tb200_launch_trsm_rupn(A, B, m, n, lda, ldb, *alpha, batch, h->stream);
+  return rc == 0 ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+const char *tb200_version(void) { return "tinycublas_b200 " TB200_GIT_DESCRIBE " sm_100a"; }

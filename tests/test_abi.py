@@ -1,0 +1,165 @@
+"""The C-ABI boundary on the CPU: the library loads, exports what include/tinycublas_b200.h declares,
+keeps the reference's type contract and cuBLAS's argument rules, and plans kernels as pinned.
+Nothing here launches a kernel (every call returns before any CUDA work)."""
+import ctypes
+import json
+import os
+import re
+
+import pytest
+
+from macuda_b200 import cublas as cb
+from oracle import oracle as O
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "tinycublas_b200.h")
+GOLD = os.path.join(ROOT, "tests", "golden")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^[A-Za-z_][\w \*]*?\b(\w+)\s*\(", text, flags=re.M)
+    return sorted(set(n for n in names if n not in ("if", "defined")))
+
+
+def test_header_declares_the_reference_surface():
+    names = declared_functions()
+    # the linked surface ggml-cuda needs (reference cuda-shim/Makefile:100-109 coverage rule)
+    for sym in ["cublasCreate_v2", "cublasDestroy_v2", "cublasSetStream_v2", "cublasSetMathMode", "cublasSgemm_v2",
+                "cublasGemmEx", "cublasGemmStridedBatchedEx", "cublasGemmBatchedEx", "cublasSgemmStridedBatched",
+                "cublasSgemmBatched", "cublasStrsmBatched", "cublasSetWorkspace_v2", "cublasGetStatusString"]:
+        assert sym in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    exported = set()
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", lib.path], capture_output=True, text=True, check=True).stdout
+    for line in out.splitlines():
+        parts = line.split()
+        if len(parts) == 3:
+            exported.add(parts[2])
+    missing = [n for n in declared_functions() if n not in exported]
+    assert not missing, missing
+    for n in declared_functions():
+        assert hasattr(lib.lib, n)
+
+
+def test_version_names_the_arch(lib):
+    assert "sm_100a" in lib.version()
+
+
+def test_status_strings(lib):
+    assert lib.lib.cublasGetStatusString(0) == b"CUBLAS_STATUS_SUCCESS"
+    assert lib.lib.cublasGetStatusString(15) == b"CUBLAS_STATUS_NOT_SUPPORTED"
+    assert lib.lib.cublasGetStatusString(7) == b"CUBLAS_STATUS_INVALID_VALUE"
+
+
+def test_null_handle_is_not_initialized(lib):
+    one = ctypes.c_float(1.0)
+    st = lib.lib.cublasGemmEx(None, 1, 0, 4, 4, 4, ctypes.byref(one), None, cb.CUDA_R_16F, 4, None, cb.CUDA_R_16F, 4,
+                              ctypes.byref(one), None, cb.CUDA_R_32F, 4, cb.CUBLAS_COMPUTE_32F, -1)
+    assert st == cb.CUBLAS_STATUS_NOT_INITIALIZED
+    assert lib.lib.cublasSetStream_v2(None, None) == cb.CUBLAS_STATUS_NOT_INITIALIZED
+
+
+def _contract_status(h, At, Bt, Ct, ct):
+    """All three Ex entry points on an m = 0 problem: the contract is checked, nothing launches."""
+    dummy = 256
+    s1 = h.gemm_ex(1, 0, 0, 32, 32, 1.0, dummy, At, 32, dummy, Bt, 32, 0.0, dummy, Ct, 32, ct)
+    s2 = h.gemm_strided_batched_ex(1, 0, 0, 32, 32, 1.0, dummy, At, 32, 1024, dummy, Bt, 32, 1024, 0.0, dummy, Ct, 32,
+                                   1024, 2, ct)
+    s3 = h.gemm_batched_ex(1, 0, 0, 32, 32, 1.0, dummy, At, 32, dummy, Bt, 32, 0.0, dummy, Ct, 32, 2, ct)
+    return s1, s2, s3
+
+
+with open(os.path.join(GOLD, "reference_rows.json")) as f:
+    CONTRACT_ROWS = json.load(f)["contract"]["rows"]
+
+
+@pytest.mark.parametrize("row", CONTRACT_ROWS, ids=lambda r: r[0])
+def test_contract_rows_of_the_reference(lib, row):
+    what, At, Bt, Ct, ct, want = row
+    with lib.handle() as h:
+        assert _contract_status(h, At, Bt, Ct, ct) == (want, want, want), what
+
+
+def test_contract_equals_reference_on_every_type_combination(lib):
+    types = [cb.CUDA_R_32F, cb.CUDA_R_16F, cb.CUDA_R_16BF, 1]  # 1 = CUDA_R_64F, never served
+    computes = [64, 65, 68, 69, 70, 71, 72, 73, 74, 75, 77]
+    with lib.handle() as h:
+        for At in types:
+            for Bt in types:
+                for Ct in types:
+                    for ct in computes:
+                        want = cb.CUBLAS_STATUS_SUCCESS if O.ref_contract(At, Bt, Ct, ct) == 0 else \
+                            cb.CUBLAS_STATUS_NOT_SUPPORTED
+                        assert _contract_status(h, At, Bt, Ct, ct) == (want,) * 3, (At, Bt, Ct, ct)
+
+
+@pytest.mark.parametrize("args,why", [
+    (dict(m=-1), "negative m"), (dict(n=-1), "negative n"), (dict(k=-1), "negative k"),
+    (dict(ta=2), "OP_C is not served"), (dict(lda=31), "lda < k under op T"),
+    (dict(ldb=31), "ldb < k under op N"), (dict(ldc=31), "ldc < m"),
+])
+def test_invalid_arguments(lib, args, why):
+    p = dict(ta=1, tb=0, m=32, n=32, k=32, lda=32, ldb=32, ldc=32)
+    p.update(args)
+    with lib.handle() as h:
+        st = h.gemm_ex(p["ta"], p["tb"], p["m"], p["n"], p["k"], 1.0, 256, cb.CUDA_R_16F, p["lda"], 256, cb.CUDA_R_16F,
+                       p["ldb"], 0.0, 256, cb.CUDA_R_32F, p["ldc"])
+        assert st == cb.CUBLAS_STATUS_INVALID_VALUE, why
+
+
+def test_empty_problems_succeed_without_a_device(lib):
+    with lib.handle() as h:
+        assert h.gemm_ex(1, 0, 0, 8, 8, 1.0, 256, cb.CUDA_R_16F, 8, 256, cb.CUDA_R_16F, 8, 0.0, 256, cb.CUDA_R_32F,
+                         1) == 0
+        assert h.gemm_ex(1, 0, 8, 0, 8, 1.0, 256, cb.CUDA_R_16F, 8, 256, cb.CUDA_R_16F, 8, 0.0, 256, cb.CUDA_R_32F,
+                         8) == 0
+        assert h.gemm_strided_batched_ex(1, 0, 8, 8, 8, 1.0, 256, cb.CUDA_R_16F, 8, 64, 256, cb.CUDA_R_16F, 8, 64, 0.0,
+                                         256, cb.CUDA_R_32F, 8, 64, 0) == 0
+
+
+def test_trsm_refuses_unserved_cases(lib):
+    with lib.handle() as h:
+        # the reference serves only side RIGHT, upper, no transpose, non-unit (cublas.c:317)
+        assert h.strsm_batched(cb.CUBLAS_SIDE_LEFT, 1, 0, 0, 4, 4, 1.0, 256, 4, 256, 4, 2) == 15
+        assert h.strsm_batched(cb.CUBLAS_SIDE_RIGHT, 0, 0, 0, 4, 4, 1.0, 256, 4, 256, 4, 2) == 15
+        assert h.strsm_batched(cb.CUBLAS_SIDE_RIGHT, 1, 1, 0, 4, 4, 1.0, 256, 4, 256, 4, 2) == 15
+        assert h.strsm_batched(cb.CUBLAS_SIDE_RIGHT, 1, 0, 1, 4, 4, 1.0, 256, 4, 256, 4, 2) == 15
+
+
+# (transa, transb, m, n, k, batch, in, tf32, ptr, aligned) -> (kernel, BN) on 148 SMs
+PLAN_ROWS = [
+    ("config 1: ggml fp16 T,N 4096x512x4096", (1, 0, 4096, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 128)),
+    ("config 2 K/V 1024x512x4096", (1, 0, 1024, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 32)),
+    ("config 2 gate/up 14336x512x4096", (1, 0, 14336, 512, 4096, 1, 2, 0, 0, 1), (cb.TB200_KERNEL_TC, 256)),
+    ("config 2 lm_head 128256x512x4096", (1, 0, 128256, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 256)),
+    ("config 4 decode n=1", (1, 0, 4096, 1, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_SKINNY, 0)),
+    ("config 4 decode n=8", (1, 0, 14336, 8, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_SKINNY, 0)),
+    ("n=8 under op N A goes to the tensor cores", (0, 0, 4096, 8, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 32)),
+    ("n=9 leaves the skinny path", (1, 0, 4096, 9, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 32)),
+    ("unaligned operands take the SIMT kernel", (1, 0, 48, 40, 72, 3, 1, 0, 0, 0), (cb.TB200_KERNEL_SIMT, 0)),
+    ("fp32 without TF32 math stays fp32", (0, 0, 512, 512, 512, 1, 0, 0, 0, 1), (cb.TB200_KERNEL_SIMT, 0)),
+    ("fp32 with TF32 math takes the tensor cores", (0, 0, 512, 512, 512, 1, 0, 1, 0, 1), (cb.TB200_KERNEL_TC, 32)),
+    ("pointer arrays, n=32: SIMT for now", (1, 0, 768, 32, 2048, 128, 1, 0, 1, 1), (cb.TB200_KERNEL_SIMT, 0)),
+    ("pointer arrays, n<=8: skinny", (1, 0, 768, 8, 2048, 128, 1, 0, 1, 1), (cb.TB200_KERNEL_SKINNY, 0)),
+    ("k == 0 is a scale of C", (1, 0, 64, 64, 0, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_SIMT, 0)),
+    ("empty", (1, 0, 0, 64, 64, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_NONE, 0)),
+]
+
+
+@pytest.mark.parametrize("what,args,want", PLAN_ROWS, ids=[r[0] for r in PLAN_ROWS])
+def test_plan_rows(lib, what, args, want):
+    ta, tb, m, n, k, batch, it, tf32, ptr, aligned = args
+    assert lib.plan(ta, tb, m, n, k, batch, it, 0, tf32, ptr, aligned, 148) == want, what
+
+
+def test_tile_width_fills_the_sms(lib):
+    # every choice is one of the compiled widths and never more waves than the narrowest tile needs
+    for m in (128, 1024, 4096, 14336, 128256):
+        for n in (16, 32, 64, 100, 512, 2048, 16384):
+            bn = lib.lib.tb200_tc_tile_n(m, n, 1, 148)
+            assert bn in (32, 64, 128, 256)
