@@ -207,6 +207,52 @@ def decode_figures(torch, lib, cb, dtype_code, dtype):
     return out
 
 
+def run_single(args):
+    """--gemm MxNxK: one ggml-style T,N GEMM (f32 C) repeated, for profiling one kernel in isolation.
+    Weight copies rotate so that the weights touched per pass exceed twice L2."""
+    import torch
+    from macuda_b200 import cublas as cb
+    m, n, k = (int(x) for x in args.gemm.lower().split("x"))
+    if args.impl == "reference":
+        from oracle import oracle as O
+        lib = O.reference_library()
+    else:
+        lib = cb.library()
+    dtype = torch.float16 if args.dtype == "f16" else torch.bfloat16
+    ctype = cb.CUDA_R_16F if args.dtype == "f16" else cb.CUDA_R_16BF
+    copies = max(1, min(16, -(-(300 << 20) // (m * k * 2))))
+    ws = [(torch.randn(m, k, device="cuda") * 0.02).to(dtype) for _ in range(copies)]
+    x = torch.randn(n, k, device="cuda").to(dtype)
+    c = torch.empty(m * n, device="cuda")
+    h = lib.handle()
+    s = torch.cuda.Stream()
+    h.set_stream(s.cuda_stream)
+
+    def one(i):
+        st = h.gemm_ex(1, 0, m, n, k, 1.0, ws[i % copies].data_ptr(), ctype, k, x.data_ptr(), ctype, k, 0.0,
+                       c.data_ptr(), cb.CUDA_R_32F, m, cb.CUBLAS_COMPUTE_32F)
+        if st != 0:
+            raise RuntimeError(f"cublasGemmEx status {st}")
+    for i in range(args.warmup):
+        one(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for i in range(args.steps):
+        one(i)
+    e1.record(s)
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / args.steps
+    flop = 2.0 * m * n * k
+    byts = m * k * 2 + n * k * 2 + m * n * 4
+    plan = lib.plan(1, 0, m, n, k) if args.impl == "ours" else None
+    print(json.dumps({"gemm": f"{m}x{n}x{k}", "impl": args.impl, "dtype": args.dtype, "us": round(us, 2),
+                      "TFLOP/s": round(flop / us / 1e6, 1), "GB/s": round(byts / us / 1e3, 1), "plan": plan,
+                      "weight_copies": copies, "steps": args.steps}))
+    h.close()
+    return 0
+
+
 def run(args):
     import torch
     import torch.distributed as dist
@@ -248,19 +294,21 @@ def run(args):
             full[L["name"]] = {"gathered": torch.empty(L["m"] * TOKENS, device="cuda"),
                                "c": torch.empty(L["m"] * TOKENS, device="cuda")}
     done_ev = [torch.cuda.Event() for _ in layers]
-    gemm_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in layers]
+    # per-projection device time: an event before each GEMM of every timed step, read after the timed region
+    # (the queue stays full, so each interval is that kernel's device time plus the launch gap)
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(len(layers) + 1)] for _ in range(args.steps)]
     per_gemm_ms = [0.0] * len(layers)
     launches_per_step = len(layers) * (2 if world > 1 else 1)
 
-    def step(timed_gemms=False):
+    def step(ev=None):
         for i, L in enumerate(layers):
             act = acts[L["src"]]
             ldc = L["mp"] if world > 1 else L["m"]
-            if timed_gemms:
-                gemm_ev[i][0].record(stream)
+            if ev is not None:
+                ev[i].record(stream)
             st = gemm_call(h, cb, L, act, ctype, L["c_local"].data_ptr(), ldc)
-            if timed_gemms:
-                gemm_ev[i][1].record(stream)
+            if ev is not None and i == len(layers) - 1:
+                ev[i + 1].record(stream)
             if st != 0:
                 raise RuntimeError(f"{L['name']}: cublasGemmEx status {st}")
             if world > 1:
@@ -288,8 +336,8 @@ def run(args):
     if clocks:
         clocks.mark(True)
     e0.record(stream)
-    for _ in range(args.steps):
-        step()
+    for j in range(args.steps):
+        step(marks[j])
     e1.record(stream)
     torch.cuda.synchronize()
     if clocks:
@@ -303,13 +351,9 @@ def run(args):
         ms = float(t.item())
     clock_info = clocks.stop() if clocks else None
 
-    # per-projection device times, measured inside a separate pass of the same steps
-    reps = max(3, min(args.steps, 50))
-    for _ in range(reps):
-        step(timed_gemms=True)
-        torch.cuda.synchronize()
+    for j in range(args.steps):
         for i in range(len(layers)):
-            per_gemm_ms[i] += gemm_ev[i][0].elapsed_time(gemm_ev[i][1]) / reps
+            per_gemm_ms[i] += marks[j][i].elapsed_time(marks[j][i + 1]) / args.steps
     value = STEP_FLOP / (ms * 1e-3) / 1e12
 
     pk = peaks()
@@ -440,9 +484,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--gemm", default=None, help="MxNxK: time one T,N GEMM alone (profiling)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.gemm:
+        return run_single(args)
     return run(args)
 
 

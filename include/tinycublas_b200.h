@@ -127,11 +127,12 @@ int tb200_tc_tile_n(int m, int n, int batch, int num_sms);
  * Synchronises the current device. */
 int tb200_device_error(void);
 
-/* Gather the row blocks of an N-sharded GEMM into C: `parts` holds P column-major blocks, block r of
- * size rows x n with leading dimension rows (the NCCL all-gather output); block r lands in rows
- * [r*rows, (r+1)*rows) of C (ldc). elem_bytes is 2 or 4. Asynchronous on `stream`. */
+/* Gather the row blocks of an N-sharded GEMM into C: `parts` holds P column-major blocks back to back,
+ * block r of size rows x n with leading dimension rows (the NCCL all-gather output); block r lands in
+ * rows [r*rows, (r+1)*rows) of C (ldc), and rows at or beyond m_total (the padding of the last block
+ * when m is not a multiple of P) are dropped. elem_bytes is 2 or 4. Asynchronous on `stream`. */
 cublasStatus_t tb200_gather_row_blocks(const void *parts, int P, int rows, int n, int elem_bytes, void *C,
-                                       int ldc, cudaStream_t stream);
+                                       int ldc, int m_total, cudaStream_t stream);
 
 /* HBM probes, the counterparts of gemm.cu:421-431: stream n4 16-byte writes of v, or n4 16-byte
  * reads folded into *sink. Asynchronous on `stream`. */

@@ -3,7 +3,7 @@
 #include <cuda_runtime.h>
 #include <stdio.h>
 #include "tb200_internal.h"
-#include "../../include/tinycublas_b200.h"
+#include "tinycublas_b200.h"
 
 namespace {
 
@@ -26,16 +26,18 @@ __global__ void tb200_trsm_rupn_kernel(const float *const *Aarr, float *const *B
 }
 
 // parts: P blocks of rows x n, each column-major with ld = rows, back to back; block r goes to rows
-// [r*rows, (r+1)*rows) of C. Consecutive threads walk rows, so reads and writes coalesce.
+// [r*rows, (r+1)*rows) of C, rows >= m_total dropped. Consecutive threads walk rows, so reads and writes
+// coalesce.
 template <typename E>
-__global__ void tb200_gather_rows_kernel(const E *parts, int P, int rows, int n, E *C, int ldc) {
-  const long long total = (long long)P * rows * n;
+__global__ void tb200_gather_rows_kernel(const E *parts, int P, int rows, int n, E *C, int ldc, int m_total) {
+  const long long per = (long long)rows * n;
+  const long long total = (long long)P * per;
   for (long long e = (long long)blockIdx.x * blockDim.x + threadIdx.x; e < total; e += (long long)gridDim.x * blockDim.x) {
-    const long long per = (long long)rows * n;
     const int r = (int)(e / per);
     const long long w = e - (long long)r * per;
     const int col = (int)(w / rows), i = (int)(w - (long long)col * rows);
-    C[(long long)r * rows + i + (long long)col * ldc] = parts[e];
+    const long long row = (long long)r * rows + i;
+    if (row < m_total) C[row + (long long)col * ldc] = parts[e];
   }
 }
 
@@ -88,18 +90,19 @@ static unsigned grid_for(long long work, int threads) {
   return (unsigned)(g < 1 ? 1 : g);
 }
 
-extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_gather_row_blocks(const void *parts, int P, int rows, int n, int elem_bytes, void *C,
-                                                  int ldc, cudaStream_t stream) {
-  if (P <= 0 || rows < 0 || n < 0 || ldc < P * rows || (elem_bytes != 2 && elem_bytes != 4))
+extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_gather_row_blocks(
+    const void *parts, int P, int rows, int n, int elem_bytes, void *C, int ldc, int m_total, cudaStream_t stream) {
+  if (P <= 0 || rows < 0 || n < 0 || m_total < 0 || (long long)m_total > (long long)P * rows || ldc < m_total ||
+      ldc < 1 || (elem_bytes != 2 && elem_bytes != 4))
     return CUBLAS_STATUS_INVALID_VALUE;
-  if (rows == 0 || n == 0) return CUBLAS_STATUS_SUCCESS;
+  if (rows == 0 || n == 0 || m_total == 0) return CUBLAS_STATUS_SUCCESS;
   const long long total = (long long)P * rows * n;
   const unsigned g = grid_for(total, 256);
   if (elem_bytes == 4)
-    tb200_gather_rows_kernel<float><<<g, 256, 0, stream>>>((const float *)parts, P, rows, n, (float *)C, ldc);
+    tb200_gather_rows_kernel<float><<<g, 256, 0, stream>>>((const float *)parts, P, rows, n, (float *)C, ldc, m_total);
   else
     tb200_gather_rows_kernel<unsigned short>
-        <<<g, 256, 0, stream>>>((const unsigned short *)parts, P, rows, n, (unsigned short *)C, ldc);
+        <<<g, 256, 0, stream>>>((const unsigned short *)parts, P, rows, n, (unsigned short *)C, ldc, m_total);
   return cudaGetLastError() == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
 }
 

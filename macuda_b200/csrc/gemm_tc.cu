@@ -39,13 +39,14 @@ __device__ int g_tb200_err;  // error word: 1 = a pipeline wait gave up
 namespace {
 
 constexpr int TC_BM = 128;
-constexpr int TC_THREADS = 192;
-constexpr uint64_t WAIT_BUDGET_NS = 2000000000ull;  // 2 s: far beyond any legitimate wait
-constexpr uint64_t DRAIN_BUDGET_NS = 200000000ull;
+constexpr int TC_THREADS = 224;  // 7 warps: A loads, MMA, 4 x epilogue, B loads
+// wait budgets in SM cycles (about 2 s and 0.2 s at 2 GHz): far beyond any legitimate wait
+constexpr uint64_t WAIT_BUDGET_CYC = 4000000000ull;
+constexpr uint64_t DRAIN_BUDGET_CYC = 400000000ull;
 
 struct TcParams {
   int m, n, k, batch;
-  int num_kb;
+  int num_kb;                // k-blocks of bk = KC * epr elements
   int m_tiles, n_tiles;
   long long tiles_per_batch, total_tiles;
   int group_m;
@@ -57,16 +58,21 @@ struct TcParams {
   int a_mn, b_mn;            // 1 = MN-major smem tile (m or n contiguous)
   int a_batched, b_batched;  // rank-3 tensor map
   uint32_t idesc;
-  uint32_t a_lbo, a_sbo, a_kstep;
-  uint32_t b_lbo, b_sbo, b_kstep;
+  // smem descriptor strides (bytes) of each operand, and the byte offset of UMMA step kk inside a
+  // stage: (kk / 4) * cstride + (kk % 4) * kstep
+  uint32_t a_lbo, a_sbo, b_lbo, b_sbo;
+  uint32_t a_cstride, a_kstep, b_cstride, b_kstep;
   int epr;   // elements per 128-byte row: 64 for 16-bit, 32 for f32
-  int bk;    // k elements per stage (= epr)
+  int bk;    // k elements per stage
 };
 
-template <int BN>
+// KC = 128-byte k-chunks per stage. One stage holds A (128 rows) and B (BN rows) for KC * epr values of
+// k. The producers and the MMA thread spend a few hundred cycles of issue latency per stage whatever its
+// size, so narrow tiles take two chunks per stage to keep the tensor core fed.
+template <int BN, int KC>
 struct TcCfg {
-  static constexpr int A_BYTES = TC_BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int A_BYTES = TC_BM * 128 * KC;
+  static constexpr int B_BYTES = BN * 128 * KC;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES_RAW = 196608 / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
@@ -88,11 +94,32 @@ __device__ __forceinline__ void decode_tile(const TcParams &p, long long t, int 
   nt = local / gm;
 }
 
-template <int KIND, int BN>
+// One operand's loads for one stage: `rows` (128 for A, BN for B) x KC chunks. K-major: chunk c is a
+// rows x 128-byte box at k0 + c*epr. MN-major: rows/epr boxes of epr (m or n) x KC*epr k-rows.
+template <int KC>
+__device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *tm, uint64_t *bar, int mn_major,
+                                             int batched, int rows, int epr, int mn0, int k0, int b) {
+  if (!mn_major) {
+#pragma unroll
+    for (int c = 0; c < KC; ++c) {
+      uint8_t *d = dst + c * rows * 128;
+      if (batched) tma_load_3d(d, tm, bar, k0 + c * epr, mn0, b);
+      else tma_load_2d(d, tm, bar, k0 + c * epr, mn0);
+    }
+  } else {
+    for (int j = 0; j < rows / epr; ++j) {
+      uint8_t *d = dst + j * KC * epr * 128;
+      if (batched) tma_load_3d(d, tm, bar, mn0 + j * epr, k0, b);
+      else tma_load_2d(d, tm, bar, mn0 + j * epr, k0);
+    }
+  }
+}
+
+template <int KIND, int BN, int KC>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tb200_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const TcParams p) {
-  using Cfg = TcCfg<BN>;
+  using Cfg = TcCfg<BN, KC>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment of the shared-window offset: the 128B swizzle atom is 8 rows x 128 bytes
@@ -113,7 +140,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], 2);  // one arrive.expect_tx from each producer
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -135,43 +162,27 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 6) {
+    // ------------------------------------------------------------------ TMA producers (A: warp 0, B: warp 6)
     if (lane == 0) {
+      const bool is_a = warp == 0;
+      const CUtensorMap *tm = is_a ? &tmA : &tmB;
+      uint8_t *base = is_a ? smA : smB;
+      const int stage_bytes = is_a ? Cfg::A_BYTES : Cfg::B_BYTES;
+      const int rows = is_a ? TC_BM : BN;
+      const int mn_major = is_a ? p.a_mn : p.b_mn;
+      const int batched = is_a ? p.a_batched : p.b_batched;
       int s = 0;
       uint32_t ph = 0;
       uint32_t issued = 0, issued_par = 0;  // per stage: a fill is outstanding, and its phase parity
-      const uint32_t tx = (uint32_t)Cfg::STAGE_BYTES;
       for (long long t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
         int b, mt, nt;
         decode_tile(p, t, b, mt, nt);
-        const int m0 = mt * TC_BM, n0 = nt * BN;
+        const int mn0 = is_a ? mt * TC_BM : nt * BN;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, WAIT_BUDGET_NS)) break;
-          mbar_arrive_expect_tx(&full[s], tx);
-          const int k0 = kb * p.bk;
-          uint8_t *dA = smA + s * Cfg::A_BYTES;
-          uint8_t *dB = smB + s * Cfg::B_BYTES;
-          if (!p.a_mn) {
-            if (p.a_batched) tma_load_3d(dA, &tmA, &full[s], k0, m0, b);
-            else tma_load_2d(dA, &tmA, &full[s], k0, m0);
-          } else {
-            for (int j = 0; j < TC_BM / p.epr; ++j) {
-              uint8_t *d = dA + j * p.bk * 128;
-              if (p.a_batched) tma_load_3d(d, &tmA, &full[s], m0 + j * p.epr, k0, b);
-              else tma_load_2d(d, &tmA, &full[s], m0 + j * p.epr, k0);
-            }
-          }
-          if (!p.b_mn) {
-            if (p.b_batched) tma_load_3d(dB, &tmB, &full[s], k0, n0, b);
-            else tma_load_2d(dB, &tmB, &full[s], k0, n0);
-          } else {
-            for (int j = 0; j < BN / p.epr; ++j) {
-              uint8_t *d = dB + j * p.bk * 128;
-              if (p.b_batched) tma_load_3d(d, &tmB, &full[s], n0 + j * p.epr, k0, b);
-              else tma_load_2d(d, &tmB, &full[s], n0 + j * p.epr, k0);
-            }
-          }
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, WAIT_BUDGET_CYC)) break;
+          mbar_arrive_expect_tx(&full[s], (uint32_t)stage_bytes);
+          load_operand<KC>(base + s * stage_bytes, tm, &full[s], mn_major, batched, rows, p.epr, mn0, kb * p.bk, b);
           issued |= 1u << s;
           issued_par = (issued_par & ~(1u << s)) | (ph << s);
           if (++s == STAGES) {
@@ -183,7 +194,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (*abort_flag) {  // let every copy still in flight land before the CTA's smem goes away
         volatile int no_abort = 0;
         for (int q = 0; q < STAGES; ++q)
-          if (issued & (1u << q)) (void)mbar_wait(&full[q], (issued_par >> q) & 1u, &no_abort, DRAIN_BUDGET_NS);
+          if (issued & (1u << q)) (void)mbar_wait(&full[q], (issued_par >> q) & 1u, &no_abort, DRAIN_BUDGET_CYC);
       }
     }
   } else if (warp == 1) {
@@ -193,26 +204,33 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       uint32_t ph = 0;
       int acc = 0;
       uint32_t aph = 0;
-      const uint32_t a_base = smem_u32(smA), b_base = smem_u32(smB);
+      // stage-0 descriptors, and per-step offsets in the 16-byte units of the start-address field (the
+      // sum stays inside the 14-bit field: shared memory offsets are below 256 KB)
+      const uint64_t a_desc0 = smem_desc_sw128(smem_u32(smA), p.a_lbo, p.a_sbo);
+      const uint64_t b_desc0 = smem_desc_sw128(smem_u32(smB), p.b_lbo, p.b_sbo);
+      uint32_t a_off[4 * KC], b_off[4 * KC];
+#pragma unroll
+      for (int kk = 0; kk < 4 * KC; ++kk) {
+        a_off[kk] = ((kk >> 2) * p.a_cstride + (kk & 3) * p.a_kstep) >> 4;
+        b_off[kk] = ((kk >> 2) * p.b_cstride + (kk & 3) * p.b_kstep) >> 4;
+      }
       for (long long t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
-        if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, WAIT_BUDGET_NS)) break;
+        if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, WAIT_BUDGET_CYC)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_flag, WAIT_BUDGET_NS)) {
+          if (!mbar_wait(&full[s], ph, abort_flag, WAIT_BUDGET_CYC)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = a_base + (uint32_t)(s * Cfg::A_BYTES);
-          const uint32_t sb = b_base + (uint32_t)(s * Cfg::B_BYTES);
+          const uint64_t ad0 = a_desc0 + (uint64_t)((uint32_t)(s * Cfg::A_BYTES) >> 4);
+          const uint64_t bd0 = b_desc0 + (uint64_t)((uint32_t)(s * Cfg::B_BYTES) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {  // BK / UMMA_K = 4 for both kinds (64/16, 32/8)
-            const uint64_t ad = smem_desc_sw128(sa + kk * p.a_kstep, p.a_lbo, p.a_sbo);
-            const uint64_t bd = smem_desc_sw128(sb + kk * p.b_kstep, p.b_lbo, p.b_sbo);
-            if (KIND == 0) umma_f16(d_tmem, ad, bd, p.idesc, (kb | kk) != 0);
-            else umma_tf32(d_tmem, ad, bd, p.idesc, (kb | kk) != 0);
+          for (int kk = 0; kk < 4 * KC; ++kk) {  // UMMA_K = 16 (f16/bf16) or 8 (tf32): 4 steps per chunk
+            if (KIND == 0) umma_f16(d_tmem, ad0 + a_off[kk], bd0 + b_off[kk], p.idesc, (kb | kk) != 0);
+            else umma_tf32(d_tmem, ad0 + a_off[kk], bd0 + b_off[kk], p.idesc, (kb | kk) != 0);
           }
           umma_commit(&empty[s]);
           if (++s == STAGES) {
@@ -228,7 +246,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       // every MMA issued above has completed once this commit arrives
       umma_commit(drain);
       volatile int no_abort = 0;
-      (void)mbar_wait(drain, 0, &no_abort, DRAIN_BUDGET_NS);
+      (void)mbar_wait(drain, 0, &no_abort, DRAIN_BUDGET_CYC);
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
@@ -241,7 +259,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       decode_tile(p, t, b, mt, nt);
       // one lane waits, the warp follows its verdict: tcgen05.ld below needs the whole warp converged
       int got = 0;
-      if (lane == 0) got = mbar_wait(&tfull[acc], aph, abort_flag, WAIT_BUDGET_NS) ? 1 : 0;
+      if (lane == 0) got = mbar_wait(&tfull[acc], aph, abort_flag, WAIT_BUDGET_CYC) ? 1 : 0;
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
       tc_fence_after();
@@ -331,10 +349,10 @@ bool make_map(CUtensorMap *tm, CUtensorMapDataType dt, int esz, const void *base
   return r == CUDA_SUCCESS;
 }
 
-template <int KIND, int BN>
+template <int KIND, int BN, int KC>
 int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, int num_sms, cudaStream_t s) {
-  using Cfg = TcCfg<BN>;
-  auto kern = tb200_gemm_tc_kernel<KIND, BN>;
+  using Cfg = TcCfg<BN, KC>;
+  auto kern = tb200_gemm_tc_kernel<KIND, BN, KC>;
   static int attr_done[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -345,17 +363,24 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, i
   }
   long long grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
   if (tb200_trace())
-    fprintf(stderr, "[trace] launch tb200_gemm_tc<%s,%d> grid=(%lld,1,1) block=(%d,1,1) smem=%d stages=%d m=%d n=%d k=%d batch=%d\n",
-            KIND ? "tf32" : "f16", BN, grid, TC_THREADS, Cfg::SMEM_BYTES, Cfg::STAGES, p.m, p.n, p.k, p.batch);
+    fprintf(stderr,
+            "[trace] launch tb200_gemm_tc<%s,%d,%d> grid=(%lld,1,1) block=(%d,1,1) smem=%d stages=%d m=%d n=%d k=%d "
+            "batch=%d\n",
+            KIND ? "tf32" : "f16", BN, KC, grid, TC_THREADS, Cfg::SMEM_BYTES, Cfg::STAGES, p.m, p.n, p.k, p.batch);
   kern<<<(unsigned)grid, TC_THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, p);
   return (int)cudaGetLastError();
 }
+
+// tile width BN -> k-chunks per stage: the widest tile keeps one chunk (four stages of 48 KB); narrower
+// tiles take two so that each stage carries enough tensor work to cover its issue cost
+constexpr int kc_for(int bn) { return bn >= 256 ? 1 : 2; }
 
 }  // namespace
 
 extern "C" int tb200_tc_ok(const tb200_gemm_t *g) {
   const int es = g->in_type == TB200_F32 ? 4 : 2;
   if (g->Aarr || g->Barr || g->Carr) return 0;
+  if (g->in_type == TB200_F32 && (g->opA != 1 || g->opB != 0)) return 0;  // TF32: K-major operands only
   if (g->k <= 0) return 0;
   if (((long long)g->lda * es) % 16 || ((long long)g->ldb * es) % 16) return 0;
   if (((uintptr_t)g->A & 15) || ((uintptr_t)g->B & 15)) return 0;
@@ -380,11 +405,12 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int num_sms, c
   memset(&p, 0, sizeof p);
   CUtensorMap ta, tb;
   bool ok;
+  const int kc = kc_for(bn);
   if (!a_mn) ok = make_map(&ta, dt, es, g->A, g->k, g->m, g->lda, g->batch, g->sA, epr, TC_BM, &p.a_batched);
-  else ok = make_map(&ta, dt, es, g->A, g->m, g->k, g->lda, g->batch, g->sA, epr, epr, &p.a_batched);
+  else ok = make_map(&ta, dt, es, g->A, g->m, g->k, g->lda, g->batch, g->sA, epr, epr * kc, &p.a_batched);
   if (ok) {
     if (!b_mn) ok = make_map(&tb, dt, es, g->B, g->k, g->n, g->ldb, g->batch, g->sB, epr, bn, &p.b_batched);
-    else ok = make_map(&tb, dt, es, g->B, g->n, g->k, g->ldb, g->batch, g->sB, epr, epr, &p.b_batched);
+    else ok = make_map(&tb, dt, es, g->B, g->n, g->k, g->ldb, g->batch, g->sB, epr, epr * kc, &p.b_batched);
   }
   if (!ok) {
     if (tb200_trace()) fprintf(stderr, "[trace] tensor map refused; SIMT kernel instead\n");
@@ -392,7 +418,7 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int num_sms, c
   }
   p.m = g->m; p.n = g->n; p.k = g->k; p.batch = g->batch;
   p.epr = epr;
-  p.bk = epr;
+  p.bk = epr * kc;
   p.num_kb = (g->k + p.bk - 1) / p.bk;
   p.m_tiles = (g->m + TC_BM - 1) / TC_BM;
   p.n_tiles = (g->n + bn - 1) / bn;
@@ -402,33 +428,36 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int num_sms, c
   p.alpha = g->alpha; p.beta = g->beta;
   p.C = g->C; p.ldc = g->ldc; p.sC = g->sC; p.out_type = g->out_type;
   p.a_mn = a_mn; p.b_mn = b_mn;
-  // K-major: 8-row core groups 1024 bytes apart, UMMA_K step = 32 bytes inside the swizzle atom.
-  // MN-major: 128-byte rows along m/n, 8 k-rows per 1024-byte atom (SBO), atoms along m/n one box
-  // (bk rows x 128 bytes) apart (LBO), UMMA_K step = UMMA_K rows of 128 bytes.
+  // K-major: 8-row core groups 1024 bytes apart (SBO), chunk c of a stage rows*128 bytes in, UMMA_K step
+  // = 32 bytes inside the swizzle atom. MN-major: 128-byte rows along m/n, 8 k-rows per 1024-byte atom
+  // (SBO), atoms along m/n one box (bk rows x 128 bytes) apart (LBO), UMMA_K step = UMMA_K rows of 128
+  // bytes, and a stage's chunks follow each other inside the box.
   const uint32_t umma_k = 32 / es;
   p.a_lbo = a_mn ? (uint32_t)(p.bk * 128) : 16u;
   p.a_sbo = 1024u;
   p.a_kstep = a_mn ? umma_k * 128u : 32u;
+  p.a_cstride = a_mn ? 4u * p.a_kstep : (uint32_t)(TC_BM * 128);
   p.b_lbo = b_mn ? (uint32_t)(p.bk * 128) : 16u;
   p.b_sbo = 1024u;
   p.b_kstep = b_mn ? umma_k * 128u : 32u;
+  p.b_cstride = b_mn ? 4u * p.b_kstep : (uint32_t)(bn * 128);
   const uint32_t fmt = f32in ? 2u : (g->in_type == TB200_BF16 ? 1u : 0u);
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
             ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
 
   if (f32in) {
     switch (bn) {
-      case 32: return launch_bn<1, 32>(ta, tb, p, num_sms, s);
-      case 64: return launch_bn<1, 64>(ta, tb, p, num_sms, s);
-      case 128: return launch_bn<1, 128>(ta, tb, p, num_sms, s);
-      default: return launch_bn<1, 256>(ta, tb, p, num_sms, s);
+      case 32: return launch_bn<1, 32, kc_for(32)>(ta, tb, p, num_sms, s);
+      case 64: return launch_bn<1, 64, kc_for(64)>(ta, tb, p, num_sms, s);
+      case 128: return launch_bn<1, 128, kc_for(128)>(ta, tb, p, num_sms, s);
+      default: return launch_bn<1, 256, kc_for(256)>(ta, tb, p, num_sms, s);
     }
   }
   switch (bn) {
-    case 32: return launch_bn<0, 32>(ta, tb, p, num_sms, s);
-    case 64: return launch_bn<0, 64>(ta, tb, p, num_sms, s);
-    case 128: return launch_bn<0, 128>(ta, tb, p, num_sms, s);
-    default: return launch_bn<0, 256>(ta, tb, p, num_sms, s);
+    case 32: return launch_bn<0, 32, kc_for(32)>(ta, tb, p, num_sms, s);
+    case 64: return launch_bn<0, 64, kc_for(64)>(ta, tb, p, num_sms, s);
+    case 128: return launch_bn<0, 128, kc_for(128)>(ta, tb, p, num_sms, s);
+    default: return launch_bn<0, 256, kc_for(256)>(ta, tb, p, num_sms, s);
   }
 }
 

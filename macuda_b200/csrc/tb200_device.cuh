@@ -27,13 +27,6 @@ __device__ __forceinline__ void store_out(void *C, long long i, float v, int out
   else ((__nv_bfloat16 *)C)[i] = __float2bfloat16_rn(v);
 }
 
-// ---- timing and errors ---------------------------------------------------------------------------
-__device__ __forceinline__ uint64_t globaltimer_ns() {
-  uint64_t t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 // ---- mbarrier ------------------------------------------------------------------------------------
@@ -47,27 +40,34 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps (up to the hint, in ns)
+// until the phase completes instead of spinning. Spinning waiters share their SM sub-partition's issue
+// slots with the producer and MMA threads, whose single-thread issue rate bounds the main loop.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
-// Wait for the phase with the given parity to complete. Gives up after `budget_ns` or as soon as
-// *abort is set by another role of the CTA; on giving up by time it sets *abort itself.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort, uint64_t budget_ns) {
+// Wait for the phase with the given parity to complete. Gives up after `budget_cycles` SM clock cycles
+// or as soon as *abort is set by another role of the CTA; on giving up by time it sets *abort itself.
+// The budget is kept on clock64 (the SM's own cycle counter) and looked at every 16 polls (each poll
+// may sleep up to 1 ms), so the check stays off the critical path of a k-block.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort, uint64_t budget_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  long long t0 = -1;
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 31) == 0) {
+    if ((it & 15) == 0) {
       if (*abort) return false;
-      if (globaltimer_ns() - t0 > budget_ns) {
+      const long long now = clock64();
+      if (t0 < 0) t0 = now;
+      else if ((uint64_t)(now - t0) > budget_cycles) {
         *abort = 1;
         return false;
       }

@@ -22,7 +22,7 @@
 #include <cuda_runtime_api.h>
 #include <cublas_v2.h>
 #include "tb200_internal.h"
-#include "../../include/tinycublas_b200.h"
+#include "tinycublas_b200.h"
 
 #ifndef TB200_GIT_DESCRIBE
 #define TB200_GIT_DESCRIBE "unknown"
@@ -153,7 +153,10 @@ int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_ty
   int sixteen = in_type == TB200_F16 || in_type == TB200_BF16;
   if (sixteen && n <= 8 && transa == 1 && transb == 0 && k % 8 == 0 && aligned && skinny_enabled())
     return TB200_KERNEL_SKINNY;
-  if ((sixteen || (in_type == TB200_F32 && tf32)) && aligned && !ptr_array) {
+  /* TF32 only with both operands K-major: an MN-major 32-bit operand needs the 128B swizzle with 32-byte
+   * atoms (a layout this kernel does not stage); those GEMMs stay exact fp32 on the SIMT kernel */
+  int tf32_ok = in_type == TB200_F32 && tf32 && transa == 1 && transb == 0;
+  if ((sixteen || tf32_ok) && aligned && !ptr_array) {
     int bn = tb200_tc_tile_n(m, n, batch, num_sms);
     if (tile_n) *tile_n = bn;
     return TB200_KERNEL_TC;

@@ -78,7 +78,7 @@ EXTENSIONS = [
     ("tb200_plan", _i, [_i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_i)]),
     ("tb200_tc_tile_n", _i, [_i, _i, _i, _i]),
     ("tb200_device_error", _i, []),
-    ("tb200_gather_row_blocks", _i, [_vp, _i, _i, _i, _i, _vp, _i, _vp]),
+    ("tb200_gather_row_blocks", _i, [_vp, _i, _i, _i, _i, _vp, _i, _i, _vp]),
     ("tb200_bw_write", _i, [_vp, _ll, _f, _vp]),
     ("tb200_bw_read", _i, [_vp, _ll, _vp, _vp]),
     ("tb200_version", ctypes.c_char_p, []),

@@ -85,7 +85,7 @@ def test_tensor_core_shapes(lib, h, monkeypatch, bn, opA, opB, m, n, k):
 def test_tensor_core_bf16_tf32_by_width(lib, h, monkeypatch, bn):
     monkeypatch.setenv("TB200_TC_BN", str(bn))
     assert_ok(run_and_check(lib, h, opA=1, opB=0, m=600, n=400, k=300, in_t=O.BF16, seed=5 + bn), "bf16")
-    assert_ok(run_and_check(lib, h, opA=0, opB=1, m=600, n=400, k=300, in_t=O.F32, out_t=O.F32, a_sigma=1.0,
+    assert_ok(run_and_check(lib, h, opA=1, opB=0, m=600, n=400, k=300, in_t=O.F32, out_t=O.F32, a_sigma=1.0,
                             compute=cb.CUBLAS_COMPUTE_32F_FAST_TF32, seed=6 + bn), "tf32")
 
 
@@ -156,21 +156,25 @@ def test_known_answer_f16_4x4_compute16f(lib, h):
     assert np.array_equal(O.from_bits(host(dC, C), O.F16), np.array(ka["C"], np.float32))
 
 
-def test_known_answer_sgemm48_exact_fp32_and_tf32(lib, h):
-    """link_smoke.c:41-52: small integers, exact in fp32 and in TF32, across a multi-block grid."""
+def test_known_answer_sgemm48_exact_fp32_and_tf32(lib):
+    """link_smoke.c:41-52: small integers, exact in fp32 and in TF32, across a multi-block grid; as NN (the
+    reference's call, fp32 kernel under either math mode) and as TN (the TF32 tensor-core path)."""
     import torch
     ka = json.load(open(os.path.join(GOLD, "known_answers.json")))["sgemm48"]
     A = np.array(ka["A"], np.float32)
     B = np.array(ka["B"], np.float32)
     want = np.array(ka["C"], np.float32)
+    At = np.ascontiguousarray(A.reshape(48, 48).T)  # stored A^T (column-major), so op T gives A back
     for mode in (cb.CUBLAS_DEFAULT_MATH, cb.CUBLAS_TF32_TENSOR_OP_MATH):
-        C = np.full(48 * 48, np.nan, np.float32)
-        dA, dB, dC = dev(A), dev(B), dev(C)
-        assert h.set_math_mode(mode) == 0
-        assert h.sgemm(0, 0, 48, 48, 48, 1.0, dA.data_ptr(), 48, dB.data_ptr(), 48, 0.0, dC.data_ptr(), 48) == 0
-        torch.cuda.synchronize()
-        assert np.array_equal(host(dC, C), want), mode
-    h.set_math_mode(cb.CUBLAS_DEFAULT_MATH)
+        for ta, a in ((0, A), (1, At.reshape(-1))):
+            with lib.handle() as hh:
+                assert hh.set_math_mode(mode) == 0
+                C = np.full(48 * 48, np.nan, np.float32)
+                dA, dB, dC = dev(a), dev(B), dev(C)
+                assert hh.sgemm(ta, 0, 48, 48, 48, 1.0, dA.data_ptr(), 48, dB.data_ptr(), 48, 0.0, dC.data_ptr(),
+                                48) == 0
+                torch.cuda.synchronize()
+                assert np.array_equal(host(dC, C), want), (mode, ta)
 
 
 def test_sgemm_fp32_and_tf32(lib, h):
@@ -180,6 +184,9 @@ def test_sgemm_fp32_and_tf32(lib, h):
                         compute=cb.CUBLAS_COMPUTE_32F_FAST_TF32, seed=91)
     assert_ok(res, "TF32 tensor cores")
     assert res["norm_err"] > 1e-7, "TF32 rounding should be visible: was the fp32 path taken?"
+    res = run_and_check(lib, h, opA=0, opB=1, m=300, n=200, k=250, in_t=O.F32, out_t=O.F32, a_sigma=1.0,
+                        compute=cb.CUBLAS_COMPUTE_32F_FAST_TF32, seed=92)
+    assert_ok(res, "TF32 requested with MN-major operands: exact fp32 kernel")
 
 
 def test_k_zero_scales_c(lib, h):
