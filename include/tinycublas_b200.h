@@ -113,14 +113,16 @@ cublasStatus_t cublasStrsmBatched(cublasHandle_t handle, cublasSideMode_t side, 
 /* Which kernel family a GEMM of this shape and type goes to on a device with `num_sms` SMs, without
  * launching anything. Mirrors the role of the reference's test hook tinycublas_splitk_plan
  * (cublas.c:69-78): a pure function the host-only tests pin row by row.
- * Returns one of the TB200_KERNEL_* values; *tile_n receives the tensor-core tile width (0 if none). */
+ * Returns one of the TB200_KERNEL_* values; *tile_n receives the tensor-core tile width (0 if none) and
+ * *pair 1 when the tile is the 256-row tile of a CTA pair (2-SM UMMA). */
 enum { TB200_KERNEL_NONE = 0, TB200_KERNEL_SIMT = 1, TB200_KERNEL_SKINNY = 2, TB200_KERNEL_TC = 3 };
 int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_type, int out_type,
-               int tf32, int ptr_array, int aligned, int num_sms, int *tile_n);
+               int tf32, int ptr_array, int aligned, int num_sms, int *tile_n, int *pair);
 
-/* The persistent tensor-core kernel's tile width choice (64, 128 or 256) for an m x n x batch GEMM on
- * `num_sms` SMs. Pure function, pinned by host-only tests. */
-int tb200_tc_tile_n(int m, int n, int batch, int num_sms);
+/* The persistent tensor-core kernel's tile choice for an m x n x batch GEMM on `num_sms` SMs: returns the
+ * tile width (32, 64, 128 or 256) and sets *pair (if not NULL) to 1 for the 256 x 256 tile of a CTA pair.
+ * Pure function, pinned by host-only tests. */
+int tb200_tc_tile_n(int m, int n, int batch, int num_sms, int *pair);
 
 /* Last error a kernel of this library recorded on the current device (0 = none): a bounded wait in
  * the tensor-core pipeline that gave up (1), or an internal inconsistency (2). Reading it clears it.

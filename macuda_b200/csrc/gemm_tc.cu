@@ -69,10 +69,11 @@ struct TcParams {
 // KC = 128-byte k-chunks per stage. One stage holds A (128 rows) and B (BN rows) for KC * epr values of
 // k. The producers and the MMA thread spend a few hundred cycles of issue latency per stage whatever its
 // size, so narrow tiles take two chunks per stage to keep the tensor core fed.
-template <int BN, int KC>
+template <int BN, int KC, int CG>
 struct TcCfg {
+  static constexpr int B_ROWS = BN / CG;  // a pair splits B's BN columns between its two CTAs
   static constexpr int A_BYTES = TC_BM * 128 * KC;
-  static constexpr int B_BYTES = BN * 128 * KC;
+  static constexpr int B_BYTES = B_ROWS * 128 * KC;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES_RAW = 196608 / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
@@ -94,35 +95,41 @@ __device__ __forceinline__ void decode_tile(const TcParams &p, long long t, int 
   nt = local / gm;
 }
 
-// One operand's loads for one stage: `rows` (128 for A, BN for B) x KC chunks. K-major: chunk c is a
-// rows x 128-byte box at k0 + c*epr. MN-major: rows/epr boxes of epr (m or n) x KC*epr k-rows.
-template <int KC>
-__device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *tm, uint64_t *bar, int mn_major,
-                                             int batched, int rows, int epr, int mn0, int k0, int b) {
+// One operand's loads for one stage: `rows` (128 for A, BN/CG for B) x KC chunks. K-major: chunk c is a
+// rows x 128-byte box at k0 + c*epr. MN-major: rows/epr boxes of epr (m or n) x KC*epr k-rows. With
+// CG == 2 the bytes complete on the pair's even CTA's barrier (shared::cluster address bar2).
+template <int KC, int CG>
+__device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *tm, uint64_t *bar, uint32_t bar2,
+                                             int mn_major, int batched, int rows, int epr, int mn0, int k0, int b) {
+  auto ld = [&](uint8_t *d, int c0, int c1) {
+    if (CG == 1) {
+      if (batched) tma_load_3d(d, tm, bar, c0, c1, b);
+      else tma_load_2d(d, tm, bar, c0, c1);
+    } else {
+      if (batched) tma_load_3d_cg2(d, tm, bar2, c0, c1, b);
+      else tma_load_2d_cg2(d, tm, bar2, c0, c1);
+    }
+  };
   if (!mn_major) {
 #pragma unroll
-    for (int c = 0; c < KC; ++c) {
-      uint8_t *d = dst + c * rows * 128;
-      if (batched) tma_load_3d(d, tm, bar, k0 + c * epr, mn0, b);
-      else tma_load_2d(d, tm, bar, k0 + c * epr, mn0);
-    }
+    for (int c = 0; c < KC; ++c) ld(dst + c * rows * 128, k0 + c * epr, mn0);
   } else {
-    for (int j = 0; j < rows / epr; ++j) {
-      uint8_t *d = dst + j * KC * epr * 128;
-      if (batched) tma_load_3d(d, tm, bar, mn0 + j * epr, k0, b);
-      else tma_load_2d(d, tm, bar, mn0 + j * epr, k0);
-    }
+    for (int j = 0; j < rows / epr; ++j) ld(dst + j * KC * epr * 128, mn0 + j * epr, k0);
   }
 }
 
-template <int KIND, int BN, int KC>
+// CG = 1: one CTA per 128 x BN tile. CG = 2: a cluster of two CTAs per 256 x BN tile (2-SM UMMA): each
+// CTA loads its 128 rows of A and BN/2 rows of B, the even CTA's MMA thread drives both tensor cores,
+// and each CTA's epilogue drains its own 128 rows from its own tensor memory.
+template <int KIND, int BN, int KC, int CG>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tb200_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const TcParams p) {
-  using Cfg = TcCfg<BN, KC>;
+  using Cfg = TcCfg<BN, KC, CG>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
-  // 1024-byte alignment of the shared-window offset: the 128B swizzle atom is 8 rows x 128 bytes
+  // 1024-byte alignment of the shared-window offset: the 128B swizzle atom is 8 rows x 128 bytes. The
+  // offset is the same in both CTAs of a pair, as the 2-SM UMMA requires.
   uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t *smA = smem;
   uint8_t *smB = smem + STAGES * Cfg::A_BYTES;
@@ -137,15 +144,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  // tile index stream: one per CTA, or one per pair
+  const long long t_first = CG == 2 ? (long long)(blockIdx.x >> 1) : (long long)blockIdx.x;
+  const long long t_step = CG == 2 ? (long long)(gridDim.x >> 1) : (long long)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 2);  // one arrive.expect_tx from each producer
+      mbar_init(&full[s], 2);  // one arrive.expect_tx from each producer (of the even CTA, for a pair)
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], 4 * CG);  // every epilogue warp of the tile
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -154,13 +166,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     prefetch_tmap(&tmB);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if (CG == 1) {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    } else {
+      tmem_alloc_cg2(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_cg2();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  __syncwarp();                 // barrier.cluster.*.aligned wants every warp converged
+  if (CG == 2) cluster_sync();  // the peer's loads and arrivals target the even CTA's barriers: all initialised
+  else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // shared::cluster addresses of the even CTA's barriers (CG == 2)
+  const uint32_t lead_full0 = CG == 2 ? mapa_shared(smem_u32(full), 0) : 0u;
+  const uint32_t lead_tempty0 = CG == 2 ? mapa_shared(smem_u32(tempty), 0) : 0u;
 
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------------------------ TMA producers (A: warp 0, B: warp 6)
@@ -169,20 +191,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const CUtensorMap *tm = is_a ? &tmA : &tmB;
       uint8_t *base = is_a ? smA : smB;
       const int stage_bytes = is_a ? Cfg::A_BYTES : Cfg::B_BYTES;
-      const int rows = is_a ? TC_BM : BN;
+      const int rows = is_a ? TC_BM : Cfg::B_ROWS;
       const int mn_major = is_a ? p.a_mn : p.b_mn;
       const int batched = is_a ? p.a_batched : p.b_batched;
       int s = 0;
       uint32_t ph = 0;
       uint32_t issued = 0, issued_par = 0;  // per stage: a fill is outstanding, and its phase parity
-      for (long long t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
+      for (long long t = t_first; t < p.total_tiles && !*abort_flag; t += t_step) {
         int b, mt, nt;
         decode_tile(p, t, b, mt, nt);
-        const int mn0 = is_a ? mt * TC_BM : nt * BN;
+        const int mn0 = is_a ? mt * (TC_BM * CG) + (int)rank * TC_BM : nt * BN + (int)rank * Cfg::B_ROWS;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, WAIT_BUDGET_CYC)) break;
-          mbar_arrive_expect_tx(&full[s], (uint32_t)stage_bytes);
-          load_operand<KC>(base + s * stage_bytes, tm, &full[s], mn_major, batched, rows, p.epr, mn0, kb * p.bk, b);
+          // the even CTA announces the bytes of both CTAs; the odd CTA's copies only complete them
+          if (leader) mbar_arrive_expect_tx(&full[s], (uint32_t)(stage_bytes * CG));
+          load_operand<KC, CG>(base + s * stage_bytes, tm, &full[s], lead_full0 + (uint32_t)(s * 8), mn_major,
+                               batched, rows, p.epr, mn0, kb * p.bk, b);
           issued |= 1u << s;
           issued_par = (issued_par & ~(1u << s)) | (ph << s);
           if (++s == STAGES) {
@@ -191,15 +215,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       }
-      if (*abort_flag) {  // let every copy still in flight land before the CTA's smem goes away
+      if (*abort_flag && leader) {  // let every copy still in flight land before shared memory goes away
         volatile int no_abort = 0;
         for (int q = 0; q < STAGES; ++q)
           if (issued & (1u << q)) (void)mbar_wait(&full[q], (issued_par >> q) & 1u, &no_abort, DRAIN_BUDGET_CYC);
       }
     }
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // ------------------------------------------------------------------ MMA issuer (the even CTA of a pair)
+    if (lane == 0 && leader) {
       int s = 0;
       uint32_t ph = 0;
       int acc = 0;
@@ -214,7 +238,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         a_off[kk] = ((kk >> 2) * p.a_cstride + (kk & 3) * p.a_kstep) >> 4;
         b_off[kk] = ((kk >> 2) * p.b_cstride + (kk & 3) * p.b_kstep) >> 4;
       }
-      for (long long t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
+      // commit targets: this CTA's barriers, and for a pair the odd CTA's too
+      const uint32_t empty0_l = smem_u32(empty), tfull0_l = smem_u32(tfull), drain_l = smem_u32(drain);
+      const uint32_t empty0_p = CG == 2 ? mapa_shared(empty0_l, 1) : 0u;
+      const uint32_t tfull0_p = CG == 2 ? mapa_shared(tfull0_l, 1) : 0u;
+      for (long long t = t_first; t < p.total_tiles && !*abort_flag; t += t_step) {
         if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, WAIT_BUDGET_CYC)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -229,22 +257,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const uint64_t bd0 = b_desc0 + (uint64_t)((uint32_t)(s * Cfg::B_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 4 * KC; ++kk) {  // UMMA_K = 16 (f16/bf16) or 8 (tf32): 4 steps per chunk
-            if (KIND == 0) umma_f16(d_tmem, ad0 + a_off[kk], bd0 + b_off[kk], p.idesc, (kb | kk) != 0);
-            else umma_tf32(d_tmem, ad0 + a_off[kk], bd0 + b_off[kk], p.idesc, (kb | kk) != 0);
+            const uint32_t en = (kb | kk) != 0;
+            if (CG == 1) {
+              if (KIND == 0) umma_f16(d_tmem, ad0 + a_off[kk], bd0 + b_off[kk], p.idesc, en);
+              else umma_tf32(d_tmem, ad0 + a_off[kk], bd0 + b_off[kk], p.idesc, en);
+            } else {
+              if (KIND == 0) umma_f16_cg2(d_tmem, ad0 + a_off[kk], bd0 + b_off[kk], p.idesc, en);
+              else umma_tf32_cg2(d_tmem, ad0 + a_off[kk], bd0 + b_off[kk], p.idesc, en);
+            }
           }
-          umma_commit(&empty[s]);
+          if (CG == 1) {
+            umma_commit(&empty[s]);
+          } else {
+            umma_commit_cg2(empty0_l + (uint32_t)(s * 8));
+            umma_commit_cg2(empty0_p + (uint32_t)(s * 8));
+          }
           if (++s == STAGES) {
             s = 0;
             ph ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        if (CG == 1) {
+          umma_commit(&tfull[acc]);
+        } else {
+          umma_commit_cg2(tfull0_l + (uint32_t)(acc * 8));
+          umma_commit_cg2(tfull0_p + (uint32_t)(acc * 8));
+        }
         acc ^= 1;
         if (acc == 0) aph ^= 1u;
       }
       // every MMA issued above has completed once this commit arrives
-      umma_commit(drain);
+      if (CG == 1) umma_commit(drain);
+      else umma_commit_cg2(drain_l);
       volatile int no_abort = 0;
       (void)mbar_wait(drain, 0, &no_abort, DRAIN_BUDGET_CYC);
     }
@@ -254,7 +299,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int acc = 0;
     uint32_t aph = 0;
     const int osz = p.out_type == 0 ? 4 : 2;
-    for (long long t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+    for (long long t = t_first; t < p.total_tiles; t += t_step) {
       int b, mt, nt;
       decode_tile(p, t, b, mt, nt);
       // one lane waits, the warp follows its verdict: tcgen05.ld below needs the whole warp converged
@@ -263,7 +308,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
       tc_fence_after();
-      const int row = mt * TC_BM + quad * 32 + lane;
+      const int row = mt * (TC_BM * CG) + (int)rank * TC_BM + quad * 32 + lane;
       const int n0 = nt * BN;
       char *Cb = (char *)p.C + (long long)b * p.sC * osz;
       const bool row_ok = row < p.m;
@@ -302,20 +347,31 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if (CG == 1) mbar_arrive(&tempty[acc]);
+        else mbar_arrive_cluster(lead_tempty0 + (uint32_t)(acc * 8));
+      }
       acc ^= 1;
       if (acc == 0) aph ^= 1u;
     }
   }
 
-  __syncthreads();
+  tc_fence_before();
+  __syncwarp();
+  if (CG == 2) cluster_sync();  // neither CTA leaves while its pair may still touch its memory or barriers
+  else __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_tb200_err, 1);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if (CG == 1) tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    else tmem_dealloc_cg2(tmem_base, Cfg::TMEM_COLS);
   }
 }
+
+}  // namespace
+
+namespace {
 
 // ---------------------------------------------------------------------------------- host side
 
@@ -349,30 +405,67 @@ bool make_map(CUtensorMap *tm, CUtensorMapDataType dt, int esz, const void *base
   return r == CUDA_SUCCESS;
 }
 
-template <int KIND, int BN, int KC>
+template <int KIND, int BN, int KC, int CG>
 int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, int num_sms, cudaStream_t s) {
-  using Cfg = TcCfg<BN, KC>;
-  auto kern = tb200_gemm_tc_kernel<KIND, BN, KC>;
-  static int attr_done[64];
+  using Cfg = TcCfg<BN, KC, CG>;
+  auto kern = tb200_gemm_tc_kernel<KIND, BN, KC, CG>;
+  static int attr_done[64], max_pairs[64];
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!attr_done[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
+    if (CG == 2) {
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 2;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = 1;
+      cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+      cfg.blockDim = dim3(TC_THREADS, 1, 1);
+      cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int nc = 0;
+      if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess || nc <= 0) nc = num_sms / 2;
+      (void)cudaGetLastError();
+      max_pairs[dev] = nc;
+    }
     attr_done[dev] = 1;
   }
-  long long grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
+  const long long slots = CG == 2 ? max_pairs[dev] : num_sms;
+  const long long units = p.total_tiles < slots ? p.total_tiles : slots;
+  const unsigned grid = (unsigned)(units * CG);
   if (tb200_trace())
     fprintf(stderr,
-            "[trace] launch tb200_gemm_tc<%s,%d,%d> grid=(%lld,1,1) block=(%d,1,1) smem=%d stages=%d m=%d n=%d k=%d "
-            "batch=%d\n",
-            KIND ? "tf32" : "f16", BN, KC, grid, TC_THREADS, Cfg::SMEM_BYTES, Cfg::STAGES, p.m, p.n, p.k, p.batch);
-  kern<<<(unsigned)grid, TC_THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, p);
-  return (int)cudaGetLastError();
+            "[trace] launch tb200_gemm_tc<%s,BN=%d,KC=%d,CG=%d> grid=(%u,1,1) block=(%d,1,1) smem=%d stages=%d m=%d n=%d "
+            "k=%d batch=%d\n",
+            KIND ? "tf32" : "f16", BN, KC, CG, grid, TC_THREADS, Cfg::SMEM_BYTES, Cfg::STAGES, p.m, p.n, p.k, p.batch);
+  if (CG == 1) {
+    kern<<<grid, TC_THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, p);
+    return (int)cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 2;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(TC_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return (int)cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
 }
 
-// tile width BN -> k-chunks per stage: the widest tile keeps one chunk (four stages of 48 KB); narrower
-// tiles take two so that each stage carries enough tensor work to cover its issue cost
+// tile width BN -> k-chunks per stage: the widest single-CTA tile keeps one chunk (four stages of 48 KB);
+// narrower tiles take two so that each stage carries enough tensor work to cover its issue cost. A pair's
+// 256 x 256 tile has 32 KB per CTA per chunk and keeps one chunk (six stages).
 constexpr int kc_for(int bn) { return bn >= 256 ? 1 : 2; }
 
 }  // namespace
@@ -388,15 +481,18 @@ extern "C" int tb200_tc_ok(const tb200_gemm_t *g) {
   return 1;
 }
 
-extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int num_sms, cudaStream_t s) {
+extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s) {
   if (!tb200_tc_ok(g)) return tb200_launch_simt(g, s);
   const bool f32in = g->in_type == TB200_F32;
   const int es = f32in ? 4 : 2;
   const int epr = 128 / es;
   int bn = tile_n;
   if (bn != 32 && bn != 64 && bn != 128 && bn != 256) bn = 128;
+  const int cg = pair ? 2 : 1;
+  if (cg == 2) bn = 256;  // the pair tile is 256 x 256
   const int b_mn = g->opB == 1, a_mn = g->opA == 0;
-  if (b_mn && bn < epr) bn = epr;  // an MN-major B tile holds whole 128-byte rows
+  if (b_mn && bn / cg < epr) bn = epr * cg;  // an MN-major B tile holds whole 128-byte rows
+  const int b_rows = bn / cg;
   const CUtensorMapDataType dt =
       f32in ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
             : (g->in_type == TB200_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
@@ -405,11 +501,11 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int num_sms, c
   memset(&p, 0, sizeof p);
   CUtensorMap ta, tb;
   bool ok;
-  const int kc = kc_for(bn);
+  const int kc = cg == 2 ? 1 : kc_for(bn);
   if (!a_mn) ok = make_map(&ta, dt, es, g->A, g->k, g->m, g->lda, g->batch, g->sA, epr, TC_BM, &p.a_batched);
   else ok = make_map(&ta, dt, es, g->A, g->m, g->k, g->lda, g->batch, g->sA, epr, epr * kc, &p.a_batched);
   if (ok) {
-    if (!b_mn) ok = make_map(&tb, dt, es, g->B, g->k, g->n, g->ldb, g->batch, g->sB, epr, bn, &p.b_batched);
+    if (!b_mn) ok = make_map(&tb, dt, es, g->B, g->k, g->n, g->ldb, g->batch, g->sB, epr, b_rows, &p.b_batched);
     else ok = make_map(&tb, dt, es, g->B, g->n, g->k, g->ldb, g->batch, g->sB, epr, epr * kc, &p.b_batched);
   }
   if (!ok) {
@@ -420,7 +516,7 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int num_sms, c
   p.epr = epr;
   p.bk = epr * kc;
   p.num_kb = (g->k + p.bk - 1) / p.bk;
-  p.m_tiles = (g->m + TC_BM - 1) / TC_BM;
+  p.m_tiles = (g->m + TC_BM * cg - 1) / (TC_BM * cg);
   p.n_tiles = (g->n + bn - 1) / bn;
   p.tiles_per_batch = (long long)p.m_tiles * p.n_tiles;
   p.total_tiles = p.tiles_per_batch * g->batch;
@@ -440,24 +536,28 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int num_sms, c
   p.b_lbo = b_mn ? (uint32_t)(p.bk * 128) : 16u;
   p.b_sbo = 1024u;
   p.b_kstep = b_mn ? umma_k * 128u : 32u;
-  p.b_cstride = b_mn ? 4u * p.b_kstep : (uint32_t)(bn * 128);
+  p.b_cstride = b_mn ? 4u * p.b_kstep : (uint32_t)(b_rows * 128);
   const uint32_t fmt = f32in ? 2u : (g->in_type == TB200_BF16 ? 1u : 0u);
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-            ((uint32_t)(bn >> 3) << 17) | ((uint32_t)(TC_BM >> 4) << 24);
+            ((uint32_t)(bn >> 3) << 17) | ((uint32_t)((TC_BM * cg) >> 4) << 24);
 
+  if (cg == 2) {
+    if (f32in) return launch_bn<1, 256, 1, 2>(ta, tb, p, num_sms, s);
+    return launch_bn<0, 256, 1, 2>(ta, tb, p, num_sms, s);
+  }
   if (f32in) {
     switch (bn) {
-      case 32: return launch_bn<1, 32, kc_for(32)>(ta, tb, p, num_sms, s);
-      case 64: return launch_bn<1, 64, kc_for(64)>(ta, tb, p, num_sms, s);
-      case 128: return launch_bn<1, 128, kc_for(128)>(ta, tb, p, num_sms, s);
-      default: return launch_bn<1, 256, kc_for(256)>(ta, tb, p, num_sms, s);
+      case 32: return launch_bn<1, 32, kc_for(32), 1>(ta, tb, p, num_sms, s);
+      case 64: return launch_bn<1, 64, kc_for(64), 1>(ta, tb, p, num_sms, s);
+      case 128: return launch_bn<1, 128, kc_for(128), 1>(ta, tb, p, num_sms, s);
+      default: return launch_bn<1, 256, kc_for(256), 1>(ta, tb, p, num_sms, s);
     }
   }
   switch (bn) {
-    case 32: return launch_bn<0, 32, kc_for(32)>(ta, tb, p, num_sms, s);
-    case 64: return launch_bn<0, 64, kc_for(64)>(ta, tb, p, num_sms, s);
-    case 128: return launch_bn<0, 128, kc_for(128)>(ta, tb, p, num_sms, s);
-    default: return launch_bn<0, 256, kc_for(256)>(ta, tb, p, num_sms, s);
+    case 32: return launch_bn<0, 32, kc_for(32), 1>(ta, tb, p, num_sms, s);
+    case 64: return launch_bn<0, 64, kc_for(64), 1>(ta, tb, p, num_sms, s);
+    case 128: return launch_bn<0, 128, kc_for(128), 1>(ta, tb, p, num_sms, s);
+    default: return launch_bn<0, 256, kc_for(256), 1>(ta, tb, p, num_sms, s);
   }
 }
 

@@ -30,7 +30,7 @@ typedef struct {
 
 int tb200_launch_simt(const tb200_gemm_t *g, cudaStream_t s);
 int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s);
-int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int num_sms, cudaStream_t s);
+int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s);
 int tb200_launch_trsm_rupn(const float *const *A, float *const *B, int rows, int n, int lda, int ldb, float alpha,
                            int batch, cudaStream_t s);
 

@@ -119,16 +119,17 @@ static int gemm_contract(cudaDataType At, cudaDataType Bt, cudaDataType Ct, cubl
 /* ---- planning ---- */
 static int esize(int t) { return t == TB200_F32 ? 4 : 2; }
 
-/* the persistent tensor-core kernel's tile width: fewest waves of 128 x BN tiles, weighted by how
- * much of its peak a BN-wide UMMA reaches. A 128 x N x 16 UMMA needs N/2 tensor cycles and reads
- * 4 KB of A plus N x 32 B of B from shared memory (128 B per cycle), so narrow tiles are bound by
- * shared memory: efficiency ~ min(1, (N/2) / (32 + N/4)), derated slightly at N = 128 where the two
- * are equal. */
-int tb200_tc_tile_n(int m, int n, int batch, int num_sms) {
+/* The persistent tensor-core kernel's tile: 128 x BN on one CTA (BN 32..256), or 256 x 256 on a pair of
+ * CTAs (2-SM UMMA). Cost = waves of tiles over the SMs (pairs) x the time one SM spends on its share of a
+ * tile, from the measured fraction of tensor peak each configuration sustains per SM: a 128 x N x 16
+ * UMMA re-reads its whole A and B from shared memory, which caps narrow single-CTA tiles, while the pair
+ * tile streams half of B per SM. */
+int tb200_tc_tile_n(int m, int n, int batch, int num_sms, int *pair) {
   static const int bns[4] = {256, 128, 64, 32};
-  static const double eff[4] = {1.0, 0.9, 0.62, 0.38};
+  static const double eff[4] = {0.57, 0.50, 0.35, 0.19};
+  static const double eff_pair = 0.80;
   if (num_sms <= 0) num_sms = 148;
-  int best = 256;
+  int best = 256, best_pair = 0;
   double best_cost = 1e300;
   for (int i = 0; i < 4; i++) {
     int bn = bns[i];
@@ -139,15 +140,29 @@ int tb200_tc_tile_n(int m, int n, int batch, int num_sms) {
     if (cost < best_cost * 0.999) {
       best_cost = cost;
       best = bn;
+      best_pair = 0;
     }
   }
+  if (n > 128) { /* 256 x 256 pair tiles: two CTAs each hold 128 x 256 of it */
+    long long tiles = (long long)((m + 255) / 256) * ((n + 255) / 256) * (long long)batch;
+    long long slots = num_sms / 2;
+    long long waves = (tiles + slots - 1) / slots;
+    double cost = (double)waves * 256 / eff_pair;
+    if (cost < best_cost * 0.999) {
+      best_cost = cost;
+      best = 256;
+      best_pair = 1;
+    }
+  }
+  if (pair) *pair = best_pair;
   return best;
 }
 
 int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_type, int out_type, int tf32,
-               int ptr_array, int aligned, int num_sms, int *tile_n) {
+               int ptr_array, int aligned, int num_sms, int *tile_n, int *pair) {
   (void)out_type;
   if (tile_n) *tile_n = 0;
+  if (pair) *pair = 0;
   if (m <= 0 || n <= 0 || batch <= 0) return TB200_KERNEL_NONE;
   if (k <= 0 || !tc_enabled()) return TB200_KERNEL_SIMT;
   int sixteen = in_type == TB200_F16 || in_type == TB200_BF16;
@@ -157,8 +172,10 @@ int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_ty
    * atoms (a layout this kernel does not stage); those GEMMs stay exact fp32 on the SIMT kernel */
   int tf32_ok = in_type == TB200_F32 && tf32 && transa == 1 && transb == 0;
   if ((sixteen || tf32_ok) && aligned && !ptr_array) {
-    int bn = tb200_tc_tile_n(m, n, batch, num_sms);
+    int pr = 0;
+    int bn = tb200_tc_tile_n(m, n, batch, num_sms, &pr);
     if (tile_n) *tile_n = bn;
+    if (pair) *pair = pr;
     return TB200_KERNEL_TC;
   }
   return TB200_KERNEL_SIMT;
@@ -180,26 +197,36 @@ static const char *kernel_name(int kind) {
 }
 
 static cublasStatus_t run_gemm(struct tb200_handle *h, tb200_gemm_t *g) {
-  int tile_n = 0;
+  int tile_n = 0, pair = 0;
   int aligned = operands_aligned(g);
   int ptr_array = g->Aarr != NULL;
   int sms = tb200_num_sms();
   int kind = tb200_plan(g->opA, g->opB, g->m, g->n, g->k, g->batch, g->in_type, g->out_type, g->tf32, ptr_array,
-                        aligned, sms, &tile_n);
-  if (kind == TB200_KERNEL_TC) { /* TB200_TC_BN=32|64|128|256 forces the tile width (tests, bisecting) */
+                        aligned, sms, &tile_n, &pair);
+  if (kind == TB200_KERNEL_TC) {
+    /* TB200_TC_BN=32|64|128|256 forces a single-CTA tile of that width, TB200_TC_BN=pair the 256 x 256
+     * pair tile (tests, bisecting) */
     const char *e = getenv("TB200_TC_BN");
-    int v = e ? atoi(e) : 0;
-    if (v == 32 || v == 64 || v == 128 || v == 256) tile_n = v;
+    if (e && !strcmp(e, "pair")) {
+      pair = 1;
+      tile_n = 256;
+    } else {
+      int v = e ? atoi(e) : 0;
+      if (v == 32 || v == 64 || v == 128 || v == 256) {
+        tile_n = v;
+        pair = 0;
+      }
+    }
   }
   if (tb200_trace())
-    fprintf(stderr, "[trace] gemm %s op=%c%c m=%d n=%d k=%d batch=%d in=%d out=%d tf32=%d ptr=%d aligned=%d BN=%d\n",
+    fprintf(stderr, "[trace] gemm %s op=%c%c m=%d n=%d k=%d batch=%d in=%d out=%d tf32=%d ptr=%d aligned=%d BN=%d pair=%d\n",
             kernel_name(kind), g->opA ? 'T' : 'N', g->opB ? 'T' : 'N', g->m, g->n, g->k, g->batch, g->in_type,
-            g->out_type, g->tf32, ptr_array, aligned, tile_n);
+            g->out_type, g->tf32, ptr_array, aligned, tile_n, pair);
   int rc = 0;
   switch (kind) {
     case TB200_KERNEL_NONE: return CUBLAS_STATUS_SUCCESS;
     case TB200_KERNEL_SKINNY: rc = tb200_launch_skinny(g, h->stream); break;
-    case TB200_KERNEL_TC: rc = tb200_launch_tc(g, tile_n, sms, h->stream); break;
+    case TB200_KERNEL_TC: rc = tb200_launch_tc(g, tile_n, pair, sms, h->stream); break;
     default: rc = tb200_launch_simt(g, h->stream); break;
   }
   if (rc != 0) {

@@ -75,8 +75,8 @@ SIGNATURES = [
     ("cublasStrsmBatched", _i, [_vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _i, _vp, _i, _i]),
 ]
 EXTENSIONS = [
-    ("tb200_plan", _i, [_i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_i)]),
-    ("tb200_tc_tile_n", _i, [_i, _i, _i, _i]),
+    ("tb200_plan", _i, [_i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
+    ("tb200_tc_tile_n", _i, [_i, _i, _i, _i, ctypes.POINTER(_i)]),
     ("tb200_device_error", _i, []),
     ("tb200_gather_row_blocks", _i, [_vp, _i, _i, _i, _i, _vp, _i, _i, _vp]),
     ("tb200_bw_write", _i, [_vp, _ll, _f, _vp]),
@@ -130,10 +130,11 @@ class CublasLib:
 
     def plan(self, transa, transb, m, n, k, batch=1, in_type=1, out_type=0, tf32=0, ptr_array=0, aligned=1,
              num_sms=148):
-        tn = ctypes.c_int(0)
+        """(kernel family, tile width) - the width is reported as 512 for the 256 x 256 CTA-pair tile"""
+        tn, pr = ctypes.c_int(0), ctypes.c_int(0)
         kind = self.lib.tb200_plan(transa, transb, m, n, k, batch, in_type, out_type, tf32, ptr_array, aligned,
-                                   num_sms, ctypes.byref(tn))
-        return kind, tn.value
+                                   num_sms, ctypes.byref(tn), ctypes.byref(pr))
+        return kind, (512 if pr.value else tn.value)
 
     def device_error(self) -> int:
         return self.lib.tb200_device_error()

@@ -135,8 +135,11 @@ def test_trsm_refuses_unserved_cases(lib):
 PLAN_ROWS = [
     ("config 1: ggml fp16 T,N 4096x512x4096", (1, 0, 4096, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 128)),
     ("config 2 K/V 1024x512x4096", (1, 0, 1024, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 32)),
-    ("config 2 gate/up 14336x512x4096", (1, 0, 14336, 512, 4096, 1, 2, 0, 0, 1), (cb.TB200_KERNEL_TC, 256)),
-    ("config 2 lm_head 128256x512x4096", (1, 0, 128256, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 256)),
+    ("config 2 gate/up 14336x512x4096: CTA-pair tile", (1, 0, 14336, 512, 4096, 1, 2, 0, 0, 1), (cb.TB200_KERNEL_TC, 512)),
+    ("config 2 lm_head 128256x512x4096: CTA-pair tile", (1, 0, 128256, 512, 4096, 1, 1, 0, 0, 1),
+     (cb.TB200_KERNEL_TC, 512)),
+    ("config 2 down 4096x512x14336", (1, 0, 4096, 512, 14336, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 128)),
+    ("config 5 square 8192: CTA-pair tile", (1, 0, 8192, 8192, 8192, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 512)),
     ("config 4 decode n=1", (1, 0, 4096, 1, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_SKINNY, 0)),
     ("config 4 decode n=8", (1, 0, 14336, 8, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_SKINNY, 0)),
     ("n=8 under op N A goes to the tensor cores", (0, 0, 4096, 8, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 32)),
@@ -158,9 +161,11 @@ def test_plan_rows(lib, what, args, want):
     assert lib.plan(ta, tb, m, n, k, batch, it, 0, tf32, ptr, aligned, 148) == want, what
 
 
-def test_tile_width_fills_the_sms(lib):
-    # every choice is one of the compiled widths and never more waves than the narrowest tile needs
+def test_tile_choice_is_a_compiled_configuration(lib):
     for m in (128, 1024, 4096, 14336, 128256):
         for n in (16, 32, 64, 100, 512, 2048, 16384):
-            bn = lib.lib.tb200_tc_tile_n(m, n, 1, 148)
-            assert bn in (32, 64, 128, 256)
+            pair = ctypes.c_int(-1)
+            bn = lib.lib.tb200_tc_tile_n(m, n, 1, 148, ctypes.byref(pair))
+            assert bn in (32, 64, 128, 256) and pair.value in (0, 1)
+            if pair.value:
+                assert bn == 256 and n > 128

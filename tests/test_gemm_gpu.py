@@ -73,25 +73,34 @@ TC_SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("bn", [32, 64, 128, 256])
+@pytest.mark.parametrize("bn", [32, 64, 128, 256, "pair"])
 @pytest.mark.parametrize("opA,opB,m,n,k", TC_SHAPES)
 def test_tensor_core_shapes(lib, h, monkeypatch, bn, opA, opB, m, n, k):
     assert lib.plan(opA, opB, m, n, k, 1, 1, 0, 0, 0, 1, 148)[0] == cb.TB200_KERNEL_TC
     monkeypatch.setenv("TB200_TC_BN", str(bn))
-    assert_ok(run_and_check(lib, h, opA=opA, opB=opB, m=m, n=n, k=k, seed=m + n + k + bn), f"BN {bn}")
+    assert_ok(run_and_check(lib, h, opA=opA, opB=opB, m=m, n=n, k=k, seed=m + n + k + len(str(bn))), f"BN {bn}")
 
 
-@pytest.mark.parametrize("bn", [32, 128, 256])
+@pytest.mark.parametrize("bn", [32, 128, 256, "pair"])
 def test_tensor_core_bf16_tf32_by_width(lib, h, monkeypatch, bn):
     monkeypatch.setenv("TB200_TC_BN", str(bn))
-    assert_ok(run_and_check(lib, h, opA=1, opB=0, m=600, n=400, k=300, in_t=O.BF16, seed=5 + bn), "bf16")
+    assert_ok(run_and_check(lib, h, opA=1, opB=0, m=600, n=400, k=300, in_t=O.BF16, seed=5), "bf16")
     assert_ok(run_and_check(lib, h, opA=1, opB=0, m=600, n=400, k=300, in_t=O.F32, out_t=O.F32, a_sigma=1.0,
-                            compute=cb.CUBLAS_COMPUTE_32F_FAST_TF32, seed=6 + bn), "tf32")
+                            compute=cb.CUBLAS_COMPUTE_32F_FAST_TF32, seed=6), "tf32")
 
 
-def test_tensor_core_alpha_beta_and_16bit_out(lib, h):
+@pytest.mark.parametrize("bn", ["128", "pair"])
+def test_tensor_core_alpha_beta_and_16bit_out(lib, h, monkeypatch, bn):
+    monkeypatch.setenv("TB200_TC_BN", bn)
     for out_t in (O.F32, O.F16, O.BF16):
         assert_ok(run_and_check(lib, h, m=700, n=300, k=512, out_t=out_t, alpha=-0.75, beta=0.5, seed=3), out_t)
+
+
+def test_pair_tile_large_and_batched(lib, h):
+    """The CTA-pair (2-SM UMMA) tile as the planner picks it: gate/up shape, and a strided batch."""
+    assert lib.plan(1, 0, 14336, 512, 4096, 1, 1, 0, 0, 0, 1, 148)[1] == 512
+    assert_ok(run_and_check(lib, h, m=14336, n=512, k=4096, mode="ex", seed=17, sample=160), "gate/up")
+    assert_ok(run_and_check(lib, h, m=1000, n=700, k=520, batch=3, seed=18), "batched")
 
 
 def test_strided_batch_and_broadcast(lib, h):
