@@ -131,15 +131,16 @@ def make_inputs(torch, rank, world, dtype, seed=1234):
         "x": (torch.randn(TOKENS, HIDDEN, device="cuda", generator=g)).to(dtype).contiguous(),  # B: k x n, ldb = k
         "h": (torch.randn(TOKENS, FFN, device="cuda", generator=g)).to(dtype).contiguous(),
     }
+    from macuda_b200.dist import shard_rows
     layers = []
     for name, m, k, src in PROJECTIONS:
-        mp = m // world
-        w = torch.empty(mp, k, device="cuda", dtype=dtype)  # row r of w = output feature r: k contiguous
+        first, rows, mp = shard_rows(m, world, rank)
+        w = torch.empty(max(rows, 1), k, device="cuda", dtype=dtype)  # row r = output feature first + r
         gw = torch.Generator(device="cuda")
         gw.manual_seed(seed * 131 + sum(map(ord, name)) * 7 + rank)
-        w.copy_(torch.randn(mp, k, device="cuda", generator=gw) * 0.02)
-        c = torch.empty(mp * TOKENS if world > 1 else m * TOKENS, device="cuda", dtype=torch.float32)
-        layers.append({"name": name, "m": m, "mp": mp, "k": k, "src": src, "w": w, "c_local": c})
+        w.copy_(torch.randn(w.shape[0], k, device="cuda", generator=gw) * 0.02)
+        c = torch.empty(m * TOKENS, device="cuda", dtype=torch.float32) if world == 1 else None
+        layers.append({"name": name, "m": m, "mp": rows, "k": k, "src": src, "w": w, "c_local": c})
     return acts, layers
 
 
@@ -264,6 +265,7 @@ def run(args):
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout: one JSON line only
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     if args.impl == "reference":
         from oracle import oracle as O
@@ -273,6 +275,7 @@ def run(args):
                 print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libtinycublas_ref.so was not built "
                                   "(needs the reference tree at build time)"}))
             return 0
+        launched = world
         if world > 1:  # the reference is single-GPU: rank 0 alone runs it
             dist.barrier()
             if rank != 0:
@@ -288,12 +291,11 @@ def run(args):
     comm = torch.cuda.Stream() if world > 1 else None
     h = lib.handle()
     h.set_stream(stream.cuda_stream)
-    full = {}
+    sharded = []
     if world > 1:
+        from macuda_b200.dist import ShardedGemm
         for L in layers:
-            full[L["name"]] = {"gathered": torch.empty(L["m"] * TOKENS, device="cuda"),
-                               "c": torch.empty(L["m"] * TOKENS, device="cuda")}
-    done_ev = [torch.cuda.Event() for _ in layers]
+            sharded.append(ShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype))
     # per-projection device time: an event before each GEMM of every timed step, read after the timed region
     # (the queue stays full, so each interval is that kernel's device time plus the launch gap)
     marks = [[torch.cuda.Event(enable_timing=True) for _ in range(len(layers) + 1)] for _ in range(args.steps)]
@@ -303,21 +305,16 @@ def run(args):
     def step(ev=None):
         for i, L in enumerate(layers):
             act = acts[L["src"]]
-            ldc = L["mp"] if world > 1 else L["m"]
             if ev is not None:
                 ev[i].record(stream)
-            st = gemm_call(h, cb, L, act, ctype, L["c_local"].data_ptr(), ldc)
+            if world == 1:
+                st = gemm_call(h, cb, L, act, ctype, L["c_local"].data_ptr(), L["m"])
+            else:  # this rank's rows, then the all-gather + layout on the comm stream (overlaps the next GEMM)
+                st = sharded[i].run(act, stream, comm)
             if ev is not None and i == len(layers) - 1:
                 ev[i + 1].record(stream)
             if st != 0:
-                raise RuntimeError(f"{L['name']}: cublasGemmEx status {st}")
-            if world > 1:
-                done_ev[i].record(stream)
-                comm.wait_event(done_ev[i])
-                with torch.cuda.stream(comm):
-                    dist.all_gather_into_tensor(full[L["name"]]["gathered"], L["c_local"])
-                    lib.lib.tb200_gather_row_blocks(full[L["name"]]["gathered"].data_ptr(), world, L["mp"], TOKENS, 4,
-                                                    full[L["name"]]["c"].data_ptr(), L["m"], comm.cuda_stream)
+                raise RuntimeError(f"{L['name']}: status {st}")
         if world > 1:
             stream.wait_stream(comm)
 
@@ -355,6 +352,11 @@ def run(args):
         for i in range(len(layers)):
             per_gemm_ms[i] += marks[j][i].elapsed_time(marks[j][i + 1]) / args.steps
     value = STEP_FLOP / (ms * 1e-3) / 1e12
+    gemm_only_ms = sum(per_gemm_ms)  # this rank's GEMMs alone (the all-gathers overlap on the comm stream)
+    if world > 1:
+        t = torch.tensor([gemm_only_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        gemm_only_ms = float(t.item())
 
     pk = peaks()
     dom = layers.index(next(L for L in layers if L["name"] == "lm_head"))
@@ -384,48 +386,60 @@ def run(args):
     # memory (double-buffered on a copy stream, overlapping the previous step) and reads back the last
     # token's logits
     e2e = None
-    if world == 1:
-        hx = [acts["x"].cpu().pin_memory(), acts["h"].cpu().pin_memory()]
-        dev_bufs = [[torch.empty_like(acts["x"]), torch.empty_like(acts["h"])] for _ in range(2)]
-        logits = torch.empty(VOCAB, dtype=torch.float32).pin_memory()
-        copy = torch.cuda.Stream()
-        ready = [torch.cuda.Event() for _ in range(2)]
-        free = [torch.cuda.Event() for _ in range(2)]
-        lm = layers[dom]
-        n_e2e = max(3, min(args.steps, 100))
+    hx = [acts["x"].cpu().pin_memory(), acts["h"].cpu().pin_memory()]
+    dev_bufs = [[torch.empty_like(acts["x"]), torch.empty_like(acts["h"])] for _ in range(2)]
+    logits = torch.empty(VOCAB, dtype=torch.float32).pin_memory()
+    copy = torch.cuda.Stream()
+    ready = [torch.cuda.Event() for _ in range(2)]
+    free = [torch.cuda.Event() for _ in range(2)]
+    lm = layers[dom]
+    n_e2e = max(3, min(args.steps, 100))
 
-        def e2e_step(i):
-            b = i % 2
-            with torch.cuda.stream(copy):
-                copy.wait_event(free[b])
-                dev_bufs[b][0].copy_(hx[0], non_blocking=True)
-                dev_bufs[b][1].copy_(hx[1], non_blocking=True)
-                ready[b].record(copy)
-            stream.wait_event(ready[b])
-            for L2 in layers:
-                act = dev_bufs[b][0] if L2["src"] == "x" else dev_bufs[b][1]
+    def e2e_step(i):
+        b = i % 2
+        with torch.cuda.stream(copy):
+            copy.wait_event(free[b])
+            dev_bufs[b][0].copy_(hx[0], non_blocking=True)
+            dev_bufs[b][1].copy_(hx[1], non_blocking=True)
+            ready[b].record(copy)
+        stream.wait_event(ready[b])
+        for j, L2 in enumerate(layers):
+            act = dev_bufs[b][0] if L2["src"] == "x" else dev_bufs[b][1]
+            if world == 1:
                 st = gemm_call(h, cb, L2, act, ctype, L2["c_local"].data_ptr(), L2["m"])
-                if st != 0:
-                    raise RuntimeError("e2e gemm failed")
-            free[b].record(stream)
-            with torch.cuda.stream(stream):
-                logits.copy_(lm["c_local"][(TOKENS - 1) * lm["m"]:TOKENS * lm["m"]], non_blocking=True)
+            else:
+                st = sharded[j].run(act, stream, comm)
+            if st != 0:
+                raise RuntimeError("e2e gemm failed")
+        if world > 1:
+            stream.wait_stream(comm)
+        free[b].record(stream)
+        c_lm = lm["c_local"] if world == 1 else sharded[dom].c
+        with torch.cuda.stream(stream):
+            logits.copy_(c_lm[(TOKENS - 1) * lm["m"]:TOKENS * lm["m"]], non_blocking=True)
 
-        for i in range(3):
-            e2e_step(i)
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
         torch.cuda.synchronize()
-        f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        f0.record(stream)
-        t_wall = time.perf_counter()
-        for i in range(n_e2e):
-            e2e_step(i)
-        f1.record(stream)
-        torch.cuda.synchronize()
-        t_wall = time.perf_counter() - t_wall
-        e2e_ms = f0.elapsed_time(f1) / n_e2e
-        e2e = {"value": round(STEP_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-               "h2d_bytes_per_step": int(hx[0].numel() * 2 + hx[1].numel() * 2), "d2h_bytes_per_step": VOCAB * 4,
-               "ms_per_step": round(e2e_ms, 4), "wall_ms_per_step": round(t_wall * 1e3 / n_e2e, 4), "steps": n_e2e}
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    t_wall = time.perf_counter()
+    for i in range(n_e2e):
+        e2e_step(i)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    t_wall = time.perf_counter() - t_wall
+    e2e_ms = f0.elapsed_time(f1) / n_e2e
+    if world > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e = {"value": round(STEP_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+           "h2d_bytes_per_step": int(hx[0].numel() * 2 + hx[1].numel() * 2), "d2h_bytes_per_step": VOCAB * 4,
+           "ms_per_step": round(e2e_ms, 4), "wall_ms_per_step": round(t_wall * 1e3 / n_e2e, 4), "steps": n_e2e}
 
     cpu = None
     if rank == 0 and world == 1 and args.impl == "ours" and not args.no_cpu_baseline:
@@ -451,9 +465,15 @@ def run(args):
                        "l2": "inputs larger than L2 (1.9 GB per step); no flush"},
             "frac_of_peak": round(value / pk["bf16_tflops_sustained"], 4),
             "roofline": roofline, "shapes": shapes, "gpu_launches": launches_per_step * args.steps,
+            "gemm_only": {"ms_per_step": round(gemm_only_ms, 4),
+                          "TFLOP/s": round(STEP_FLOP / (gemm_only_ms * 1e-3) / 1e12, 2),
+                          "note": "device time of this rank's GEMMs alone (max over ranks); at N > 1 the "
+                                  "all-gathers run on a second stream and the step time includes them"},
         }
         if args.impl == "reference":
             line["impl"] = "reference"
+            line["n_gpus"] = launched
+            line["note"] = "the reference library is single-GPU: rank 0 ran the whole step on one GPU"
             line["cpu_baseline"] = {"value": line["value"], "unit": "TFLOP/s", "cores": 0, "kind": "reference",
                                     "sample": "the whole step through the reference's own libtinycublas (cublas.c + "
                                               "gemm.cu compiled from source for sm_100a) on one B200; the reference's "
@@ -470,6 +490,8 @@ def run(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        dist.destroy_process_group()
+    elif dist.is_initialized():  # the reference arm under torchrun: rank 0 ran alone
         dist.destroy_process_group()
     return 0
 
