@@ -11,9 +11,10 @@ K 4096->1024, V 4096->1024, O 4096->4096, gate and up 4096->14336, down 14336->4
 Inputs are larger than L2 (1.9 GB touched per step), so no flush is needed between steps.
 
 At N > 1 (torchrun, one process per GPU, NCCL): every projection is N-sharded along m (the weight's
-output features); each rank computes its m/N rows, an NCCL all-gather on a second stream replicates C
-(overlapped with the next projection), and a gather kernel lays the blocks out as the column-major C.
-Total work is fixed, so scaling is "strong".
+output features); each rank computes its m/N rows and its GEMM epilogue stores them into every rank's
+C over NVLink (CUDA IPC mappings, macuda_b200.dist.FusedShardedGemm), with one 4-byte NCCL all-reduce
+per step as the completion barrier; --exchange allgather uses an NCCL all-gather + layout kernel
+instead. Total work is fixed, so scaling is "strong".
 
 Keys beyond the base contract: roofline (dominant kernel = the lm_head GEMM), cpu_baseline (the
 oracle's multithreaded fp16 GEMM on the host, a stand-in for ggml-cpu), e2e (the same step through the
@@ -265,7 +266,7 @@ def run(args):
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout: one JSON line only
+        os.environ["NCCL_DEBUG"] = "WARN"  # keep NCCL's version banner off stdout: one JSON line only
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     if args.impl == "reference":
         from oracle import oracle as O
@@ -292,15 +293,19 @@ def run(args):
     h = lib.handle()
     h.set_stream(stream.cuda_stream)
     sharded = []
+    fused = world > 1 and args.exchange == "fused"
     if world > 1:
-        from macuda_b200.dist import ShardedGemm
+        from macuda_b200.dist import FusedShardedGemm, ShardedGemm, step_barrier
         for L in layers:
-            sharded.append(ShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype))
+            if fused:
+                sharded.append(FusedShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype))
+            else:
+                sharded.append(ShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype))
     # per-projection device time: an event before each GEMM of every timed step, read after the timed region
     # (the queue stays full, so each interval is that kernel's device time plus the launch gap)
     marks = [[torch.cuda.Event(enable_timing=True) for _ in range(len(layers) + 1)] for _ in range(args.steps)]
     per_gemm_ms = [0.0] * len(layers)
-    launches_per_step = len(layers) * (2 if world > 1 else 1)
+    launches_per_step = len(layers) * (2 if world > 1 and not fused else 1)
 
     def step(ev=None):
         for i, L in enumerate(layers):
@@ -309,13 +314,17 @@ def run(args):
                 ev[i].record(stream)
             if world == 1:
                 st = gemm_call(h, cb, L, act, ctype, L["c_local"].data_ptr(), L["m"])
+            elif fused:  # this rank's rows, stored by the epilogue into every rank's C
+                st = sharded[i].run(act, stream)
             else:  # this rank's rows, then the all-gather + layout on the comm stream (overlaps the next GEMM)
                 st = sharded[i].run(act, stream, comm)
             if ev is not None and i == len(layers) - 1:
                 ev[i + 1].record(stream)
             if st != 0:
                 raise RuntimeError(f"{L['name']}: status {st}")
-        if world > 1:
+        if fused:
+            step_barrier(stream)  # every peer's stores into this rank's C have landed
+        elif world > 1:
             stream.wait_stream(comm)
 
     # warm-up
@@ -407,11 +416,15 @@ def run(args):
             act = dev_bufs[b][0] if L2["src"] == "x" else dev_bufs[b][1]
             if world == 1:
                 st = gemm_call(h, cb, L2, act, ctype, L2["c_local"].data_ptr(), L2["m"])
+            elif fused:
+                st = sharded[j].run(act, stream)
             else:
                 st = sharded[j].run(act, stream, comm)
             if st != 0:
                 raise RuntimeError("e2e gemm failed")
-        if world > 1:
+        if fused:
+            step_barrier(stream)
+        elif world > 1:
             stream.wait_stream(comm)
         free[b].record(stream)
         c_lm = lm["c_local"] if world == 1 else sharded[dom].c
@@ -452,6 +465,9 @@ def run(args):
     if rank == 0 and world == 1 and not args.no_decode:
         decode = decode_figures(torch, lib, cb, ctype, dtype)
 
+    if fused:
+        for g in sharded:
+            g.close()
     h.close()
     if rank == 0:
         line = {
@@ -461,7 +477,9 @@ def run(args):
             "dtype": args.dtype, "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) activations; no checkpoint)",
             "config": {"workload": "llama3.1-8b prefill projections q,k,v,o,gate,up,down,lm_head @ 512 tokens "
                                    "(BASELINE configs[1])", "tokens": TOKENS, "step_gflop": round(STEP_FLOP / 1e9, 1),
-                       "parallelism": f"N-shard x{world} + NCCL all-gather" if world > 1 else "single GPU",
+                       "parallelism": (f"N-shard x{world}, C exchanged by " + ("P2P stores from the GEMM epilogue "
+                                       "(NVLink) + one NCCL barrier per step" if fused else "NCCL all-gather + "
+                                       "layout kernel")) if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (1.9 GB per step); no flush"},
             "frac_of_peak": round(value / pk["bf16_tflops_sustained"], 4),
             "roofline": roofline, "shapes": shapes, "gpu_launches": launches_per_step * args.steps,
@@ -507,6 +525,8 @@ def main():
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--gemm", default=None, help="MxNxK: time one T,N GEMM alone (profiling)")
+    ap.add_argument("--exchange", choices=["fused", "allgather"], default="fused",
+                    help="N > 1: how the sharded C is replicated")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

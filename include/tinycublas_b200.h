@@ -136,6 +136,29 @@ int tb200_device_error(void);
 cublasStatus_t tb200_gather_row_blocks(const void *parts, int P, int rows, int n, int elem_bytes, void *C,
                                        int ldc, int m_total, cudaStream_t stream);
 
+/* The N-sharded GEMM with its output exchange fused into the epilogue (no reference counterpart: the
+ * reference is single-GPU). This rank computes rows [row0, row0 + m_local) of C = alpha * op(A) op(B)
+ * (A holds only those rows: m_local x k under op T) and stores them into each of the P replicas of C
+ * (C_replicas: a HOST array of P device pointers valid in this process - this GPU's own C and the
+ * peers' C mapped with tb200_ipc_open), each m x n with leading dimension ldc >= row0 + m_local.
+ * Peers' replicas are written over NVLink by the tensor-core epilogue while later tiles compute.
+ * beta is 0 (C is overwritten). Completion on a peer is known only after a cross-GPU synchronisation
+ * that follows this launch on every rank (e.g. an NCCL collective on the same stream).
+ * Returns NOT_SUPPORTED when the operands do not fit the tensor-core kernel (alignment, types). */
+cublasStatus_t tb200_gemm_ex_allgather(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb,
+                                       int m_local, int n, int k, const void *alpha, const void *A, cudaDataType Atype,
+                                       int lda, const void *B, cudaDataType Btype, int ldb, void *const *C_replicas,
+                                       int P, cudaDataType Ctype, int ldc, int row0, cublasComputeType_t computeType);
+
+/* Set-up helpers for the replicas (not on the GEMM path): device memory another process of the node can
+ * map. tb200_ipc_alloc returns the pointer and writes the 64-byte CUDA IPC handle to `handle`;
+ * tb200_ipc_open maps a peer's handle into this process; tb200_ipc_close unmaps it; tb200_ipc_free
+ * releases memory from tb200_ipc_alloc. */
+cublasStatus_t tb200_ipc_alloc(size_t bytes, void **ptr, void *handle);
+cublasStatus_t tb200_ipc_open(const void *handle, void **ptr);
+cublasStatus_t tb200_ipc_close(void *ptr);
+cublasStatus_t tb200_ipc_free(void *ptr);
+
 /* HBM probes, the counterparts of gemm.cu:421-431: stream n4 16-byte writes of v, or n4 16-byte
  * reads folded into *sink. Asynchronous on `stream`. */
 cublasStatus_t tb200_bw_write(void *p, long long n4, float v, cudaStream_t stream);

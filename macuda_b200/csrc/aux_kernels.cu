@@ -2,6 +2,7 @@
 // gather used after an N-sharded GEMM's all-gather, HBM bandwidth probes, and device queries.
 #include <cuda_runtime.h>
 #include <stdio.h>
+#include <string.h>
 #include "tb200_internal.h"
 #include "tinycublas_b200.h"
 
@@ -116,4 +117,38 @@ extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_bw_read(c
   if (n4 <= 0) return CUBLAS_STATUS_SUCCESS;
   tb200_bw_read_kernel<<<grid_for(n4, 256), 256, 0, stream>>>((const float4 *)p, n4, sink);
   return cudaGetLastError() == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+// ---- device memory that other processes of the node can map (the N-sharded GEMM's C replicas) ----
+// Set-up calls, never on the GEMM path. `handle` is the 64-byte cudaIpcMemHandle_t.
+extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_ipc_alloc(size_t bytes, void **ptr,
+                                                                                  void *handle) {
+  if (!ptr || !handle || bytes == 0) return CUBLAS_STATUS_INVALID_VALUE;
+  *ptr = nullptr;
+  if (cudaMalloc(ptr, bytes) != cudaSuccess) return CUBLAS_STATUS_ALLOC_FAILED;
+  cudaIpcMemHandle_t hd;
+  if (cudaIpcGetMemHandle(&hd, *ptr) != cudaSuccess) {
+    cudaFree(*ptr);
+    *ptr = nullptr;
+    return CUBLAS_STATUS_EXECUTION_FAILED;
+  }
+  memcpy(handle, &hd, sizeof hd);
+  return CUBLAS_STATUS_SUCCESS;
+}
+
+extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_ipc_open(const void *handle, void **ptr) {
+  if (!ptr || !handle) return CUBLAS_STATUS_INVALID_VALUE;
+  cudaIpcMemHandle_t hd;
+  memcpy(&hd, handle, sizeof hd);
+  *ptr = nullptr;
+  return cudaIpcOpenMemHandle(ptr, hd, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess ? CUBLAS_STATUS_SUCCESS
+                                                                                      : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_ipc_close(void *ptr) {
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_ipc_free(void *ptr) {
+  return cudaFree(ptr) == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
 }

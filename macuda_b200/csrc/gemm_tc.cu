@@ -64,6 +64,8 @@ struct TcParams {
   uint32_t a_cstride, a_kstep, b_cstride, b_kstep;
   int epr;   // elements per 128-byte row: 64 for 16-bit, 32 for f32
   int bk;    // k elements per stage
+  int nrep, row0;  // replicated output: rows go to row0 + row of each of nrep replicas (beta == 0)
+  void *rep[8];
 };
 
 // KC = 128-byte k-chunks per stage. One stage holds A (128 rows) and B (BN rows) for KC * epr values of
@@ -320,7 +322,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int col0 = n0 + c * 32;
         if (row_ok && col0 < p.n) {
           const int ncols = p.n - col0 < 32 ? p.n - col0 : 32;
-          if (p.beta == 0.f) {
+          if (p.nrep > 0) {
+            // N-sharded GEMM: this rank's rows go straight into every replica of C, peers' over NVLink
+            for (int q = 0; q < p.nrep; ++q) {
+              char *Cq = (char *)p.rep[q] + (long long)p.row0 * osz;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < ncols)
+                  store_out(Cq, row + (long long)(col0 + j) * p.ldc, p.alpha * __uint_as_float(r[j]), p.out_type);
+            }
+          } else if (p.beta == 0.f) {
             if (p.out_type == 0 && p.alpha == 1.f) {
               float *dst = (float *)Cb + row + (long long)col0 * p.ldc;
 #pragma unroll
@@ -356,6 +367,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   }
 
+  if (p.nrep > 0 && warp >= 2 && warp <= 5) __threadfence_system();  // peers' replicas: stores performed
   tc_fence_before();
   __syncwarp();
   if (CG == 2) cluster_sync();  // neither CTA leaves while its pair may still touch its memory or barriers
@@ -482,7 +494,7 @@ extern "C" int tb200_tc_ok(const tb200_gemm_t *g) {
 }
 
 extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s) {
-  if (!tb200_tc_ok(g)) return tb200_launch_simt(g, s);
+  if (!tb200_tc_ok(g)) return g->nrep ? (int)cudaErrorNotSupported : tb200_launch_simt(g, s);
   const bool f32in = g->in_type == TB200_F32;
   const int es = f32in ? 4 : 2;
   const int epr = 128 / es;
@@ -509,6 +521,7 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int 
     else ok = make_map(&tb, dt, es, g->B, g->n, g->k, g->ldb, g->batch, g->sB, epr, epr * kc, &p.b_batched);
   }
   if (!ok) {
+    if (g->nrep) return (int)cudaErrorNotSupported;  // only the tensor-core epilogue replicates
     if (tb200_trace()) fprintf(stderr, "[trace] tensor map refused; SIMT kernel instead\n");
     return tb200_launch_simt(g, s);
   }
@@ -523,6 +536,9 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int 
   p.group_m = 8;
   p.alpha = g->alpha; p.beta = g->beta;
   p.C = g->C; p.ldc = g->ldc; p.sC = g->sC; p.out_type = g->out_type;
+  p.nrep = g->nrep;
+  p.row0 = g->row0;
+  for (int q = 0; q < g->nrep && q < 8; ++q) p.rep[q] = g->rep[q];
   p.a_mn = a_mn; p.b_mn = b_mn;
   // K-major: 8-row core groups 1024 bytes apart (SBO), chunk c of a stage rows*128 bytes in, UMMA_K step
   // = 32 bytes inside the swizzle atom. MN-major: 128-byte rows along m/n, 8 k-rows per 1024-byte atom

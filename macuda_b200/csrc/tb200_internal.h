@@ -26,6 +26,11 @@ typedef struct {
   void *C; int ldc; long long sC; void *const *Carr;
   int in_type, out_type;    /* TB200_F32 / F16 / BF16 */
   int tf32;                 /* f32 inputs only: 1 = TF32 tensor cores allowed */
+  /* replicated output (N-sharded GEMM with the exchange fused into the epilogue): when nrep > 0 the
+   * rows are stored at row offset row0 into each of the nrep replicas (device pointers valid in this
+   * process, peers' buffers included) instead of C; tensor-core kernel only, beta == 0, batch == 1 */
+  int nrep, row0;
+  void *rep[8];
 } tb200_gemm_t;
 
 int tb200_launch_simt(const tb200_gemm_t *g, cudaStream_t s);

@@ -402,4 +402,47 @@ cublasStatus_t cublasStrsmBatched(cublasHandle_t handle, cublasSideMode_t side, 
   return rc == 0 ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
 }
 
+cublasStatus_t tb200_gemm_ex_allgather(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb,
+                                       int m_local, int n, int k, const void *alpha, const void *A, cudaDataType Atype,
+                                       int lda, const void *B, cudaDataType Btype, int ldb, void *const *C_replicas,
+                                       int P, cudaDataType Ctype, int ldc, int row0, cublasComputeType_t ct) {
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  tb200_gemm_t g;
+  memset(&g, 0, sizeof g);
+  int tf32 = 0;
+  if (gemm_contract(Atype, Btype, Ctype, ct, &g.in_type, &g.out_type, &tf32)) return CUBLAS_STATUS_NOT_SUPPORTED;
+  g.opA = op_code(transa);
+  g.opB = op_code(transb);
+  if (!C_replicas || P < 1 || P > 8 || row0 < 0 || !alpha) return CUBLAS_STATUS_INVALID_VALUE;
+  for (int q = 0; q < P; q++)
+    if (!C_replicas[q]) return CUBLAS_STATUS_INVALID_VALUE;
+  cublasStatus_t st = check_args(g.opA, g.opB, m_local, n, k, lda, ldb, ldc, 1);
+  if (st != CUBLAS_STATUS_SUCCESS) return st;
+  if ((long long)row0 + m_local > ldc) return CUBLAS_STATUS_INVALID_VALUE; /* rows stay inside each replica's column */
+  if (m_local == 0 || n == 0) return CUBLAS_STATUS_SUCCESS;
+  g.tf32 = tf32;
+  g.m = m_local;
+  g.n = n;
+  g.k = k;
+  g.batch = 1;
+  g.alpha = read_scalar(alpha, ct);
+  g.beta = 0.f;
+  g.A = A; g.lda = lda;
+  g.B = B; g.ldb = ldb;
+  g.C = C_replicas[0]; g.ldc = ldc;
+  g.nrep = P;
+  g.row0 = row0;
+  for (int q = 0; q < P; q++) g.rep[q] = C_replicas[q];
+  if (!operands_aligned(&g) || !tb200_tc_ok(&g)) return CUBLAS_STATUS_NOT_SUPPORTED;
+  int sms = tb200_num_sms(), pair = 0;
+  int bn = tb200_tc_tile_n(m_local, n, 1, sms, &pair);
+  if (tb200_trace())
+    fprintf(stderr, "[trace] gemm tc-allgather m_local=%d n=%d k=%d P=%d row0=%d BN=%d pair=%d\n", m_local, n, k, P, row0,
+            bn, pair);
+  int rc = tb200_launch_tc(&g, bn, pair, sms, h->stream);
+  if (rc == (int)cudaErrorNotSupported) return CUBLAS_STATUS_NOT_SUPPORTED;
+  return rc == 0 ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
 const char *tb200_version(void) { return "tinycublas_b200 " TB200_GIT_DESCRIBE " sm_100a"; }

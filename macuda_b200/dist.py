@@ -1,14 +1,17 @@
-"""N-sharded GEMM across the GPUs of one node: each rank computes its rows of C, NCCL all-gathers them.
+"""N-sharded GEMM across the GPUs of one node: each rank computes its rows of C, every rank ends with all of C.
 
 The reference is single-GPU. For the largest GEMMs (lm_head, FFN, big squares) this library splits the
-weight's output features - cuBLAS m under ggml's (T, N) call - across P ranks, one process per GPU:
+weight's output features - cuBLAS m under ggml's (T, N) call - across P ranks, one process per GPU;
+rank r owns weight rows [r*mp, r*mp + rows_r) with mp = ceil(m / P) (the last rank may own fewer).
+Two ways to replicate C:
 
-  rank r owns weight rows [r*mp, r*mp + rows_r) with mp = ceil(m / P) (the last rank may own fewer);
-  it runs cublasGemmEx(T, N, rows_r, n, k) into a local column-major block of mp x n (ldc = mp);
-  an NCCL all-gather over NVLink concatenates the P blocks ([P][mp x n]) on a communication stream;
-  tb200_gather_row_blocks lays them out as the column-major m x n C (ldc >= m), dropping the padding rows.
+  FusedShardedGemm (default): every rank's C is mapped into every other rank (CUDA IPC); the tensor-core
+    epilogue of tb200_gemm_ex_allgather stores this rank's rows into all P replicas, the peers' over
+    NVLink P2P, overlapping the exchange with the remaining tiles; one 4-byte NCCL all-reduce per step
+    tells each rank that its peers' stores have landed.
+  ShardedGemm: the GEMM writes a local mp x n block, an NCCL all-gather on a communication stream
+    concatenates the P blocks, and tb200_gather_row_blocks lays them out as the column-major C.
 
-Nothing here touches another GPU's memory directly: peer data arrives through NCCL into local memory.
 `gather_row_blocks_host` is the host mirror of the device gather (the layout contract the tests pin).
 """
 from __future__ import annotations
@@ -84,3 +87,93 @@ class ShardedGemm:
                                                        self.elem, self.c.data_ptr(), self.m, self.m, comm.cuda_stream)
         self.done.record(comm)
         return st or st2
+
+
+class _DeviceArray:
+    """A raw device allocation exposed to torch through __cuda_array_interface__ (no copy)."""
+
+    def __init__(self, ptr: int, count: int, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": (count,), "typestr": typestr, "data": (ptr, False), "version": 3,
+                                         "strides": None, "stream": None}
+
+
+class FusedShardedGemm:
+    """N-sharded GEMM with the output exchange fused into the tensor-core epilogue.
+
+    Every rank allocates its full C (m x n, f32) with tb200_ipc_alloc, the 64-byte IPC handles are
+    all-gathered, and each rank maps every peer's C (tb200_ipc_open). `run` launches
+    tb200_gemm_ex_allgather: this rank's rows are stored into all P replicas of C by the epilogue, the
+    peers' over NVLink P2P while later tiles still compute - no all-gather call, no layout kernel.
+    After the last GEMM of a step, `step_barrier` (a 4-byte NCCL all-reduce on the compute stream) tells
+    every rank that all peers' kernels, and so their stores into its C, have completed.
+    """
+
+    def __init__(self, lib, handle, m: int, n: int, k: int, rank: int, world: int, w_local, dtype_code: int,
+                 group=None):
+        import ctypes
+
+        import torch
+        import torch.distributed as dist
+        self.lib, self.h = lib, handle
+        self.m, self.n, self.k = m, n, k
+        self.rank, self.world, self.group = rank, world, group
+        self.first, self.rows, self.mp = shard_rows(m, world, rank)
+        self.w = w_local
+        self.dtype_code = dtype_code
+        own = ctypes.c_void_p()
+        hbuf = ctypes.create_string_buffer(64)
+        st = lib.lib.tb200_ipc_alloc(m * n * 4, ctypes.byref(own), hbuf)
+        if st != 0:
+            raise RuntimeError(f"tb200_ipc_alloc: status {st}")
+        handles = [None] * world
+        dist.all_gather_object(handles, hbuf.raw, group=group)
+        self.reps, self.opened = [], []
+        for r in range(world):
+            if r == rank:
+                self.reps.append(own.value)
+                continue
+            p = ctypes.c_void_p()
+            st = lib.lib.tb200_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(p))
+            if st != 0:
+                raise RuntimeError(f"tb200_ipc_open (rank {r}): status {st}")
+            self.reps.append(p.value)
+            self.opened.append(p.value)
+        self.own = own.value
+        self.rep_array = (ctypes.c_void_p * world)(*self.reps)
+        self.c = torch.as_tensor(_DeviceArray(self.own, m * n), device="cuda")
+
+    def run(self, x, stream=None) -> int:
+        import ctypes
+        from . import cublas as cb
+        if self.rows == 0:
+            return 0
+        one = ctypes.c_float(1.0)
+        return self.lib.lib.tb200_gemm_ex_allgather(
+            self.h.h, cb.CUBLAS_OP_T, cb.CUBLAS_OP_N, self.rows, self.n, self.k, ctypes.byref(one), self.w.data_ptr(),
+            self.dtype_code, self.k, x.data_ptr(), self.dtype_code, self.k, self.rep_array, self.world, cb.CUDA_R_32F,
+            self.m, self.first, cb.CUBLAS_COMPUTE_32F)
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            self.lib.lib.tb200_ipc_close(p)
+        self.opened = []
+        dist.barrier(group=self.group)  # every peer has unmapped this rank's C before it is freed
+        if self.own:
+            self.lib.lib.tb200_ipc_free(self.own)
+            self.own = 0
+
+
+def step_barrier(stream, group=None, _flag={}):
+    """A 4-byte NCCL all-reduce on `stream`: when it completes on a rank, every rank's earlier kernels on
+    its stream - and so every peer store into this rank's replicas - have completed."""
+    import torch
+    import torch.distributed as dist
+    dev = torch.cuda.current_device()
+    if dev not in _flag:
+        _flag[dev] = torch.zeros(1, dtype=torch.int32, device="cuda")
+    with torch.cuda.stream(stream):
+        dist.all_reduce(_flag[dev], group=group)

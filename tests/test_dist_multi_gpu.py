@@ -1,0 +1,92 @@
+"""The N-sharded GEMM on 2 GPUs (skipped with fewer): both exchanges, every rank's full C - including
+the rows its peer computed and delivered (over NCCL, or by P2P stores from the peer's epilogue) - checked
+against the fp64 oracle on seeded row samples."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, mode, m, n, k, q):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ok, info = False, ""
+    try:
+        from macuda_b200 import cublas as cb
+        from macuda_b200.dist import FusedShardedGemm, ShardedGemm, shard_rows, step_barrier
+        from oracle import oracle as O
+        lib = cb.library()
+        h = lib.handle()
+        stream = torch.cuda.Stream()
+        h.set_stream(stream.cuda_stream)
+        rng = np.random.default_rng(7)
+        W = O.to_bits(rng.normal(0, 0.02, m * k).astype(np.float32), O.F16)  # m rows of k: op T, lda = k
+        X = O.to_bits(rng.normal(0, 1, k * n).astype(np.float32), O.F16)
+        first, rows, _ = shard_rows(m, world, rank)
+        w_local = torch.from_numpy(W[first * k:(first + rows) * k].view(np.int16).copy()).cuda()
+        x = torch.from_numpy(X.view(np.int16)).cuda()
+        if mode == "fused":
+            g = FusedShardedGemm(lib, h, m, n, k, rank, world, w_local, cb.CUDA_R_16F)
+            g.c.fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier()
+            for _ in range(2):  # twice: the second run overwrites the first in place
+                st = g.run(x, stream)
+                step_barrier(stream)
+            torch.cuda.synchronize()
+            C = g.c.cpu().numpy()
+        else:
+            g = ShardedGemm(lib, h, m, n, k, rank, world, w_local, cb.CUDA_R_16F)
+            comm = torch.cuda.Stream()
+            st = g.run(x, stream, comm)
+            torch.cuda.synchronize()
+            C = g.c.cpu().numpy()
+        rows_s = np.unique(np.concatenate([np.arange(0, m, 37), [first, m - 1]])).astype(np.int32)
+        R, S = O.gemm(1, 0, m, n, k, 1.0, W, O.F16, k, X, O.F16, k, rows=rows_s)
+        res = O.check(O.extract(C, O.F32, m, n, m, rows=rows_s), R, S, O.F32)
+        ok, info = (st == 0 and res["ok"]), f"st={st} {res}"
+        if mode == "fused":
+            g.close()
+        h.close()
+    except Exception as ex:
+        info = repr(ex)
+    q.put((rank, ok, info))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("mode", ["fused", "allgather"])
+def test_two_gpu_sharded_gemm(mode):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    m, n, k = 4096 + 256, 512, 2048
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, m, n, k, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=300) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    for rank, ok, info in out:
+        assert ok, f"rank {rank}: {info}"
