@@ -39,7 +39,8 @@ extern "C" {
  * binds the legacy default stream and records the current device. Touches no device memory. */
 cublasStatus_t cublasCreate_v2(cublasHandle_t *handle);
 
-/* replaces cublas.c:245-247. Frees the handle and any workspace the library allocated for it. */
+/* replaces cublas.c:245-247. Frees the handle and any scratch the library allocated for it (waiting for
+ * the streams that used it). */
 cublasStatus_t cublasDestroy_v2(cublasHandle_t handle);
 
 /* replaces cublas.c:248. NULL selects the legacy default stream. */
@@ -123,6 +124,12 @@ int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_ty
  * tile width (32, 64, 128 or 256) and sets *pair (if not NULL) to 1 for the 256 x 256 tile of a CTA pair.
  * Pure function, pinned by host-only tests. */
 int tb200_tc_tile_n(int m, int n, int batch, int num_sms, int *pair);
+
+/* Device scratch allocations this handle has made so far (test hook, the counterpart of the reference's
+ * tinycublas_splitk_ws_allocs, cublas.c:91-92). The library allocates scratch only for pointer-array
+ * batches on the tensor cores: one buffer per (handle, stream), made at the first such call on that
+ * stream outside stream capture and grown when needed; Destroy frees it. */
+unsigned tb200_scratch_allocs(cublasHandle_t handle);
 
 /* Last error a kernel of this library recorded on the current device (0 = none): a bounded wait in
  * the tensor-core pipeline that gave up (1), or an internal inconsistency (2). Reading it clears it.

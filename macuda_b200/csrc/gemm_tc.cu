@@ -66,6 +66,11 @@ struct TcParams {
   int bk;    // k elements per stage
   int nrep, row0;  // replicated output: rows go to row0 + row of each of nrep replicas (beta == 0)
   void *rep[8];
+  // pointer-array batches: per batch element b, maps[2b] (A) and maps[2b+1] (B) in global memory, C from
+  // Carr[b]; the launch does nothing if *skip != 0 (some pointer unfit for TMA: the general kernel runs)
+  const CUtensorMap *maps;
+  void *const *Carr;
+  const int *skip;
 };
 
 // KC = 128-byte k-chunks per stage. One stage holds A (128 rows) and B (BN rows) for KC * epr values of
@@ -144,6 +149,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint32_t *tmem_slot = (uint32_t *)(drain + 1);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
+  // uniform early exit, before any barrier or TMEM allocation: every thread of every CTA reads the same flag
+  if (p.skip && *(volatile const int *)p.skip != 0) return;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
@@ -190,7 +197,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ------------------------------------------------------------------ TMA producers (A: warp 0, B: warp 6)
     if (lane == 0) {
       const bool is_a = warp == 0;
-      const CUtensorMap *tm = is_a ? &tmA : &tmB;
+      const CUtensorMap *tm0 = is_a ? &tmA : &tmB;
       uint8_t *base = is_a ? smA : smB;
       const int stage_bytes = is_a ? Cfg::A_BYTES : Cfg::B_BYTES;
       const int rows = is_a ? TC_BM : Cfg::B_ROWS;
@@ -203,6 +210,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         int b, mt, nt;
         decode_tile(p, t, b, mt, nt);
         const int mn0 = is_a ? mt * (TC_BM * CG) + (int)rank * TC_BM : nt * BN + (int)rank * Cfg::B_ROWS;
+        const CUtensorMap *tm = tm0;
+        if (p.maps) {  // this batch element's own map, written by the prep kernel through the generic proxy
+          tm = p.maps + 2 * b + (is_a ? 0 : 1);
+          fence_tensormap_acquire(tm);
+        }
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, WAIT_BUDGET_CYC)) break;
           // the even CTA announces the bytes of both CTAs; the odd CTA's copies only complete them
@@ -312,7 +324,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_after();
       const int row = mt * (TC_BM * CG) + (int)rank * TC_BM + quad * 32 + lane;
       const int n0 = nt * BN;
-      char *Cb = (char *)p.C + (long long)b * p.sC * osz;
+      char *Cb = p.Carr ? (char *)p.Carr[b] : (char *)p.C + (long long)b * p.sC * osz;
       const bool row_ok = row < p.m;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -384,6 +396,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 }  // namespace
 
 namespace {
+
+// One thread per batch element of a pointer-array GEMM: copies the template maps (built on the host with a
+// placeholder address) to maps[2b] / maps[2b+1], points them at Aarr[b] / Barr[b], and raises *bad when a
+// pointer is not 16-byte aligned (a TMA source must be) so that the tensor-core launch stands down.
+__global__ void tb200_ptr_maps_kernel(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
+                                      const void *const *Aarr, const void *const *Barr, CUtensorMap *maps, int batch,
+                                      int *bad) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= batch) return;
+  const void *a = Aarr[b];
+  const void *bb = Barr[b];
+  if ((((uintptr_t)a) | ((uintptr_t)bb)) & 15) atomicOr(bad, 1);
+  maps[2 * b] = tA;
+  maps[2 * b + 1] = tB;
+  tensormap_set_address(&maps[2 * b], a);
+  tensormap_set_address(&maps[2 * b + 1], bb);
+  fence_tensormap_release();
+}
 
 // ---------------------------------------------------------------------------------- host side
 
@@ -493,8 +523,8 @@ extern "C" int tb200_tc_ok(const tb200_gemm_t *g) {
   return 1;
 }
 
-extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s) {
-  if (!tb200_tc_ok(g)) return g->nrep ? (int)cudaErrorNotSupported : tb200_launch_simt(g, s);
+// The shared launcher. ptr_ws != NULL: pointer-array batch, scratch laid out as [flag (256 B)][maps].
+static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, void *ptr_ws, cudaStream_t s) {
   const bool f32in = g->in_type == TB200_F32;
   const int es = f32in ? 4 : 2;
   const int epr = 128 / es;
@@ -514,12 +544,17 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int 
   CUtensorMap ta, tb;
   bool ok;
   const int kc = cg == 2 ? 1 : kc_for(bn);
-  if (!a_mn) ok = make_map(&ta, dt, es, g->A, g->k, g->m, g->lda, g->batch, g->sA, epr, TC_BM, &p.a_batched);
-  else ok = make_map(&ta, dt, es, g->A, g->m, g->k, g->lda, g->batch, g->sA, epr, epr * kc, &p.a_batched);
+  // pointer arrays: rank-2 template maps with a placeholder address, re-pointed per element on the device
+  const void *baseA = ptr_ws ? (const void *)(uintptr_t)0x10000 : g->A;
+  const void *baseB = ptr_ws ? (const void *)(uintptr_t)0x10000 : g->B;
+  const int mbatch = ptr_ws ? 1 : g->batch;
+  if (!a_mn) ok = make_map(&ta, dt, es, baseA, g->k, g->m, g->lda, mbatch, g->sA, epr, TC_BM, &p.a_batched);
+  else ok = make_map(&ta, dt, es, baseA, g->m, g->k, g->lda, mbatch, g->sA, epr, epr * kc, &p.a_batched);
   if (ok) {
-    if (!b_mn) ok = make_map(&tb, dt, es, g->B, g->k, g->n, g->ldb, g->batch, g->sB, epr, b_rows, &p.b_batched);
-    else ok = make_map(&tb, dt, es, g->B, g->n, g->k, g->ldb, g->batch, g->sB, epr, epr * kc, &p.b_batched);
+    if (!b_mn) ok = make_map(&tb, dt, es, baseB, g->k, g->n, g->ldb, mbatch, g->sB, epr, b_rows, &p.b_batched);
+    else ok = make_map(&tb, dt, es, baseB, g->n, g->k, g->ldb, mbatch, g->sB, epr, epr * kc, &p.b_batched);
   }
+  if (!ok && ptr_ws) return (int)cudaErrorNotSupported;  // the caller takes the general kernel
   if (!ok) {
     if (g->nrep) return (int)cudaErrorNotSupported;  // only the tensor-core epilogue replicates
     if (tb200_trace()) fprintf(stderr, "[trace] tensor map refused; SIMT kernel instead\n");
@@ -539,6 +574,21 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int 
   p.nrep = g->nrep;
   p.row0 = g->row0;
   for (int q = 0; q < g->nrep && q < 8; ++q) p.rep[q] = g->rep[q];
+  if (ptr_ws) {
+    int *flag = (int *)ptr_ws;
+    CUtensorMap *maps = (CUtensorMap *)((char *)ptr_ws + 256);
+    p.maps = maps;
+    p.Carr = g->Carr;
+    p.skip = flag;
+    cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), s);
+    if (e != cudaSuccess) return (int)e;
+    const unsigned blocks = (unsigned)((g->batch + 127) / 128);
+    if (tb200_trace())
+      fprintf(stderr, "[trace] launch tb200_ptr_maps_kernel grid=(%u,1,1) block=(128,1,1) batch=%d\n", blocks, g->batch);
+    tb200_ptr_maps_kernel<<<blocks, 128, 0, s>>>(ta, tb, g->Aarr, g->Barr, maps, g->batch, flag);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return (int)e;
+  }
   p.a_mn = a_mn; p.b_mn = b_mn;
   // K-major: 8-row core groups 1024 bytes apart (SBO), chunk c of a stage rows*128 bytes in, UMMA_K step
   // = 32 bytes inside the swizzle atom. MN-major: 128-byte rows along m/n, 8 k-rows per 1024-byte atom
@@ -557,24 +607,45 @@ extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int 
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
             ((uint32_t)(bn >> 3) << 17) | ((uint32_t)((TC_BM * cg) >> 4) << 24);
 
+  int rc;
   if (cg == 2) {
-    if (f32in) return launch_bn<1, 256, 1, 2>(ta, tb, p, num_sms, s);
-    return launch_bn<0, 256, 1, 2>(ta, tb, p, num_sms, s);
-  }
-  if (f32in) {
+    rc = f32in ? launch_bn<1, 256, 1, 2>(ta, tb, p, num_sms, s) : launch_bn<0, 256, 1, 2>(ta, tb, p, num_sms, s);
+  } else if (f32in) {
     switch (bn) {
-      case 32: return launch_bn<1, 32, kc_for(32), 1>(ta, tb, p, num_sms, s);
-      case 64: return launch_bn<1, 64, kc_for(64), 1>(ta, tb, p, num_sms, s);
-      case 128: return launch_bn<1, 128, kc_for(128), 1>(ta, tb, p, num_sms, s);
-      default: return launch_bn<1, 256, kc_for(256), 1>(ta, tb, p, num_sms, s);
+      case 32: rc = launch_bn<1, 32, kc_for(32), 1>(ta, tb, p, num_sms, s); break;
+      case 64: rc = launch_bn<1, 64, kc_for(64), 1>(ta, tb, p, num_sms, s); break;
+      case 128: rc = launch_bn<1, 128, kc_for(128), 1>(ta, tb, p, num_sms, s); break;
+      default: rc = launch_bn<1, 256, kc_for(256), 1>(ta, tb, p, num_sms, s); break;
+    }
+  } else {
+    switch (bn) {
+      case 32: rc = launch_bn<0, 32, kc_for(32), 1>(ta, tb, p, num_sms, s); break;
+      case 64: rc = launch_bn<0, 64, kc_for(64), 1>(ta, tb, p, num_sms, s); break;
+      case 128: rc = launch_bn<0, 128, kc_for(128), 1>(ta, tb, p, num_sms, s); break;
+      default: rc = launch_bn<0, 256, kc_for(256), 1>(ta, tb, p, num_sms, s); break;
     }
   }
-  switch (bn) {
-    case 32: return launch_bn<0, 32, kc_for(32), 1>(ta, tb, p, num_sms, s);
-    case 64: return launch_bn<0, 64, kc_for(64), 1>(ta, tb, p, num_sms, s);
-    case 128: return launch_bn<0, 128, kc_for(128), 1>(ta, tb, p, num_sms, s);
-    default: return launch_bn<0, 256, kc_for(256), 1>(ta, tb, p, num_sms, s);
-  }
+  if (rc != 0 || !ptr_ws) return rc;
+  // the general kernel behind it: it computes the batch only if some pointer was unfit for TMA
+  tb200_gemm_t gf = *g;
+  gf.run_if = p.skip;
+  return tb200_launch_simt(&gf, s);
+}
+
+extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s) {
+  if (!tb200_tc_ok(g)) return g->nrep ? (int)cudaErrorNotSupported : tb200_launch_simt(g, s);
+  return launch_tc_impl(g, tile_n, pair, num_sms, nullptr, s);
+}
+
+extern "C" size_t tb200_tc_ptr_ws_bytes(int batch) { return 256 + (size_t)(batch > 0 ? batch : 0) * 256; }
+
+extern "C" int tb200_launch_tc_ptr(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, void *ws, cudaStream_t s) {
+  const int es = g->in_type == TB200_F32 ? 4 : 2;
+  if (!ws || !g->Aarr || !g->Barr || !g->Carr || g->nrep || g->k <= 0) return (int)cudaErrorNotSupported;
+  if (g->in_type == TB200_F32 && (g->opA != 1 || g->opB != 0)) return (int)cudaErrorNotSupported;
+  if (((long long)g->lda * es) % 16 || ((long long)g->ldb * es) % 16) return (int)cudaErrorNotSupported;
+  if (((uintptr_t)ws) & 255) return (int)cudaErrorNotSupported;
+  return launch_tc_impl(g, tile_n, pair, num_sms, ws, s);
 }
 
 extern "C" __attribute__((visibility("default"))) int tb200_device_error(void) {

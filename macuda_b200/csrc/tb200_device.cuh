@@ -126,6 +126,19 @@ __device__ __forceinline__ void tma_load_3d_cg2(void *dst, const void *tmap, uin
       "l"((uint64_t)tmap), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
+// tensor maps edited in global memory (pointer-array batches): the writer replaces the global address
+// and releases through the tensormap proxy; the reader acquires before the first TMA that uses the map
+__device__ __forceinline__ void tensormap_set_address(void *gmap, const void *addr) {
+  asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;" ::"l"((uint64_t)gmap),
+               "l"((uint64_t)addr)
+               : "memory");
+}
+__device__ __forceinline__ void fence_tensormap_release() {
+  asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
+}
+__device__ __forceinline__ void fence_tensormap_acquire(const void *gmap) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"((uint64_t)gmap) : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)tmap) : "memory");
 }

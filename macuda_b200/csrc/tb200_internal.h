@@ -31,11 +31,18 @@ typedef struct {
    * process, peers' buffers included) instead of C; tensor-core kernel only, beta == 0, batch == 1 */
   int nrep, row0;
   void *rep[8];
+  /* the general kernel runs only if *run_if != 0 (NULL: always): the fallback launch behind a
+   * pointer-array tensor-core launch, taken when some batch pointer is not 16-byte aligned */
+  const int *run_if;
 } tb200_gemm_t;
 
 int tb200_launch_simt(const tb200_gemm_t *g, cudaStream_t s);
 int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s);
 int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s);
+/* pointer-array batches on the tensor cores: `ws` is device scratch of tb200_tc_ptr_ws_bytes(batch)
+ * bytes owned by the caller for the duration of the launch */
+size_t tb200_tc_ptr_ws_bytes(int batch);
+int tb200_launch_tc_ptr(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, void *ws, cudaStream_t s);
 int tb200_launch_trsm_rupn(const float *const *A, float *const *B, int rows, int n, int lda, int ldb, float alpha,
                            int batch, cudaStream_t s);
 

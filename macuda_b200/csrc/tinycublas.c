@@ -28,13 +28,64 @@
 #define TB200_GIT_DESCRIBE "unknown"
 #endif
 
+/* Device scratch the library allocates for itself: one buffer per (handle, stream), so that two
+ * streams sharing a handle never share scratch (the reference's per-handle split-K workspace did, and
+ * raced: cublas.c:56-61). Made lazily, outside any stream capture, and grown when a call needs more. */
+#define TB200_WS_SLOTS 8
+struct tb200_ws {
+  cudaStream_t stream;
+  void *ptr;
+  size_t bytes;
+};
+
 struct tb200_handle {
   cudaStream_t stream;
   cublasMath_t math_mode;
   int device;
   void *user_ws;
   size_t user_ws_bytes;
+  struct tb200_ws ws[TB200_WS_SLOTS];
+  unsigned ws_allocs; /* allocations made, for the tests */
 };
+
+/* scratch of at least `bytes` for the handle's current stream, or NULL (capturing, or out of memory:
+ * the caller then takes a path that needs none) */
+static void *handle_scratch(struct tb200_handle *h, size_t bytes) {
+  enum cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  int slot = -1;
+  for (int i = 0; i < TB200_WS_SLOTS; i++)
+    if (h->ws[i].ptr && h->ws[i].stream == h->stream) {
+      slot = i;
+      break;
+    }
+  if (slot >= 0 && h->ws[slot].bytes >= bytes) return h->ws[slot].ptr;
+  if (cudaStreamIsCapturing(h->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return NULL;
+  if (slot < 0) {
+    for (int i = 0; i < TB200_WS_SLOTS && slot < 0; i++)
+      if (!h->ws[i].ptr) slot = i;
+    if (slot < 0) { /* all slots taken by other streams: retire the first after its stream drains */
+      slot = 0;
+      cudaStreamSynchronize(h->ws[0].stream);
+    }
+  }
+  if (h->ws[slot].ptr) {
+    cudaStreamSynchronize(h->ws[slot].stream); /* growth: earlier launches on this stream may still read it */
+    cudaFree(h->ws[slot].ptr);
+    h->ws[slot].ptr = NULL;
+    h->ws[slot].bytes = 0;
+  }
+  size_t want = bytes < (64u << 10) ? (64u << 10) : bytes;
+  void *p = NULL;
+  if (cudaMalloc(&p, want) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return NULL;
+  }
+  h->ws[slot].stream = h->stream;
+  h->ws[slot].ptr = p;
+  h->ws[slot].bytes = want;
+  h->ws_allocs++;
+  return p;
+}
 
 /* ---- environment knobs, read once (the reference's TINYCUBLAS_TC / TINYCUBLAS_GEMM bisect knobs,
  * cublas.c:79-81, under this library's own names) ---- */
@@ -171,7 +222,7 @@ int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_ty
   /* TF32 only with both operands K-major: an MN-major 32-bit operand needs the 128B swizzle with 32-byte
    * atoms (a layout this kernel does not stage); those GEMMs stay exact fp32 on the SIMT kernel */
   int tf32_ok = in_type == TB200_F32 && tf32 && transa == 1 && transb == 0;
-  if ((sixteen || tf32_ok) && aligned && !ptr_array) {
+  if ((sixteen || tf32_ok) && aligned) { /* pointer arrays included: per-element tensor maps on the device */
     int pr = 0;
     int bn = tb200_tc_tile_n(m, n, batch, num_sms, &pr);
     if (tile_n) *tile_n = bn;
@@ -226,7 +277,15 @@ static cublasStatus_t run_gemm(struct tb200_handle *h, tb200_gemm_t *g) {
   switch (kind) {
     case TB200_KERNEL_NONE: return CUBLAS_STATUS_SUCCESS;
     case TB200_KERNEL_SKINNY: rc = tb200_launch_skinny(g, h->stream); break;
-    case TB200_KERNEL_TC: rc = tb200_launch_tc(g, tile_n, pair, sms, h->stream); break;
+    case TB200_KERNEL_TC:
+      if (ptr_array) {
+        void *ws = handle_scratch(h, tb200_tc_ptr_ws_bytes(g->batch));
+        rc = ws ? tb200_launch_tc_ptr(g, tile_n, pair, sms, ws, h->stream) : (int)cudaErrorNotSupported;
+        if (rc == (int)cudaErrorNotSupported) rc = tb200_launch_simt(g, h->stream); /* no scratch: general kernel */
+      } else {
+        rc = tb200_launch_tc(g, tile_n, pair, sms, h->stream);
+      }
+      break;
     default: rc = tb200_launch_simt(g, h->stream); break;
   }
   if (rc != 0) {
@@ -296,8 +355,20 @@ cublasStatus_t cublasCreate_v2(cublasHandle_t *handle) {
 }
 
 cublasStatus_t cublasDestroy_v2(cublasHandle_t handle) {
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  if (h) {
+    for (int i = 0; i < TB200_WS_SLOTS; i++)
+      if (h->ws[i].ptr) {
+        cudaStreamSynchronize(h->ws[i].stream);
+        cudaFree(h->ws[i].ptr);
+      }
+  }
   free(handle);
   return CUBLAS_STATUS_SUCCESS;
+}
+
+unsigned tb200_scratch_allocs(cublasHandle_t handle) {
+  return handle ? ((struct tb200_handle *)handle)->ws_allocs : 0u;
 }
 
 cublasStatus_t cublasSetStream_v2(cublasHandle_t handle, cudaStream_t stream) {

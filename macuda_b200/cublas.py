@@ -88,6 +88,7 @@ EXTENSIONS = [
     ("tb200_ipc_open", _i, [_vp, ctypes.POINTER(_vp)]),
     ("tb200_ipc_close", _i, [_vp]),
     ("tb200_ipc_free", _i, [_vp]),
+    ("tb200_scratch_allocs", ctypes.c_uint, [_vp]),
 ]
 
 

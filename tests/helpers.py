@@ -42,7 +42,7 @@ def sample_idx(rng, size: int, cap: int):
 
 def run_and_check(lib, h, *, opA=1, opB=0, m, n, k, in_t=O.F16, out_t=O.F32, alpha=1.0, beta=0.0, batch=1,
                   lda=None, ldb=None, ldc=None, sA=None, sB=None, sC=None, mode="strided", seed=0,
-                  compute=cb.CUBLAS_COMPUTE_32F, a_sigma=0.02, sample=256, c_offset=0, broadcast_a=1):
+                  compute=cb.CUBLAS_COMPUTE_32F, a_sigma=0.02, sample=256, c_offset=0, broadcast_a=1, a_ptr_shift=0):
     """Build seeded operands, run one GEMM through the library's C ABI, check it against the oracle.
     mode: 'ex' (cublasGemmEx, batch 1), 'strided' (cublasGemmStridedBatchedEx), 'ptr' (cublasGemmBatchedEx,
     A pointers repeated `broadcast_a` times, as for GQA). Returns the check dict (plus the status)."""
@@ -57,7 +57,7 @@ def run_and_check(lib, h, *, opA=1, opB=0, m, n, k, in_t=O.F16, out_t=O.F32, alp
     sB = sB if sB is not None else ldb * b_cols
     sC = sC if sC is not None else ldc * n
     nA = batch if mode != "ptr" else (batch + broadcast_a - 1) // broadcast_a
-    A = storage(rng, max(1, sA * (nA - 1) + lda * a_cols), in_t, a_sigma)
+    A = storage(rng, max(1, sA * (nA - 1) + lda * a_cols + a_ptr_shift), in_t, a_sigma)
     B = storage(rng, max(1, sB * (batch - 1) + ldb * b_cols), in_t, 1.0)
     C0 = storage(rng, sC * (batch - 1) + ldc * n + c_offset, out_t, 1.0)
     dA, dB, dC = dev(A), dev(B), dev(C0)
@@ -73,7 +73,9 @@ def run_and_check(lib, h, *, opA=1, opB=0, m, n, k, in_t=O.F16, out_t=O.F32, alp
         st = h.gemm_strided_batched_ex(opA, opB, m, n, k, alpha, dA.data_ptr(), ct_in, lda, sA, dB.data_ptr(), ct_in,
                                        ldb, sB, beta, cbase, ct_out, ldc, sC, batch, compute)
     else:
-        a_ptrs = [dA.data_ptr() + (b // broadcast_a) * sA * esA for b in range(batch)]
+        # a_ptr_shift: odd batch elements' A starts that many elements later (breaks 16-byte alignment)
+        a_off = [(b // broadcast_a) * sA + (a_ptr_shift if b % 2 else 0) for b in range(batch)]
+        a_ptrs = [dA.data_ptr() + o * esA for o in a_off]
         b_ptrs = [dB.data_ptr() + b * sB * esA for b in range(batch)]
         c_ptrs = [cbase + b * sC * esC for b in range(batch)]
         tA, tB, tC = ptr_table(a_ptrs), ptr_table(b_ptrs), ptr_table(c_ptrs)
@@ -87,7 +89,7 @@ def run_and_check(lib, h, *, opA=1, opB=0, m, n, k, in_t=O.F16, out_t=O.F32, alp
     cols = sample_idx(rng, n, sample)
     C0v = C0[c_offset:]
     if mode == "ptr":
-        A_list = [A[(b // broadcast_a) * sA:(b // broadcast_a) * sA + lda * a_cols] for b in range(batch)]
+        A_list = [A[o:o + lda * a_cols] for o in a_off]
         B_list = [B[b * sB:b * sB + ldb * b_cols] for b in range(batch)]
         C_list = [C0v[b * sC:b * sC + ldc * n] for b in range(batch)]
         R, S = O.gemm(opA, opB, m, n, k, alpha, None, in_t, lda, None, in_t, ldb, beta, None, out_t, ldc, batch=batch,

@@ -148,7 +148,8 @@ PLAN_ROWS = [
     ("fp32 without TF32 math stays fp32", (0, 0, 512, 512, 512, 1, 0, 0, 0, 1), (cb.TB200_KERNEL_SIMT, 0)),
     ("fp32 with TF32 math takes the tensor cores", (1, 0, 512, 512, 512, 1, 0, 1, 0, 1), (cb.TB200_KERNEL_TC, 32)),
     ("TF32 with an MN-major operand stays fp32", (0, 0, 512, 512, 512, 1, 0, 1, 0, 1), (cb.TB200_KERNEL_SIMT, 0)),
-    ("pointer arrays, n=32: SIMT for now", (1, 0, 768, 32, 2048, 128, 1, 0, 1, 1), (cb.TB200_KERNEL_SIMT, 0)),
+    ("pointer arrays, n=32 (MoE experts): tensor cores", (1, 0, 768, 32, 2048, 128, 1, 0, 1, 1), (cb.TB200_KERNEL_TC, 32)),
+    ("pointer arrays, unaligned ld: SIMT", (1, 0, 768, 32, 2048, 128, 1, 0, 1, 0), (cb.TB200_KERNEL_SIMT, 0)),
     ("pointer arrays, n<=8: skinny", (1, 0, 768, 8, 2048, 128, 1, 0, 1, 1), (cb.TB200_KERNEL_SKINNY, 0)),
     ("k == 0 is a scale of C", (1, 0, 64, 64, 0, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_SIMT, 0)),
     ("empty", (1, 0, 0, 64, 64, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_NONE, 0)),

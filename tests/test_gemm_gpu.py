@@ -132,6 +132,45 @@ def test_skinny_pointer_arrays_gqa(lib, h):
     assert_ok(run_and_check(lib, h, m=768, n=8, k=2048, batch=8, mode="ptr", broadcast_a=4, seed=60), "ptr n=8")
 
 
+@pytest.mark.parametrize("bn", [None, "64", "pair"])
+def test_pointer_arrays_tensor_cores(lib, h, monkeypatch, bn):
+    """cublasGemmBatchedEx on the tensor cores: per-element tensor maps built on the device."""
+    if bn:
+        monkeypatch.setenv("TB200_TC_BN", bn)
+    assert lib.plan(1, 0, 768, 32, 2048, 16, 1, 0, 0, 1, 1, 148)[0] == cb.TB200_KERNEL_TC
+    assert_ok(run_and_check(lib, h, m=768, n=32, k=2048, batch=16, mode="ptr", seed=63), "MoE experts")
+    assert_ok(run_and_check(lib, h, m=512, n=256, k=128, batch=8, mode="ptr", broadcast_a=4, seed=64), "GQA KQ")
+    assert_ok(run_and_check(lib, h, opA=0, m=128, n=256, k=512, batch=8, mode="ptr", broadcast_a=4, seed=65),
+              "GQA KQV (MN-major A)")
+    assert_ok(run_and_check(lib, h, m=300, n=200, k=136, batch=5, mode="ptr", in_t=O.BF16, out_t=O.BF16, alpha=0.5,
+                            beta=-1.0, seed=66), "bf16 out, alpha/beta, tails")
+
+
+def test_pointer_arrays_misaligned_element_falls_back(lib, h):
+    """An element pointer off 16-byte alignment cannot feed TMA: the tensor-core launch stands down on the
+    device and the general kernel queued behind it computes the batch - no host sync, same result."""
+    assert_ok(run_and_check(lib, h, m=256, n=64, k=256, batch=4, mode="ptr", a_ptr_shift=2, seed=67),
+              "A pointers of odd elements shifted by 4 bytes")
+    assert_ok(run_and_check(lib, h, m=256, n=64, k=256, batch=4, mode="ptr", seed=68), "aligned again")
+
+
+def test_pointer_array_scratch_is_per_stream(lib):
+    import torch
+    with lib.handle() as hh:
+        run_and_check(lib, hh, m=256, n=64, k=256, batch=4, mode="ptr", seed=69)
+        run_and_check(lib, hh, m=256, n=64, k=256, batch=3, mode="ptr", seed=70)
+        assert lib.lib.tb200_scratch_allocs(hh.h) == 1
+        s2 = torch.cuda.Stream()
+        hh.set_stream(s2.cuda_stream)
+        with torch.cuda.stream(s2):
+            res = run_and_check(lib, hh, m=256, n=64, k=256, batch=4, mode="ptr", seed=71)
+        assert res["ok"], res
+        assert lib.lib.tb200_scratch_allocs(hh.h) == 2
+    with lib.handle() as hh:  # strided GEMMs never allocate
+        run_and_check(lib, hh, m=512, n=256, k=256, batch=3, seed=72)
+        assert lib.lib.tb200_scratch_allocs(hh.h) == 0
+
+
 def test_pointer_arrays_general(lib, h):
     assert_ok(run_and_check(lib, h, m=768, n=32, k=512, batch=6, mode="ptr", seed=61), "ptr n=32")
     assert_ok(run_and_check(lib, h, opA=0, m=128, n=64, k=256, batch=4, mode="ptr", broadcast_a=2, seed=62), "GQA")
@@ -303,6 +342,43 @@ def test_graph_capture_replays(lib):
     R[:, :4, :] += R4
     got = O.extract(dC.cpu().numpy(), O.F32, m, n, m)
     assert_ok(O.check(got, R, 2 * S, O.F32), "graph replay")
+    del g
+    hh.close()
+
+
+def test_graph_capture_pointer_arrays(lib):
+    """After the first call on a stream made its scratch, pointer-array GEMMs capture and replay."""
+    import torch
+    from tests.helpers import storage as st_
+    rng = np.random.default_rng(131)
+    m, n, k, batch = 256, 64, 512, 6
+    A = st_(rng, m * k * batch, O.F16, 0.02)
+    B = st_(rng, k * n * batch, O.F16)
+    dA, dB = dev(A), dev(B)
+    dC = torch.zeros(m * n * batch, device="cuda")
+    tA = ptr_table([dA.data_ptr() + b * m * k * 2 for b in range(batch)])
+    tB = ptr_table([dB.data_ptr() + b * k * n * 2 for b in range(batch)])
+    tC = ptr_table([dC.data_ptr() + b * m * n * 4 for b in range(batch)])
+    s = torch.cuda.Stream()
+    hh = lib.handle()
+    hh.set_stream(s.cuda_stream)
+
+    def issue():
+        assert hh.gemm_batched_ex(1, 0, m, n, k, 1.0, tA.data_ptr(), cb.CUDA_R_16F, k, tB.data_ptr(), cb.CUDA_R_16F, k,
+                                  0.0, tC.data_ptr(), cb.CUDA_R_32F, m, batch) == 0
+
+    with torch.cuda.stream(s):
+        issue()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        issue()
+    dC.fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize()
+    R, S = O.gemm(1, 0, m, n, k, 1.0, A, O.F16, k, B, O.F16, k, sA=m * k, sB=k * n, batch=batch)
+    got = O.extract(dC.cpu().numpy(), O.F32, m, n, m, sC=m * n, batch=batch)
+    assert_ok(O.check(got, R, S, O.F32), "pointer-array graph replay")
     del g
     hh.close()
 
