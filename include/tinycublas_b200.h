@@ -125,6 +125,33 @@ int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_ty
  * Pure function, pinned by host-only tests. */
 int tb200_tc_tile_n(int m, int n, int batch, int num_sms, int *pair);
 
+/* cublasGemmBatchedEx for callers that cannot let a library allocate device memory. No counterpart in the
+ * reference (its pointer-array path copies the arrays to the host instead).
+ *
+ * Who needs it: code that must not call cudaMalloc while it runs - a stream capture in global capture
+ * mode, where cudaMalloc is not permitted; a server that has given all device memory to its own
+ * allocator up front, where a library's cudaMalloc fails or fragments it; a latency-critical loop that
+ * cannot afford the implicit synchronisation cudaMalloc and cudaFree bring. cublasGemmBatchedEx itself
+ * allocates device scratch once per (handle, stream) for pointer arrays on the tensor cores.
+ *
+ * Same arguments and results as cublasGemmBatchedEx; it allocates nothing. Where device scratch is
+ * needed it uses one fixed array inside the library (256 KB + 256 B, held by every GPU that loads the
+ * library until the process exits), so batchCount is limited to tb200_noalloc_max_batch() (1024):
+ * larger batches return CUBLAS_STATUS_INVALID_VALUE with a message on stderr.
+ * The first call on a device looks up that array's device address (cudaGetSymbolAddress): make it
+ * before any stream capture. All calls share the array and it keeps the last call's contents (each call
+ * rewrites what it uses): calls whose launches overlap on the GPU - on different streams, or from
+ * different threads - race on it; serialise them. */
+cublasStatus_t tb200_gemm_batched_ex_noalloc(cublasHandle_t handle, cublasOperation_t transa,
+                                             cublasOperation_t transb, int m, int n, int k, const void *alpha,
+                                             const void *const Aarray[], cudaDataType Atype, int lda,
+                                             const void *const Barray[], cudaDataType Btype, int ldb,
+                                             const void *beta, void *const Carray[], cudaDataType Ctype, int ldc,
+                                             int batchCount, cublasComputeType_t computeType);
+
+/* The largest batchCount tb200_gemm_batched_ex_noalloc accepts. */
+int tb200_noalloc_max_batch(void);
+
 /* Device scratch allocations this handle has made so far (test hook, the counterpart of the reference's
  * tinycublas_splitk_ws_allocs, cublas.c:91-92). The library allocates scratch only for pointer-array
  * batches on the tensor cores: one buffer per (handle, stream), made at the first such call on that

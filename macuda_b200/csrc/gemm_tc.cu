@@ -655,3 +655,46 @@ extern "C" __attribute__((visibility("default"))) int tb200_device_error(void) {
   cudaMemcpyToSymbol(g_tb200_err, &zero, sizeof zero);
   return v;
 }
+
+// ---------------------------------------------------------------------------------------------------
+// Allocation-free variant of the pointer-array launch.
+//
+// The pointer-array path needs device scratch for one pair of tensor maps per batch element (plus a flag).
+// tb200_gemm_batched_ex_noalloc serves callers that must not have the library call cudaMalloc: their
+// scratch is this fixed array, part of the library's device image, so every GPU that loads the library
+// holds its 256 KB + 256 B until the process exits. It bounds the batch at TB200_NOALLOC_MAX_BATCH.
+// All calls, on every stream, share it and it keeps the last call's contents: the flag that must start
+// at zero is cleared by each call (an asynchronous memset on the call's stream), the maps are rewritten
+// for every element, and calls whose launches overlap on the GPU race on it.
+#define TB200_NOALLOC_MAX_BATCH 1024
+static __device__ __align__(256) unsigned char g_tb200_noalloc_scratch[256 + TB200_NOALLOC_MAX_BATCH * 256];
+
+// The host-side name g_tb200_noalloc_scratch is only a stand-in for the symbol, never a device address:
+// the device address comes from cudaGetSymbolAddress, looked up once per device with that device current.
+static void *noalloc_scratch(void) {
+  static void *addr[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!addr[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_tb200_noalloc_scratch);
+    if (e != cudaSuccess || !p) {
+      fprintf(stderr, "[tinycublas_b200] cudaGetSymbolAddress(scratch) failed on device %d: %s\n", dev,
+              cudaGetErrorString(e));
+      (void)cudaGetLastError();
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+extern "C" __attribute__((visibility("default"))) int tb200_noalloc_max_batch(void) { return TB200_NOALLOC_MAX_BATCH; }
+
+extern "C" int tb200_launch_tc_ptr_noalloc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s) {
+  if (g->batch > TB200_NOALLOC_MAX_BATCH || tb200_tc_ptr_ws_bytes(g->batch) > sizeof(g_tb200_noalloc_scratch))
+    return (int)cudaErrorInvalidValue;
+  void *ws = noalloc_scratch();
+  if (!ws) return (int)cudaErrorInvalidSymbol;
+  return tb200_launch_tc_ptr(g, tile_n, pair, num_sms, ws, s);
+}

@@ -43,6 +43,9 @@ int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cu
  * bytes owned by the caller for the duration of the launch */
 size_t tb200_tc_ptr_ws_bytes(int batch);
 int tb200_launch_tc_ptr(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, void *ws, cudaStream_t s);
+/* the same with the library's fixed device scratch instead of caller-provided scratch (no allocation) */
+int tb200_noalloc_max_batch(void);
+int tb200_launch_tc_ptr_noalloc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s);
 int tb200_launch_trsm_rupn(const float *const *A, float *const *B, int rows, int n, int lda, int ldb, float alpha,
                            int batch, cudaStream_t s);
 

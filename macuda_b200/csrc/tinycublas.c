@@ -516,4 +516,65 @@ cublasStatus_t tb200_gemm_ex_allgather(cublasHandle_t handle, cublasOperation_t 
   return rc == 0 ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
 }
 
+/* cublasGemmBatchedEx without any device allocation: same arguments, same results; where the pointer-array
+ * tensor-core path needs scratch it takes the library's fixed device array (tb200_launch_tc_ptr_noalloc)
+ * instead of the handle's lazily allocated buffer. batchCount is bounded by that array. */
+cublasStatus_t tb200_gemm_batched_ex_noalloc(cublasHandle_t handle, cublasOperation_t transa,
+                                             cublasOperation_t transb, int m, int n, int k, const void *alpha,
+                                             const void *const Aarray[], cudaDataType Atype, int lda,
+                                             const void *const Barray[], cudaDataType Btype, int ldb,
+                                             const void *beta, void *const Carray[], cudaDataType Ctype, int ldc,
+                                             int batchCount, cublasComputeType_t ct) {
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (batchCount > tb200_noalloc_max_batch()) {
+    fprintf(stderr,
+            "[tinycublas_b200] tb200_gemm_batched_ex_noalloc: batchCount %d exceeds the %d its fixed scratch holds\n",
+            batchCount, tb200_noalloc_max_batch());
+    return CUBLAS_STATUS_INVALID_VALUE;
+  }
+  tb200_gemm_t g;
+  memset(&g, 0, sizeof g);
+  int tf32 = 0;
+  if (gemm_contract(Atype, Btype, Ctype, ct, &g.in_type, &g.out_type, &tf32)) return CUBLAS_STATUS_NOT_SUPPORTED;
+  g.opA = op_code(transa);
+  g.opB = op_code(transb);
+  cublasStatus_t st = check_args(g.opA, g.opB, m, n, k, lda, ldb, ldc, batchCount);
+  if (st != CUBLAS_STATUS_SUCCESS) return st;
+  if (!alpha || !beta) return CUBLAS_STATUS_INVALID_VALUE;
+  if (m == 0 || n == 0 || batchCount == 0) return CUBLAS_STATUS_SUCCESS;
+  if (!Aarray || !Barray || !Carray) return CUBLAS_STATUS_INVALID_VALUE;
+  if (g.in_type == TB200_F32)
+    g.tf32 = tf32 || (((int)h->math_mode & 0xf) == CUBLAS_TF32_TENSOR_OP_MATH && ct == CUBLAS_COMPUTE_32F);
+  g.m = m;
+  g.n = n;
+  g.k = k;
+  g.batch = batchCount;
+  g.alpha = read_scalar(alpha, ct);
+  g.beta = read_scalar(beta, ct);
+  g.Aarr = Aarray; g.lda = lda;
+  g.Barr = Barray; g.ldb = ldb;
+  g.Carr = Carray; g.ldc = ldc;
+  int tile_n = 0, pair = 0;
+  int sms = tb200_num_sms();
+  int kind = tb200_plan(g.opA, g.opB, m, n, k, batchCount, g.in_type, g.out_type, g.tf32, 1, operands_aligned(&g),
+                        sms, &tile_n, &pair);
+  if (tb200_trace())
+    fprintf(stderr, "[trace] gemm-noalloc %s m=%d n=%d k=%d batch=%d BN=%d pair=%d\n", kernel_name(kind), m, n, k,
+            batchCount, tile_n, pair);
+  int rc = 0;
+  if (kind == TB200_KERNEL_NONE) return CUBLAS_STATUS_SUCCESS;
+  if (kind == TB200_KERNEL_SKINNY) rc = tb200_launch_skinny(&g, h->stream); /* no scratch */
+  else if (kind == TB200_KERNEL_TC) {
+    rc = tb200_launch_tc_ptr_noalloc(&g, tile_n, pair, sms, h->stream);
+    if (rc == (int)cudaErrorNotSupported) rc = tb200_launch_simt(&g, h->stream);
+  } else rc = tb200_launch_simt(&g, h->stream);
+  if (rc != 0) {
+    fprintf(stderr, "[tinycublas_b200] tb200_gemm_batched_ex_noalloc launch failed: %s\n",
+            cudaGetErrorString((cudaError_t)rc));
+    return CUBLAS_STATUS_EXECUTION_FAILED;
+  }
+  return CUBLAS_STATUS_SUCCESS;
+}
+
 const char *tb200_version(void) { return "tinycublas_b200 " TB200_GIT_DESCRIBE " sm_100a"; }

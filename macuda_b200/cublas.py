@@ -89,6 +89,9 @@ EXTENSIONS = [
     ("tb200_ipc_close", _i, [_vp]),
     ("tb200_ipc_free", _i, [_vp]),
     ("tb200_scratch_allocs", ctypes.c_uint, [_vp]),
+    ("tb200_gemm_batched_ex_noalloc", _i,
+     [_vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp, _i, _i, _vp, _vp, _i, _i, _i, _i]),
+    ("tb200_noalloc_max_batch", _i, []),
 ]
 
 
