@@ -8,8 +8,9 @@
  * Differences from the reference's host layer (cuda-shim/libtinycublas/cublas.c), by design:
  *   - pointer-array batches are read on the device (reference: device-to-host copy + stream sync +
  *     one launch per element, cublas.c:292-303);
- *   - nothing here allocates device memory or synchronises, so every call is graph-capturable
- *     (the reference's split-K path bypassed capture, cublas.c:170);
+ *   - no call synchronises the stream or reads device memory back, so every call is graph-capturable
+ *     (the reference's split-K path bypassed capture, cublas.c:170); the one device allocation, the
+ *     tensor maps of pointer-array batches, is made once per (handle, stream) outside any capture;
  *   - cublasSetMathMode is honoured for fp32 GEMMs (the reference stored it and always used TF32,
  *     cublas.c:218, :249);
  *   - the kernel plan reads the device's SM count (the reference hard-codes the RTX 5090's 170,
