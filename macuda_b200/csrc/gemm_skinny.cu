@@ -63,6 +63,10 @@ __device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t 
 template <typename T>
 __global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gemm_t g, int z0) {
   __shared__ float red[SK_WARPS][SK_ROWS][8];
+  // launched with programmatic stream serialization: wait for the kernel before this one in the stream to
+  // complete before touching memory, then let the next one be scheduled on SMs this grid leaves free
+  griddep_wait();
+  griddep_launch_dependents();
   const int b = blockIdx.y + z0;
   const T *A = g.Aarr ? (const T *)g.Aarr[b] : (const T *)g.A + (long long)b * g.sA;
   const T *B = g.Barr ? (const T *)g.Barr[b] : (const T *)g.B + (long long)b * g.sB;
@@ -172,10 +176,17 @@ extern "C" int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s) {
     if (tb200_trace())
       fprintf(stderr, "[trace] launch tb200_gemm_skinny grid=(%lld,%u,1) block=(%d,1,1) m=%d n=%d k=%d out=%d\n", gx, gy,
               SK_T, g->m, g->n, g->k, g->out_type);
-    dim3 grid((unsigned)gx, gy, 1);
-    if (g->in_type == TB200_F16) tb200_gemm_skinny_kernel<__half><<<grid, SK_T, 0, s>>>(*g, z0);
-    else tb200_gemm_skinny_kernel<__nv_bfloat16><<<grid, SK_T, 0, s>>>(*g, z0);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.gridDim = dim3((unsigned)gx, gy, 1);
+    cfg.blockDim = dim3(SK_T, 1, 1);
+    cfg.stream = s;
+    cfg.attrs = at;
+    cfg.numAttrs = tb200_pdl() ? 1 : 0;
+    cudaError_t e = g->in_type == TB200_F16 ? cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_kernel<__half>, *g, z0)
+                                            : cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_kernel<__nv_bfloat16>, *g, z0);
     if (e != cudaSuccess) return (int)e;
   }
   return 0;

@@ -150,7 +150,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
 
   // uniform early exit, before any barrier or TMEM allocation: every thread of every CTA reads the same flag
-  if (p.skip && *(volatile const int *)p.skip != 0) return;
+  // (written by the kernel before this one, so read only once that kernel has completed)
+  if (p.skip) {
+    griddep_wait();
+    if (*(volatile const int *)p.skip != 0) return;
+  }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
@@ -188,6 +192,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if (CG == 2) cluster_sync();  // the peer's loads and arrivals target the even CTA's barriers: all initialised
   else __syncthreads();
   tc_fence_after();
+  // Everything above touched only this CTA's own resources and the kernel parameters, and may overlap the
+  // end of the kernel before this one in the stream. From here on operands and C are read and written:
+  // wait for that kernel to complete. Then let the next kernel set up on the SMs this one leaves free.
+  griddep_wait();
+  griddep_launch_dependents();
   const uint32_t tmem_base = *tmem_slot;
   // shared::cluster addresses of the even CTA's barriers (CG == 2)
   const uint32_t lead_full0 = CG == 2 ? mapa_shared(smem_u32(full), 0) : 0u;
@@ -486,22 +495,30 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, i
             "[trace] launch tb200_gemm_tc<%s,BN=%d,KC=%d,CG=%d> grid=(%u,1,1) block=(%d,1,1) smem=%d stages=%d m=%d n=%d "
             "k=%d batch=%d\n",
             KIND ? "tf32" : "f16", BN, KC, CG, grid, TC_THREADS, Cfg::SMEM_BYTES, Cfg::STAGES, p.m, p.n, p.k, p.batch);
-  if (CG == 1) {
-    kern<<<grid, TC_THREADS, Cfg::SMEM_BYTES, s>>>(ta, tb, p);
-    return (int)cudaGetLastError();
-  }
+  // Programmatic stream serialization: this grid may be scheduled while the kernel before it in the stream
+  // finishes (the kernel waits for it with griddep_wait before touching memory), which hides the launch and
+  // the set-up of barriers and tensor memory behind that kernel's last tiles.
   cudaLaunchConfig_t cfg = {};
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = 2;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
+  cudaLaunchAttribute at[2];
+  int na = 0;
+  if (CG == 2) {
+    at[na].id = cudaLaunchAttributeClusterDimension;
+    at[na].val.clusterDim.x = 2;
+    at[na].val.clusterDim.y = 1;
+    at[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  if (tb200_pdl()) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
   cfg.gridDim = dim3(grid, 1, 1);
   cfg.blockDim = dim3(TC_THREADS, 1, 1);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = s;
   cfg.attrs = at;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = na;
   return (int)cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
 }
 

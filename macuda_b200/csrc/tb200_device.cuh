@@ -95,6 +95,17 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// ---- programmatic dependent launch ------------------------------------------------------------------
+// Blocks until the grids this one depends on (the kernel before it in the stream, when it was launched with
+// programmatic stream serialization) have completed and their memory operations are visible. Returns at
+// once when there is no such dependency.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the grid launched after this one in the stream be scheduled before this one completes: its CTAs set
+// up on SMs this grid leaves free, and wait (griddep_wait) before they touch memory.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---- TMA -----------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_t *bar, int c0, int c1) {
   asm volatile(

@@ -57,6 +57,8 @@ int tb200_skinny_ok(const tb200_gemm_t *g);
 int tb200_tc_ok(const tb200_gemm_t *g);
 
 int tb200_trace(void);
+/* launch the kernels with programmatic stream serialization (TB200_PDL=0 turns it off) */
+int tb200_pdl(void);
 
 #ifdef __cplusplus
 }

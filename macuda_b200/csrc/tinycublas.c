@@ -100,6 +100,9 @@ int tb200_trace(void) {
   if (v < 0) v = env_flag("TB200_TRACE", 0);
   return v;
 }
+int tb200_pdl(void) { /* TB200_PDL=0: plain stream order between launches (bisect knob, read per launch) */
+  return env_flag("TB200_PDL", 1);
+}
 static int tc_enabled(void) {     /* TB200_TC=0: no tensor-core kernel, everything on the SIMT kernel */
   static int v = -1;
   if (v < 0) v = env_flag("TB200_TC", 1);

@@ -278,6 +278,41 @@ def test_deterministic(lib, h):
         assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
 
 
+def test_dependent_chain_in_one_stream(lib, h):
+    """Each GEMM reads the previous one's output, issued back to back on one stream with no host sync:
+    kernels are launched with programmatic stream serialization, so a kernel may be scheduled before the
+    one it depends on has finished and must wait (griddepcontrol.wait) before reading. Outputs start as
+    NaN, so a read too early shows up as a non-finite value or a mismatch. Links: tensor-core chain, then
+    decode links skinny (T,N, n=8) -> tensor core (N,N, n=8) -> skinny. Every link is checked against the
+    oracle computed from the previous link's actual device output."""
+    import torch
+    rng = np.random.default_rng(140)
+    n_tc, n_dec = 256, 8
+    # (opA, m, k, n): op T weights are stored k x m, op N weights m x k; the input is the previous output
+    links = [(1, 2048, 4096, n_tc), (1, 4096, 2048, n_tc), (1, 1024, 4096, n_tc),
+             (1, 4096, 1024, n_dec), (0, 2048, 4096, n_dec), (1, 4096, 2048, n_dec)]
+    assert lib.plan(1, 0, 4096, n_dec, 1024)[0] == cb.TB200_KERNEL_SKINNY
+    assert lib.plan(0, 0, 2048, n_dec, 4096)[0] == cb.TB200_KERNEL_TC
+    x_tc = storage(rng, 4096 * n_tc, O.F16)
+    x_dec = storage(rng, 1024 * n_dec, O.F16)
+    W = [storage(rng, m * k, O.F16, 0.02) for (_, m, k, _) in links]
+    dW = [dev(w) for w in W]
+    outs = [torch.full((m * n,), float("nan"), dtype=torch.float16, device="cuda") for (_, m, _, n) in links]
+    src = [dev(x_tc)] + outs[:2] + [dev(x_dec)] + outs[3:5]
+    for i, (opA, m, k, n) in enumerate(links):
+        lda = k if opA == 1 else m
+        assert h.gemm_ex(opA, 0, m, n, k, 1.0, dW[i].data_ptr(), cb.CUDA_R_16F, lda, src[i].data_ptr(), cb.CUDA_R_16F,
+                         k, 0.0, outs[i].data_ptr(), cb.CUDA_R_16F, m) == 0
+    torch.cuda.synchronize()
+    inputs = [x_tc] + [host(o, x_tc) for o in outs[:2]] + [x_dec] + [host(o, x_tc) for o in outs[3:5]]
+    for i, (opA, m, k, n) in enumerate(links):
+        lda = k if opA == 1 else m
+        rows = np.arange(0, m, 5, dtype=np.int32)
+        R, S = O.gemm(opA, 0, m, n, k, 1.0, W[i], O.F16, lda, inputs[i], O.F16, k, 0.0, None, O.F16, m, rows=rows)
+        got = O.extract(host(outs[i], x_tc), O.F16, m, n, m, rows=rows)
+        assert_ok(O.check(got, R, S, O.F16), f"link {i}")
+
+
 def test_two_streams_no_shared_state(lib):
     """The reference's BURST arm (splitk-20260923/test_splitk.cu:153-175) with two streams fails 8/8 because
     its split-K workspace is per handle. Here: 8 decode GEMMs and 8 prefill GEMMs on two streams and two
