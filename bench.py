@@ -19,7 +19,8 @@ instead. Total work is fixed, so scaling is "strong".
 Keys beyond the base contract: roofline (dominant kernel = the lm_head GEMM), cpu_baseline (the
 oracle's multithreaded fp16 GEMM on the host, a stand-in for ggml-cpu), e2e (the same step through the
 public API with host buffers: H2D of the step's activations and D2H of the last token's logits), per
-projection figures, and decode (n <= 8) HBM bandwidth figures.
+projection figures, decode (n <= 8) HBM bandwidth figures (config 4), and configs 3 and 5 figures
+(attention batched GEMMs, MoE pointer-array GEMMs, squares).
 
 --impl reference runs the same step through the reference's own libtinycublas (its cublas.c and gemm.cu,
 compiled from source for sm_100a by oracle/build_ref.sh): the reference's implementation of this path
@@ -205,6 +206,118 @@ def decode_figures(torch, lib, cb, dtype_code, dtype):
             byts = m * k * 2 + n * k * 2 + m * n * 4
             out[f"{m}x{k}_n{n}"] = {"us": round(us, 2), "GB/s": round(byts / us / 1e3, 1)}
         del ws
+    h.close()
+    return out
+
+
+def config_figures(torch, lib, cb, dtype_code, dtype):
+    """Configs 3 and 5: attention batched GEMMs (strided with the GQA heads folded into n, and pointer arrays
+    with each KV head's pointer repeated for its 4 query heads), MoE expert GEMMs (pointer arrays over 128
+    experts, 32 tokens each) and square GEMMs, all T,N with f32 C as ggml issues them. Per case: device
+    time (CUDA events around back-to-back calls, median of 3 repeats), TFLOP/s, compulsory bytes / time, and
+    the fraction of the measured peak of its bound (HBM copy bandwidth, or burst bf16 tensor throughput)."""
+    pk = peaks()
+    out = {}
+    h = lib.handle()
+    s = torch.cuda.current_stream()
+    h.set_stream(s.cuda_stream)
+    f32 = cb.CUDA_R_32F
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, device="cuda") * scale).to(dtype)
+
+    def table(ptrs):
+        return torch.tensor(ptrs, dtype=torch.int64, device="cuda")
+
+    def measure(name, call, reps, flop, byts, bound):
+        for _ in range(2):
+            st = call()
+            if st != 0:
+                out[name] = {"status": st}
+                return
+        torch.cuda.synchronize()
+        ts = []
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(s)
+            for _ in range(reps):
+                call()
+            e1.record(s)
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1) * 1e3 / reps)
+        us = statistics.median(ts)
+        tf, gbs = flop / us / 1e6, byts / us / 1e3
+        frac = gbs / pk["hbm_gbs"] if bound == "hbm" else tf / pk["bf16_tflops"]
+        out[name] = {"us": round(us, 2), "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "bound": bound,
+                     "frac_of_measured_peak": round(frac, 3)}
+
+    # config 3: 32 query heads / 8 KV heads, head_dim 128, 512 queries, 4096 keys
+    Hq, Hkv, D, Tq, Tk = 32, 8, 128, 512, 4096
+    g = Hq // Hkv
+    K = rnd(Hkv, Tk, D)          # per KV head: k = D x m = Tk (op T, lda = D)
+    Q = rnd(Hq, Tq, D)           # per query head: k = D x n = Tq (ldb = D); heads of a group are adjacent
+    V = rnd(Hkv, D, Tk)          # per KV head: k = Tk x m = D (op T, lda = Tk)
+    P = rnd(Hq, Tq, Tk)          # per query head: k = Tk x n = Tq (ldb = Tk)
+    Ckq = torch.empty(Hq * Tk * Tq, device="cuda")
+    Ckqv = torch.empty(Hq * D * Tq, device="cuda")
+    flop3 = 2.0 * Tk * Tq * D * Hq
+    b_kq = (K.numel() + Q.numel()) * 2 + Ckq.numel() * 4
+    b_kqv = (V.numel() + P.numel()) * 2 + Ckqv.numel() * 4
+    measure("c3_kq_strided_folded", lambda: h.gemm_strided_batched_ex(
+        1, 0, Tk, g * Tq, D, 1.0, K.data_ptr(), dtype_code, D, Tk * D, Q.data_ptr(), dtype_code, D, g * Tq * D, 0.0,
+        Ckq.data_ptr(), f32, Tk, Tk * g * Tq, Hkv), 10, flop3, b_kq, "hbm")
+    measure("c3_kqv_strided_folded", lambda: h.gemm_strided_batched_ex(
+        1, 0, D, g * Tq, Tk, 1.0, V.data_ptr(), dtype_code, Tk, D * Tk, P.data_ptr(), dtype_code, Tk, g * Tq * Tk, 0.0,
+        Ckqv.data_ptr(), f32, D, D * g * Tq, Hkv), 10, flop3, b_kqv, "hbm")
+    es = 2
+    kq_a = table([K.data_ptr() + (b // g) * Tk * D * es for b in range(Hq)])
+    kq_b = table([Q.data_ptr() + b * Tq * D * es for b in range(Hq)])
+    kq_c = table([Ckq.data_ptr() + b * Tk * Tq * 4 for b in range(Hq)])
+    kqv_a = table([V.data_ptr() + (b // g) * D * Tk * es for b in range(Hq)])
+    kqv_b = table([P.data_ptr() + b * Tq * Tk * es for b in range(Hq)])
+    kqv_c = table([Ckqv.data_ptr() + b * D * Tq * 4 for b in range(Hq)])
+    measure("c3_kq_pointer_gqa", lambda: h.gemm_batched_ex(
+        1, 0, Tk, Tq, D, 1.0, kq_a.data_ptr(), dtype_code, D, kq_b.data_ptr(), dtype_code, D, 0.0, kq_c.data_ptr(), f32,
+        Tk, Hq), 10, flop3, b_kq, "hbm")
+    measure("c3_kqv_pointer_gqa", lambda: h.gemm_batched_ex(
+        1, 0, D, Tq, Tk, 1.0, kqv_a.data_ptr(), dtype_code, Tk, kqv_b.data_ptr(), dtype_code, Tk, 0.0, kqv_c.data_ptr(),
+        f32, D, Hq), 10, flop3, b_kqv, "hbm")
+    del K, Q, V, P, Ckq, Ckqv
+
+    # config 5 MoE: 128 experts, hidden 2048, expert FFN 768, 32 tokens per expert (balanced top-8 routing)
+    E, Hd, Fe, Te = 128, 2048, 768, 32
+    Wgu = rnd(E, Fe, Hd, scale=0.02)   # per expert: k = Hd x m = Fe (op T, lda = Hd)
+    Wd = rnd(E, Hd, Fe, scale=0.02)    # per expert: k = Fe x m = Hd
+    Xe = rnd(E, Te, Hd)                # tokens gathered per expert: k = Hd x n = Te
+    He = rnd(E, Te, Fe)
+    Cgu = torch.empty(E * Fe * Te, device="cuda")
+    Cd = torch.empty(E * Hd * Te, device="cuda")
+    flop5 = 2.0 * Fe * Te * Hd * E
+    pa = table([Wgu.data_ptr() + e * Fe * Hd * es for e in range(E)])
+    pb = table([Xe.data_ptr() + e * Te * Hd * es for e in range(E)])
+    pc = table([Cgu.data_ptr() + e * Fe * Te * 4 for e in range(E)])
+    measure("c5_moe_gate_up_pointer", lambda: h.gemm_batched_ex(
+        1, 0, Fe, Te, Hd, 1.0, pa.data_ptr(), dtype_code, Hd, pb.data_ptr(), dtype_code, Hd, 0.0, pc.data_ptr(), f32,
+        Fe, E), 10, flop5, (Wgu.numel() + Xe.numel()) * 2 + Cgu.numel() * 4, "hbm")
+    pa = table([Wd.data_ptr() + e * Hd * Fe * es for e in range(E)])
+    pb = table([He.data_ptr() + e * Te * Fe * es for e in range(E)])
+    pc = table([Cd.data_ptr() + e * Hd * Te * 4 for e in range(E)])
+    measure("c5_moe_down_pointer", lambda: h.gemm_batched_ex(
+        1, 0, Hd, Te, Fe, 1.0, pa.data_ptr(), dtype_code, Fe, pb.data_ptr(), dtype_code, Fe, 0.0, pc.data_ptr(), f32,
+        Hd, E), 10, flop5, (Wd.numel() + He.numel()) * 2 + Cd.numel() * 4, "hbm")
+    del Wgu, Wd, Xe, He, Cgu, Cd
+
+    # config 5 squares, both 16-bit input types
+    for S in (4096, 8192, 16384):
+        for tname, tdt, tcode in (("f16", torch.float16, cb.CUDA_R_16F), ("bf16", torch.bfloat16, cb.CUDA_R_16BF)):
+            A = (torch.randn(S, S, device="cuda") * 0.02).to(tdt)
+            B = torch.randn(S, S, device="cuda").to(tdt)
+            C = torch.empty(S * S, device="cuda")
+            measure(f"c5_square_{S}_{tname}", lambda: h.gemm_ex(
+                1, 0, S, S, S, 1.0, A.data_ptr(), tcode, S, B.data_ptr(), tcode, S, 0.0, C.data_ptr(), f32, S,
+                cb.CUBLAS_COMPUTE_32F), 3 if S == 16384 else 10, 2.0 * S ** 3, 2 * S * S * 2 + S * S * 4, "tensor")
+            del A, B, C
+    torch.cuda.empty_cache()
     h.close()
     return out
 
@@ -472,6 +585,9 @@ def run(args):
     decode = None
     if rank == 0 and world == 1 and not args.no_decode:
         decode = decode_figures(torch, lib, cb, ctype, dtype)
+    configs = None
+    if rank == 0 and world == 1 and not args.no_configs:
+        configs = config_figures(torch, lib, cb, ctype, dtype)
 
     if fused:
         for g in sharded:
@@ -517,6 +633,8 @@ def run(args):
             line["clocks"] = clock_info
         if decode:
             line["decode"] = decode
+        if configs:
+            line["configs_3_5"] = configs
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -535,6 +653,7 @@ def main():
     ap.add_argument("--dtype", choices=["f16", "bf16"], default="f16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the config 3 and 5 figures")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--gemm", default=None, help="MxNxK: time one T,N GEMM alone (profiling)")
     ap.add_argument("--exchange", choices=["fused", "allgather"], default="fused",
