@@ -23,17 +23,13 @@ namespace {
 constexpr int SB_M = 64, SB_N = 64, SB_K = 16, SB_T = 256;
 
 template <typename TI>
-__global__ void __launch_bounds__(SB_T) tb200_gemm_simt_kernel(const tb200_gemm_t g, int z0) {
-  __shared__ float As[SB_K][SB_M + 4];
-  __shared__ float Bs[SB_K][SB_N + 4];
-  if (g.run_if && *(volatile const int *)g.run_if == 0) return;  // the tensor-core launch did the work
-  const int b = blockIdx.z + z0;
+__device__ __forceinline__ void simt_tile(const tb200_gemm_t &g, int b, int m0, int n0, float (&As)[SB_K][SB_M + 4],
+                                          float (&Bs)[SB_K][SB_N + 4]) {
   const TI *A = g.Aarr ? (const TI *)g.Aarr[b] : (const TI *)g.A + (long long)b * g.sA;
   const TI *B = g.Barr ? (const TI *)g.Barr[b] : (const TI *)g.B + (long long)b * g.sB;
   const int osz = g.out_type == 0 ? 4 : 2;
   char *C = g.Carr ? (char *)g.Carr[b] : (char *)g.C + (long long)b * g.sC * osz;
   const int tid = threadIdx.x, ty = tid & 15, tx = tid >> 4;
-  const int m0 = blockIdx.x * SB_M, n0 = blockIdx.y * SB_N;
   float acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
@@ -90,22 +86,35 @@ __global__ void __launch_bounds__(SB_T) tb200_gemm_simt_kernel(const tb200_gemm_
   }
 }
 
+// Grid-stride over the 64 x 64 output tiles of every batch element (a grid of a few CTAs per SM), so that
+// a launch that has nothing to do (run_if clear) costs a few microseconds whatever the problem size.
+template <typename TI>
+__global__ void __launch_bounds__(SB_T) tb200_gemm_simt_kernel(const tb200_gemm_t g, int gx, int gy) {
+  __shared__ float As[SB_K][SB_M + 4];
+  __shared__ float Bs[SB_K][SB_N + 4];
+  if (g.run_if && *(volatile const int *)g.run_if == 0) return;  // the tensor-core launch did the work
+  const long long tiles_xy = (long long)gx * gy, total = tiles_xy * g.batch;
+  for (long long t = blockIdx.x; t < total; t += gridDim.x) {
+    const int b = (int)(t / tiles_xy);
+    const long long r = t - (long long)b * tiles_xy;
+    simt_tile<TI>(g, b, (int)(r % gx) * SB_M, (int)(r / gx) * SB_N, As, Bs);
+  }
+}
+
 }  // namespace
 
 extern "C" int tb200_launch_simt(const tb200_gemm_t *g, cudaStream_t s) {
-  const unsigned gx = (unsigned)((g->m + SB_M - 1) / SB_M), gy = (unsigned)((g->n + SB_N - 1) / SB_N);
-  if (gy > 65535u) return (int)cudaErrorInvalidConfiguration;
-  for (int z0 = 0; z0 < g->batch; z0 += 65535) {
-    const unsigned gz = (unsigned)(g->batch - z0 < 65535 ? g->batch - z0 : 65535);
-    if (tb200_trace())
-      fprintf(stderr, "[trace] launch tb200_gemm_simt grid=(%u,%u,%u) block=(%d,1,1) m=%d n=%d k=%d in=%d out=%d\n", gx,
-              gy, gz, SB_T, g->m, g->n, g->k, g->in_type, g->out_type);
-    dim3 grid(gx, gy, gz);
-    if (g->in_type == TB200_F32) tb200_gemm_simt_kernel<float><<<grid, SB_T, 0, s>>>(*g, z0);
-    else if (g->in_type == TB200_F16) tb200_gemm_simt_kernel<__half><<<grid, SB_T, 0, s>>>(*g, z0);
-    else tb200_gemm_simt_kernel<__nv_bfloat16><<<grid, SB_T, 0, s>>>(*g, z0);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return (int)e;
-  }
-  return 0;
+  const long long gx = (g->m + SB_M - 1) / SB_M, gy = (g->n + SB_N - 1) / SB_N;
+  if (gx > 0x7fffffffLL || gy > 0x7fffffffLL) return (int)cudaErrorInvalidConfiguration;
+  const long long total = gx * gy * g->batch;
+  const long long cap = 8LL * tb200_num_sms();  // 8 resident CTAs of 256 threads per SM
+  const unsigned grid = (unsigned)(total < cap ? total : cap);
+  if (grid == 0) return 0;
+  if (tb200_trace())
+    fprintf(stderr, "[trace] launch tb200_gemm_simt grid=(%u,1,1) block=(%d,1,1) tiles=%lld m=%d n=%d k=%d in=%d out=%d\n",
+            grid, SB_T, total, g->m, g->n, g->k, g->in_type, g->out_type);
+  if (g->in_type == TB200_F32) tb200_gemm_simt_kernel<float><<<grid, SB_T, 0, s>>>(*g, (int)gx, (int)gy);
+  else if (g->in_type == TB200_F16) tb200_gemm_simt_kernel<__half><<<grid, SB_T, 0, s>>>(*g, (int)gx, (int)gy);
+  else tb200_gemm_simt_kernel<__nv_bfloat16><<<grid, SB_T, 0, s>>>(*g, (int)gx, (int)gy);
+  return (int)cudaGetLastError();
 }
