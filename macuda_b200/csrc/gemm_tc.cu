@@ -524,7 +524,8 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, i
 
 // tile width BN -> k-chunks per stage: the widest single-CTA tile keeps one chunk (four stages of 48 KB);
 // narrower tiles take two so that each stage carries enough tensor work to cover its issue cost. A pair's
-// 256 x 256 tile has 32 KB per CTA per chunk and keeps one chunk (six stages).
+// 256 x 256 tile has 32 KB per CTA per chunk and keeps one chunk (six stages); its 256 x 128 tile has
+// 24 KB and takes two (four stages of 48 KB).
 constexpr int kc_for(int bn) { return bn >= 256 ? 1 : 2; }
 
 }  // namespace
@@ -548,7 +549,7 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   int bn = tile_n;
   if (bn != 32 && bn != 64 && bn != 128 && bn != 256) bn = 128;
   const int cg = pair ? 2 : 1;
-  if (cg == 2) bn = 256;  // the pair tile is 256 x 256
+  if (cg == 2 && bn != 128) bn = 256;  // the pair tiles are 256 x 256 and 256 x 128
   const int b_mn = g->opB == 1, a_mn = g->opA == 0;
   if (b_mn && bn / cg < epr) bn = epr * cg;  // an MN-major B tile holds whole 128-byte rows
   const int b_rows = bn / cg;
@@ -560,7 +561,7 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   memset(&p, 0, sizeof p);
   CUtensorMap ta, tb;
   bool ok;
-  const int kc = cg == 2 ? 1 : kc_for(bn);
+  const int kc = cg == 2 && bn == 256 ? 1 : kc_for(bn);
   // pointer arrays: rank-2 template maps with a placeholder address, re-pointed per element on the device
   const void *baseA = ptr_ws ? (const void *)(uintptr_t)0x10000 : g->A;
   const void *baseB = ptr_ws ? (const void *)(uintptr_t)0x10000 : g->B;
@@ -626,7 +627,10 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
 
   int rc;
   if (cg == 2) {
-    rc = f32in ? launch_bn<1, 256, 1, 2>(ta, tb, p, num_sms, s) : launch_bn<0, 256, 1, 2>(ta, tb, p, num_sms, s);
+    if (bn == 128)
+      rc = f32in ? launch_bn<1, 128, 2, 2>(ta, tb, p, num_sms, s) : launch_bn<0, 128, 2, 2>(ta, tb, p, num_sms, s);
+    else
+      rc = f32in ? launch_bn<1, 256, 1, 2>(ta, tb, p, num_sms, s) : launch_bn<0, 256, 1, 2>(ta, tb, p, num_sms, s);
   } else if (f32in) {
     switch (bn) {
       case 32: rc = launch_bn<1, 32, kc_for(32), 1>(ta, tb, p, num_sms, s); break;

@@ -174,39 +174,32 @@ static int gemm_contract(cudaDataType At, cudaDataType Bt, cudaDataType Ct, cubl
 /* ---- planning ---- */
 static int esize(int t) { return t == TB200_F32 ? 4 : 2; }
 
-/* The persistent tensor-core kernel's tile: 128 x BN on one CTA (BN 32..256), or 256 x 256 on a pair of
- * CTAs (2-SM UMMA). Cost = waves of tiles over the SMs (pairs) x the time one SM spends on its share of a
- * tile, from the measured fraction of tensor peak each configuration sustains per SM: a 128 x N x 16
- * UMMA re-reads its whole A and B from shared memory, which caps narrow single-CTA tiles, while the pair
- * tile streams half of B per SM. */
+/* The persistent tensor-core kernel's tile: 128 x BN on one CTA (BN 32..256), or 256 x 256 / 256 x 128 on a
+ * pair of CTAs (2-SM UMMA). Cost = waves of tiles over the SMs (pairs) x the time one SM spends on its
+ * share of a tile, from the measured fraction of tensor peak each configuration sustains per SM: a
+ * 128 x N x 16 UMMA re-reads its whole A and B from shared memory, which caps narrow single-CTA tiles,
+ * while a pair tile streams half of B per SM. */
 int tb200_tc_tile_n(int m, int n, int batch, int num_sms, int *pair) {
-  static const int bns[4] = {256, 128, 64, 32};
-  static const double eff[4] = {0.57, 0.50, 0.35, 0.19};
-  static const double eff_pair = 0.80;
+  static const int bns[6] = {256, 128, 64, 32, 256, 128};
+  static const int cgs[6] = {1, 1, 1, 1, 2, 2};
+  /* per-SM fraction of tensor peak each tile sustains, measured on the B200. The 256 x 128 pair tile ran
+   * within 5 % of the 128 x 128 tile on the 4096 x 512 shapes (slower on Q, faster on down): equal
+   * efficiency and the same area per SM, so the planner keeps the single-CTA tile on ties */
+  static const double eff[6] = {0.57, 0.50, 0.35, 0.19, 0.80, 0.50};
   if (num_sms <= 0) num_sms = 148;
   int best = 256, best_pair = 0;
   double best_cost = 1e300;
-  for (int i = 0; i < 4; i++) {
-    int bn = bns[i];
+  for (int i = 0; i < 6; i++) {
+    const int bn = bns[i], cg = cgs[i];
     if (bn > 32 && n <= bn / 2) continue; /* a tile at least half full */
-    long long tiles = (long long)((m + 127) / 128) * ((n + bn - 1) / bn) * (long long)batch;
-    long long waves = (tiles + num_sms - 1) / num_sms;
-    double cost = (double)waves * bn / eff[i];
+    const long long tiles = (long long)((m + 128 * cg - 1) / (128 * cg)) * ((n + bn - 1) / bn) * (long long)batch;
+    const long long slots = num_sms / cg;
+    const long long waves = (tiles + slots - 1) / slots;
+    const double cost = (double)waves * bn / eff[i];
     if (cost < best_cost * 0.999) {
       best_cost = cost;
       best = bn;
-      best_pair = 0;
-    }
-  }
-  if (n > 128) { /* 256 x 256 pair tiles: two CTAs each hold 128 x 256 of it */
-    long long tiles = (long long)((m + 255) / 256) * ((n + 255) / 256) * (long long)batch;
-    long long slots = num_sms / 2;
-    long long waves = (tiles + slots - 1) / slots;
-    double cost = (double)waves * 256 / eff_pair;
-    if (cost < best_cost * 0.999) {
-      best_cost = cost;
-      best = 256;
-      best_pair = 1;
+      best_pair = cg == 2;
     }
   }
   if (pair) *pair = best_pair;
@@ -260,11 +253,11 @@ static cublasStatus_t run_gemm(struct tb200_handle *h, tb200_gemm_t *g) {
                         aligned, sms, &tile_n, &pair);
   if (kind == TB200_KERNEL_TC) {
     /* TB200_TC_BN=32|64|128|256 forces a single-CTA tile of that width, TB200_TC_BN=pair the 256 x 256
-     * pair tile (tests, bisecting) */
+     * pair tile and TB200_TC_BN=pair128 the 256 x 128 pair tile (tests, bisecting) */
     const char *e = getenv("TB200_TC_BN");
-    if (e && !strcmp(e, "pair")) {
+    if (e && (!strcmp(e, "pair") || !strcmp(e, "pair128"))) {
       pair = 1;
-      tile_n = 256;
+      tile_n = e[4] ? 128 : 256;
     } else {
       int v = e ? atoi(e) : 0;
       if (v == 32 || v == 64 || v == 128 || v == 256) {

@@ -169,4 +169,4 @@ def test_tile_choice_is_a_compiled_configuration(lib):
             bn = lib.lib.tb200_tc_tile_n(m, n, 1, 148, ctypes.byref(pair))
             assert bn in (32, 64, 128, 256) and pair.value in (0, 1)
             if pair.value:
-                assert bn == 256 and n > 128
+                assert bn in (128, 256) and n > bn // 2

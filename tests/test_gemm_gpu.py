@@ -73,7 +73,7 @@ TC_SHAPES = [
 ]
 
 
-@pytest.mark.parametrize("bn", [32, 64, 128, 256, "pair"])
+@pytest.mark.parametrize("bn", [32, 64, 128, 256, "pair", "pair128"])
 @pytest.mark.parametrize("opA,opB,m,n,k", TC_SHAPES)
 def test_tensor_core_shapes(lib, h, monkeypatch, bn, opA, opB, m, n, k):
     assert lib.plan(opA, opB, m, n, k, 1, 1, 0, 0, 0, 1, 148)[0] == cb.TB200_KERNEL_TC
@@ -81,7 +81,7 @@ def test_tensor_core_shapes(lib, h, monkeypatch, bn, opA, opB, m, n, k):
     assert_ok(run_and_check(lib, h, opA=opA, opB=opB, m=m, n=n, k=k, seed=m + n + k + len(str(bn))), f"BN {bn}")
 
 
-@pytest.mark.parametrize("bn", [32, 128, 256, "pair"])
+@pytest.mark.parametrize("bn", [32, 128, 256, "pair", "pair128"])
 def test_tensor_core_bf16_tf32_by_width(lib, h, monkeypatch, bn):
     monkeypatch.setenv("TB200_TC_BN", str(bn))
     assert_ok(run_and_check(lib, h, opA=1, opB=0, m=600, n=400, k=300, in_t=O.BF16, seed=5), "bf16")
@@ -89,7 +89,7 @@ def test_tensor_core_bf16_tf32_by_width(lib, h, monkeypatch, bn):
                             compute=cb.CUBLAS_COMPUTE_32F_FAST_TF32, seed=6), "tf32")
 
 
-@pytest.mark.parametrize("bn", ["128", "pair"])
+@pytest.mark.parametrize("bn", ["128", "pair", "pair128"])
 def test_tensor_core_alpha_beta_and_16bit_out(lib, h, monkeypatch, bn):
     monkeypatch.setenv("TB200_TC_BN", bn)
     for out_t in (O.F32, O.F16, O.BF16):
@@ -132,7 +132,7 @@ def test_skinny_pointer_arrays_gqa(lib, h):
     assert_ok(run_and_check(lib, h, m=768, n=8, k=2048, batch=8, mode="ptr", broadcast_a=4, seed=60), "ptr n=8")
 
 
-@pytest.mark.parametrize("bn", [None, "64", "pair"])
+@pytest.mark.parametrize("bn", [None, "64", "pair", "pair128"])
 def test_pointer_arrays_tensor_cores(lib, h, monkeypatch, bn):
     """cublasGemmBatchedEx on the tensor cores: per-element tensor maps built on the device."""
     if bn:
