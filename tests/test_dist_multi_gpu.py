@@ -1,6 +1,7 @@
-"""The N-sharded GEMM on 2 GPUs (skipped with fewer): both exchanges, every rank's full C - including
-the rows its peer computed and delivered (over NCCL, or by P2P stores from the peer's epilogue) - checked
-against the fp64 oracle on seeded row samples."""
+"""The N-sharded GEMM on every visible GPU, up to 8 (skipped with fewer than 2): both exchanges, every
+rank's full C - including the rows its peers computed and delivered (over NCCL, or by P2P stores from the
+peers' epilogues) - checked against the fp64 oracle on seeded row samples. m is not a multiple of the
+rank count, so the last rank owns fewer rows."""
 import os
 import socket
 
@@ -71,19 +72,20 @@ def _worker(rank, world, port, mode, m, n, k, q):
 
 
 @pytest.mark.parametrize("mode", ["fused", "allgather"])
-def test_two_gpu_sharded_gemm(mode):
+def test_sharded_gemm_on_all_gpus(mode):
     import torch
-    if torch.cuda.device_count() < 2:
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
         pytest.skip("needs 2 GPUs")
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    m, n, k = 4096 + 256, 512, 2048
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, mode, m, n, k, q)) for r in range(2)]
+    m, n, k = 4300, 512, 2048
+    procs = [ctx.Process(target=_worker, args=(r, world, port, mode, m, n, k, q)) for r in range(world)]
     for p in procs:
         p.start()
-    out = [q.get(timeout=300) for _ in range(2)]
+    out = [q.get(timeout=300) for _ in range(world)]
     for p in procs:
         p.join(timeout=120)
         if p.is_alive():
