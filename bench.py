@@ -305,7 +305,22 @@ def config_figures(torch, lib, cb, dtype_code, dtype):
     measure("c5_moe_down_pointer", lambda: h.gemm_batched_ex(
         1, 0, Hd, Te, Fe, 1.0, pa.data_ptr(), dtype_code, Fe, pb.data_ptr(), dtype_code, Fe, 0.0, pc.data_ptr(), f32,
         Hd, E), 10, flop5, (Wd.numel() + He.numel()) * 2 + Cd.numel() * 4, "hbm")
-    del Wgu, Wd, Xe, He, Cgu, Cd
+    # the same experts through the grouped GEMM (one launch, per-expert token counts on the device): balanced
+    # routing as above, then a skewed routing of the same 4096 token-slots (Dirichlet(0.3) shares, seeded)
+    import numpy as np
+    Xall = Xe.reshape(E * Te, Hd)  # the tokens of all experts, one expert after another: k = Hd x n = 4096
+    Call = torch.empty(E * Te * Fe, device="cuda")
+    skew = np.random.default_rng(5).multinomial(E * Te, np.random.default_rng(6).dirichlet(np.full(E, 0.3)))
+    grouped = hasattr(lib.lib, "tb200_gemm_grouped_ex")  # this library's extension; the reference has none
+    for label, counts in (("balanced", np.full(E, Te)), ("skewed", skew)) if grouped else ():
+        offs = torch.from_numpy(np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)).cuda()
+        used = int(np.count_nonzero(counts))  # an expert without tokens never reads its weights
+        measure(f"c5_moe_gate_up_grouped_{label}", lambda: h.gemm_grouped_ex(
+            1, 0, Fe, E * Te, Hd, E, offs.data_ptr(), 1.0, Wgu.data_ptr(), dtype_code, Hd, Fe * Hd, Xall.data_ptr(),
+            dtype_code, Hd, 0.0, Call.data_ptr(), f32, Fe), 10, flop5,
+            (used * Fe * Hd + Xe.numel()) * 2 + Call.numel() * 4, "hbm")
+        out[f"c5_moe_gate_up_grouped_{label}"]["experts_with_tokens"] = used
+    del Wgu, Wd, Xe, He, Cgu, Cd, Xall, Call
 
     # config 5 squares, both 16-bit input types
     for S in (4096, 8192, 16384):

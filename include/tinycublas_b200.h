@@ -120,6 +120,23 @@ enum { TB200_KERNEL_NONE = 0, TB200_KERNEL_SIMT = 1, TB200_KERNEL_SKINNY = 2, TB
 int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_type, int out_type,
                int tf32, int ptr_array, int aligned, int num_sms, int *tile_n, int *pair);
 
+/* Grouped GEMM for mixture-of-experts layers, in one launch: for every group (expert) g,
+ *   C[:, offsets[g] : offsets[g+1]] = alpha * op(A_g) * op(B)[:, offsets[g] : offsets[g+1]] + beta * C[same],
+ * with A_g = A + g * strideA (elements; 0 shares one A), B holding every group's tokens (columns) one group
+ * after another, and C m x n_total. `offsets` is a DEVICE array of groups + 1 non-decreasing column offsets
+ * (offsets[0] = 0, offsets[groups] = n_total), so per-expert token counts computed by a router on the GPU
+ * need not reach the host, and an expert may get any number of tokens (none included). Types, compute
+ * types, alpha/beta and argument rules as cublasGemmStridedBatchedEx (batchCount = groups <= 1024). Runs on
+ * the tensor-core kernel only: operands 16-byte aligned with lda, ldb and strideA whole multiples of 16
+ * bytes, f32 inputs only in TF32 mode; otherwise CUBLAS_STATUS_NOT_SUPPORTED. No counterpart in the
+ * reference, whose only MoE form is cublasGemmBatchedEx with one n for every expert (cublas.c:292-313):
+ * a routed layer's experts each get their own number of tokens. */
+cublasStatus_t tb200_gemm_grouped_ex(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb, int m,
+                                     int n_total, int k, int groups, const int *offsets, const void *alpha,
+                                     const void *A, cudaDataType Atype, int lda, long long strideA, const void *B,
+                                     cudaDataType Btype, int ldb, const void *beta, void *C, cudaDataType Ctype,
+                                     int ldc, cublasComputeType_t computeType);
+
 /* The persistent tensor-core kernel's tile choice for an m x n x batch GEMM on `num_sms` SMs: returns the
  * tile width (32, 64, 128 or 256) and sets *pair (if not NULL) to 1 for the 256 x 256 tile of a CTA pair.
  * Pure function, pinned by host-only tests. */

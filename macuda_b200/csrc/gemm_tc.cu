@@ -71,7 +71,14 @@ struct TcParams {
   const CUtensorMap *maps;
   void *const *Carr;
   const int *skip;
+  // grouped GEMM (MoE experts): when groups > 0, group g owns columns [grp_off[g], grp_off[g + 1]) of B and
+  // of C (device offsets, read by the kernel and clamped to [0, n]) and is batch element g of A; its tiles
+  // are numbered after those of groups 0 .. g-1, m-tile fastest
+  const int *grp_off;
+  int groups;
 };
+
+constexpr int TC_MAX_GROUPS = TB200_MAX_GROUPS;
 
 // KC = 128-byte k-chunks per stage. One stage holds A (128 rows) and B (BN rows) for KC * epr values of
 // k. The producers and the MMA thread spend a few hundred cycles of issue latency per stage whatever its
@@ -86,8 +93,10 @@ struct TcCfg {
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
   static constexpr int BAR_BYTES = 256;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES;
+  static constexpr int GRP_BYTES = 2 * 4 * (TC_MAX_GROUPS + 1);  // grouped GEMM: column offsets + tile prefix
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + GRP_BYTES;
 };
+
 
 __device__ __forceinline__ void decode_tile(const TcParams &p, long long t, int &b, int &mt, int &nt) {
   b = (int)(t / p.tiles_per_batch);
@@ -100,6 +109,38 @@ __device__ __forceinline__ void decode_tile(const TcParams &p, long long t, int 
   const int local = (int)(r - (long long)g * group_tiles);
   mt = first_m + local % gm;
   nt = local / gm;
+}
+
+// One output tile: batch element (or group) b, m-tile mt, and its columns [n0, n_end) of B and C (absolute,
+// so that a grouped GEMM's tile can start inside B).
+struct TileCoord {
+  int b, mt, n0, n_end;
+};
+
+// tile t of a plain or strided/pointer-array GEMM (grouped raster inside each batch element), or of a grouped
+// GEMM (g_off / g_pre: the groups' clamped column offsets and tile-count prefix in shared memory)
+template <int BN>
+__device__ __forceinline__ TileCoord tile_coord(const TcParams &p, long long t, const int *g_off, const int *g_pre) {
+  TileCoord c;
+  if (p.groups > 0) {
+    int lo = 0, hi = p.groups - 1;  // the group whose tile range holds t: g_pre[g] <= t < g_pre[g + 1]
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (g_pre[mid] <= t) lo = mid;
+      else hi = mid - 1;
+    }
+    const int local = (int)(t - g_pre[lo]);
+    c.b = lo;
+    c.mt = local % p.m_tiles;
+    c.n0 = g_off[lo] + (local / p.m_tiles) * BN;
+    c.n_end = g_off[lo + 1];
+    return c;
+  }
+  int nt;
+  decode_tile(p, t, c.b, c.mt, nt);
+  c.n0 = nt * BN;
+  c.n_end = p.n;
+  return c;
 }
 
 // One operand's loads for one stage: `rows` (128 for A, BN/CG for B) x KC chunks. K-major: chunk c is a
@@ -148,6 +189,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t *drain = tempty + 2;
   uint32_t *tmem_slot = (uint32_t *)(drain + 1);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
+  int *g_off = (int *)((uint8_t *)bars + Cfg::BAR_BYTES);  // grouped GEMM: clamped column offsets ...
+  int *g_pre = g_off + TC_MAX_GROUPS + 1;                  // ... and tile-count prefix
 
   // uniform early exit, before any barrier or TMEM allocation: every thread of every CTA reads the same flag
   // (written by the kernel before this one, so read only once that kernel has completed)
@@ -197,6 +240,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   // wait for that kernel to complete. Then let the next kernel set up on the SMs this one leaves free.
   griddep_wait();
   griddep_launch_dependents();
+  long long total_tiles = p.total_tiles;
+  if (p.groups > 0) {
+    // the groups' columns, clamped so that no tile reaches outside B or C whatever the offsets hold, and the
+    // prefix of their tile counts (the same in every CTA)
+    for (int g = threadIdx.x; g <= p.groups; g += blockDim.x) {
+      int o = p.grp_off[g];
+      g_off[g] = o < 0 ? 0 : o > p.n ? p.n : o;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int acc = 0, lo = 0;
+      for (int g = 0; g < p.groups; ++g) {
+        g_pre[g] = acc;
+        lo = g_off[g] > lo ? g_off[g] : lo;  // columns before the previous group's start count as empty
+        const int hi = g_off[g + 1] > lo ? g_off[g + 1] : lo;
+        g_off[g] = lo;
+        acc += ((hi - lo + BN - 1) / BN) * p.m_tiles;
+      }
+      g_pre[p.groups] = acc;
+      if (g_off[p.groups] < lo) g_off[p.groups] = lo;
+    }
+    __syncthreads();
+    total_tiles = g_pre[p.groups];
+  }
   const uint32_t tmem_base = *tmem_slot;
   // shared::cluster addresses of the even CTA's barriers (CG == 2)
   const uint32_t lead_full0 = CG == 2 ? mapa_shared(smem_u32(full), 0) : 0u;
@@ -215,10 +282,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       int s = 0;
       uint32_t ph = 0;
       uint32_t issued = 0, issued_par = 0;  // per stage: a fill is outstanding, and its phase parity
-      for (long long t = t_first; t < p.total_tiles && !*abort_flag; t += t_step) {
-        int b, mt, nt;
-        decode_tile(p, t, b, mt, nt);
-        const int mn0 = is_a ? mt * (TC_BM * CG) + (int)rank * TC_BM : nt * BN + (int)rank * Cfg::B_ROWS;
+      for (long long t = t_first; t < total_tiles && !*abort_flag; t += t_step) {
+        const TileCoord tc = tile_coord<BN>(p, t, g_off, g_pre);
+        const int b = tc.b;
+        const int mn0 = is_a ? tc.mt * (TC_BM * CG) + (int)rank * TC_BM : tc.n0 + (int)rank * Cfg::B_ROWS;
         const CUtensorMap *tm = tm0;
         if (p.maps) {  // this batch element's own map, written by the prep kernel through the generic proxy
           tm = p.maps + 2 * b + (is_a ? 0 : 1);
@@ -265,7 +332,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t empty0_l = smem_u32(empty), tfull0_l = smem_u32(tfull), drain_l = smem_u32(drain);
       const uint32_t empty0_p = CG == 2 ? mapa_shared(empty0_l, 1) : 0u;
       const uint32_t tfull0_p = CG == 2 ? mapa_shared(tfull0_l, 1) : 0u;
-      for (long long t = t_first; t < p.total_tiles && !*abort_flag; t += t_step) {
+      for (long long t = t_first; t < total_tiles && !*abort_flag; t += t_step) {
         if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, WAIT_BUDGET_CYC)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -322,9 +389,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int acc = 0;
     uint32_t aph = 0;
     const int osz = p.out_type == 0 ? 4 : 2;
-    for (long long t = t_first; t < p.total_tiles; t += t_step) {
-      int b, mt, nt;
-      decode_tile(p, t, b, mt, nt);
+    for (long long t = t_first; t < total_tiles; t += t_step) {
+      const TileCoord tc = tile_coord<BN>(p, t, g_off, g_pre);
+      const int b = tc.b, mt = tc.mt;
       // one lane waits, the warp follows its verdict: tcgen05.ld below needs the whole warp converged
       int got = 0;
       if (lane == 0) got = mbar_wait(&tfull[acc], aph, abort_flag, WAIT_BUDGET_CYC) ? 1 : 0;
@@ -332,8 +399,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (!got) break;
       tc_fence_after();
       const int row = mt * (TC_BM * CG) + (int)rank * TC_BM + quad * 32 + lane;
-      const int n0 = nt * BN;
-      char *Cb = p.Carr ? (char *)p.Carr[b] : (char *)p.C + (long long)b * p.sC * osz;
+      const int n0 = tc.n0;
+      char *Cb = p.Carr ? (char *)p.Carr[b] : (char *)p.C + (p.groups > 0 ? 0ll : (long long)b * p.sC * osz);
       const bool row_ok = row < p.m;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -341,8 +408,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
         tmem_ld_wait();
         const int col0 = n0 + c * 32;
-        if (row_ok && col0 < p.n) {
-          const int ncols = p.n - col0 < 32 ? p.n - col0 : 32;
+        if (row_ok && col0 < tc.n_end) {
+          const int ncols = tc.n_end - col0 < 32 ? tc.n_end - col0 : 32;
           if (p.nrep > 0) {
             // N-sharded GEMM: this rank's rows go straight into every replica of C, peers' over NVLink
             for (int q = 0; q < p.nrep; ++q) {
@@ -574,7 +641,7 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   }
   if (!ok && ptr_ws) return (int)cudaErrorNotSupported;  // the caller takes the general kernel
   if (!ok) {
-    if (g->nrep) return (int)cudaErrorNotSupported;  // only the tensor-core epilogue replicates
+    if (g->nrep || g->groups) return (int)cudaErrorNotSupported;  // tensor-core only: replication, groups
     if (tb200_trace()) fprintf(stderr, "[trace] tensor map refused; SIMT kernel instead\n");
     return tb200_launch_simt(g, s);
   }
@@ -591,6 +658,10 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   p.C = g->C; p.ldc = g->ldc; p.sC = g->sC; p.out_type = g->out_type;
   p.nrep = g->nrep;
   p.row0 = g->row0;
+  // grouped GEMM: the tile count is known only on the device; total_tiles (m-tiles x n-tiles over all columns,
+  // per group) bounds it and sizes the grid
+  p.groups = g->groups;
+  p.grp_off = g->grp_off;
   for (int q = 0; q < g->nrep && q < 8; ++q) p.rep[q] = g->rep[q];
   if (ptr_ws) {
     int *flag = (int *)ptr_ws;
@@ -654,7 +725,8 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
 }
 
 extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s) {
-  if (!tb200_tc_ok(g)) return g->nrep ? (int)cudaErrorNotSupported : tb200_launch_simt(g, s);
+  // only the tensor-core epilogue replicates rows, and only this kernel runs grouped GEMMs
+  if (!tb200_tc_ok(g)) return (g->nrep || g->groups) ? (int)cudaErrorNotSupported : tb200_launch_simt(g, s);
   return launch_tc_impl(g, tile_n, pair, num_sms, nullptr, s);
 }
 

@@ -34,7 +34,14 @@ typedef struct {
   /* the general kernel runs only if *run_if != 0 (NULL: always): the fallback launch behind a
    * pointer-array tensor-core launch, taken when some batch pointer is not 16-byte aligned */
   const int *run_if;
+  /* grouped GEMM (tensor-core kernel only): when groups > 0, group g multiplies batch element g of A (stride
+   * sA) with columns [grp_off[g], grp_off[g + 1]) of B into the same columns of C; grp_off is a device array
+   * of groups + 1 offsets read by the kernel (batch == groups, sB == sC == 0, n = all columns) */
+  const int *grp_off;
+  int groups;
 } tb200_gemm_t;
+
+#define TB200_MAX_GROUPS 1024
 
 int tb200_launch_simt(const tb200_gemm_t *g, cudaStream_t s);
 int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s);

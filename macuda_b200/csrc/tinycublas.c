@@ -240,6 +240,22 @@ static int operands_aligned(const tb200_gemm_t *g) {
   return 1;
 }
 
+/* TB200_TC_BN=32|64|128|256 forces a single-CTA tile of that width, TB200_TC_BN=pair the 256 x 256 pair
+ * tile and TB200_TC_BN=pair128 the 256 x 128 pair tile (tests, bisecting; read per call) */
+static void tile_override(int *tile_n, int *pair) {
+  const char *e = getenv("TB200_TC_BN");
+  if (e && (!strcmp(e, "pair") || !strcmp(e, "pair128"))) {
+    *pair = 1;
+    *tile_n = e[4] ? 128 : 256;
+  } else {
+    int v = e ? atoi(e) : 0;
+    if (v == 32 || v == 64 || v == 128 || v == 256) {
+      *tile_n = v;
+      *pair = 0;
+    }
+  }
+}
+
 static const char *kernel_name(int kind) {
   return kind == TB200_KERNEL_SKINNY ? "skinny" : kind == TB200_KERNEL_TC ? "tc" : kind == TB200_KERNEL_SIMT ? "simt" : "none";
 }
@@ -251,21 +267,7 @@ static cublasStatus_t run_gemm(struct tb200_handle *h, tb200_gemm_t *g) {
   int sms = tb200_num_sms();
   int kind = tb200_plan(g->opA, g->opB, g->m, g->n, g->k, g->batch, g->in_type, g->out_type, g->tf32, ptr_array,
                         aligned, sms, &tile_n, &pair);
-  if (kind == TB200_KERNEL_TC) {
-    /* TB200_TC_BN=32|64|128|256 forces a single-CTA tile of that width, TB200_TC_BN=pair the 256 x 256
-     * pair tile and TB200_TC_BN=pair128 the 256 x 128 pair tile (tests, bisecting) */
-    const char *e = getenv("TB200_TC_BN");
-    if (e && (!strcmp(e, "pair") || !strcmp(e, "pair128"))) {
-      pair = 1;
-      tile_n = e[4] ? 128 : 256;
-    } else {
-      int v = e ? atoi(e) : 0;
-      if (v == 32 || v == 64 || v == 128 || v == 256) {
-        tile_n = v;
-        pair = 0;
-      }
-    }
-  }
+  if (kind == TB200_KERNEL_TC) tile_override(&tile_n, &pair);
   if (tb200_trace())
     fprintf(stderr, "[trace] gemm %s op=%c%c m=%d n=%d k=%d batch=%d in=%d out=%d tf32=%d ptr=%d aligned=%d BN=%d pair=%d\n",
             kernel_name(kind), g->opA ? 'T' : 'N', g->opB ? 'T' : 'N', g->m, g->n, g->k, g->batch, g->in_type,
@@ -511,6 +513,60 @@ cublasStatus_t tb200_gemm_ex_allgather(cublasHandle_t handle, cublasOperation_t 
   int rc = tb200_launch_tc(&g, bn, pair, sms, h->stream);
   if (rc == (int)cudaErrorNotSupported) return CUBLAS_STATUS_NOT_SUPPORTED;
   return rc == 0 ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+/* One launch of the tensor-core kernel for every group (expert) of a mixture-of-experts layer: group g
+ * multiplies A_g = A + g * strideA with the columns [offsets[g], offsets[g + 1]) of B into the same columns
+ * of C. offsets is a device array (the per-expert token counts come from the router on the GPU and never
+ * reach the host). Same type contract and argument rules as cublasGemmStridedBatchedEx; the operands must
+ * suit the tensor-core kernel (16-byte aligned, ld and strideA whole multiples of 16 bytes), otherwise
+ * NOT_SUPPORTED. The kernel clamps the offsets to [0, n_total] and treats a decrease as an empty group. */
+cublasStatus_t tb200_gemm_grouped_ex(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb, int m,
+                                     int n_total, int k, int groups, const int *offsets, const void *alpha,
+                                     const void *A, cudaDataType Atype, int lda, long long strideA, const void *B,
+                                     cudaDataType Btype, int ldb, const void *beta, void *C, cudaDataType Ctype,
+                                     int ldc, cublasComputeType_t computeType) {
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  tb200_gemm_t g;
+  memset(&g, 0, sizeof g);
+  int tf32 = 0;
+  if (gemm_contract(Atype, Btype, Ctype, computeType, &g.in_type, &g.out_type, &tf32)) return CUBLAS_STATUS_NOT_SUPPORTED;
+  g.opA = op_code(transa);
+  g.opB = op_code(transb);
+  cublasStatus_t st = check_args(g.opA, g.opB, m, n_total, k, lda, ldb, ldc, groups);
+  if (st != CUBLAS_STATUS_SUCCESS) return st;
+  if (!alpha || !beta || !offsets || groups > TB200_MAX_GROUPS || strideA < 0) return CUBLAS_STATUS_INVALID_VALUE;
+  if (m == 0 || n_total == 0 || groups == 0) return CUBLAS_STATUS_SUCCESS;
+  if (g.in_type == TB200_F32)
+    g.tf32 = tf32 || (((int)h->math_mode & 0xf) == CUBLAS_TF32_TENSOR_OP_MATH && computeType == CUBLAS_COMPUTE_32F);
+  if (g.in_type == TB200_F32 && !g.tf32) return CUBLAS_STATUS_NOT_SUPPORTED; /* exact fp32: no grouped kernel */
+  g.m = m;
+  g.n = n_total;
+  g.k = k;
+  g.batch = groups;
+  g.alpha = read_scalar(alpha, computeType);
+  g.beta = read_scalar(beta, computeType);
+  g.A = A; g.lda = lda; g.sA = strideA;
+  g.B = B; g.ldb = ldb;
+  g.C = C; g.ldc = ldc;
+  g.grp_off = offsets;
+  g.groups = groups;
+  if (!operands_aligned(&g) || !tb200_tc_ok(&g)) return CUBLAS_STATUS_NOT_SUPPORTED;
+  int sms = tb200_num_sms(), pair = 0;
+  int avg_n = n_total / groups > 0 ? n_total / groups : 1;
+  int bn = tb200_tc_tile_n(m, avg_n, groups, sms, &pair);
+  tile_override(&bn, &pair);
+  if (tb200_trace())
+    fprintf(stderr, "[trace] gemm tc-grouped op=%c%c m=%d n_total=%d k=%d groups=%d BN=%d pair=%d\n", g.opA ? 'T' : 'N',
+            g.opB ? 'T' : 'N', m, n_total, k, groups, bn, pair);
+  int rc = tb200_launch_tc(&g, bn, pair, sms, h->stream);
+  if (rc == (int)cudaErrorNotSupported) return CUBLAS_STATUS_NOT_SUPPORTED;
+  if (rc != 0) {
+    fprintf(stderr, "[tinycublas_b200] grouped launch failed: %s\n", cudaGetErrorString((cudaError_t)rc));
+    return CUBLAS_STATUS_EXECUTION_FAILED;
+  }
+  return CUBLAS_STATUS_SUCCESS;
 }
 
 /* cublasGemmBatchedEx without any device allocation: same arguments, same results; where the pointer-array

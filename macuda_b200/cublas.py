@@ -92,6 +92,8 @@ EXTENSIONS = [
     ("tb200_gemm_batched_ex_noalloc", _i,
      [_vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp, _i, _i, _vp, _vp, _i, _i, _i, _i]),
     ("tb200_noalloc_max_batch", _i, []),
+    ("tb200_gemm_grouped_ex", _i,
+     [_vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _ll, _vp, _i, _i, _vp, _vp, _i, _i, _i]),
 ]
 
 
@@ -202,6 +204,14 @@ class Handle:
         return self.lib.cublasGemmStridedBatchedEx(self.h, ta, tb, m, n, k, ctypes.byref(a), A, Atype, lda, sA, B,
                                                    Btype, ldb, sB, ctypes.byref(b), C, Ctype, ldc, sC, batch,
                                                    compute_type, algo)
+
+    def gemm_grouped_ex(self, ta, tb, m, n_total, k, groups, offsets, alpha, A, Atype, lda, strideA, B, Btype, ldb,
+                        beta, C, Ctype, ldc, compute_type=CUBLAS_COMPUTE_32F) -> int:
+        """tb200_gemm_grouped_ex: offsets is a device pointer to groups + 1 int32 column offsets"""
+        a, b = scalar(alpha, compute_type), scalar(beta, compute_type)
+        return self.lib.tb200_gemm_grouped_ex(self.h, ta, tb, m, n_total, k, groups, offsets, ctypes.byref(a), A,
+                                              Atype, lda, strideA, B, Btype, ldb, ctypes.byref(b), C, Ctype, ldc,
+                                              compute_type)
 
     def gemm_batched_ex(self, ta, tb, m, n, k, alpha, Aarr, Atype, lda, Barr, Btype, ldb, beta, Carr, Ctype, ldc,
                         batch, compute_type=CUBLAS_COMPUTE_32F, algo=CUBLAS_GEMM_DEFAULT) -> int:

@@ -170,3 +170,25 @@ def test_tile_choice_is_a_compiled_configuration(lib):
             assert bn in (32, 64, 128, 256) and pair.value in (0, 1)
             if pair.value:
                 assert bn in (128, 256) and n > bn // 2
+
+
+def test_grouped_gemm_argument_rules(lib):
+    """tb200_gemm_grouped_ex refuses bad arguments before any device work (cuBLAS's rules, plus its own:
+    at most 1024 groups, a device offsets array, fp32 inputs only in TF32 mode)."""
+    with lib.handle() as h:
+        args = dict(m=64, n_total=64, k=64, groups=4, offsets=256, alpha=1.0, A=256, Atype=cb.CUDA_R_16F, lda=64,
+                    strideA=4096, B=256, Btype=cb.CUDA_R_16F, ldb=64, beta=0.0, C=256, Ctype=cb.CUDA_R_32F, ldc=64)
+
+        def call(**kw):
+            a = dict(args, **kw)
+            return h.gemm_grouped_ex(1, 0, a["m"], a["n_total"], a["k"], a["groups"], a["offsets"], a["alpha"], a["A"],
+                                     a["Atype"], a["lda"], a["strideA"], a["B"], a["Btype"], a["ldb"], a["beta"], a["C"],
+                                     a["Ctype"], a["ldc"])
+        assert call(groups=1025) == cb.CUBLAS_STATUS_INVALID_VALUE
+        assert call(offsets=0) == cb.CUBLAS_STATUS_INVALID_VALUE
+        assert call(lda=32) == cb.CUBLAS_STATUS_INVALID_VALUE  # op T: lda >= k
+        assert call(m=-1) == cb.CUBLAS_STATUS_INVALID_VALUE
+        assert call(strideA=-1) == cb.CUBLAS_STATUS_INVALID_VALUE
+        assert call(Btype=cb.CUDA_R_16BF) == cb.CUBLAS_STATUS_NOT_SUPPORTED  # A and B types differ
+        assert call(Atype=cb.CUDA_R_32F, Btype=cb.CUDA_R_32F) == cb.CUBLAS_STATUS_NOT_SUPPORTED  # exact fp32
+        assert call(groups=0) == cb.CUBLAS_STATUS_SUCCESS and call(n_total=0) == cb.CUBLAS_STATUS_SUCCESS

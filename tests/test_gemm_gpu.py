@@ -313,6 +313,69 @@ def test_dependent_chain_in_one_stream(lib, h):
         assert_ok(O.check(got, R, S, O.F16), f"link {i}")
 
 
+def _grouped_case(lib, h, rng, m, k, counts, in_t=O.F16, out_t=O.F32, alpha=1.0, beta=0.0, opA=1, offsets=None,
+                  guard=64):
+    """One tb200_gemm_grouped_ex call; every group's columns checked against the oracle on sampled rows,
+    and a guard region after C checked untouched. counts: tokens per group (offsets = their prefix)."""
+    import torch
+    G = len(counts)
+    offs = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32) if offsets is None else np.asarray(offsets, np.int32)
+    n_total = int(np.sum(counts))
+    lda = k if opA == 1 else m
+    A = storage(rng, G * m * k, in_t, 0.02)
+    B = storage(rng, max(1, k * n_total), in_t)
+    C0 = storage(rng, m * n_total + guard, out_t)
+    dA, dB, dC = dev(A), dev(B), dev(C0)
+    d_off = torch.from_numpy(offs).cuda()
+    ct = {O.F16: cb.CUDA_R_16F, O.BF16: cb.CUDA_R_16BF, O.F32: cb.CUDA_R_32F}
+    st = h.gemm_grouped_ex(opA, 0, m, n_total, k, G, d_off.data_ptr(), alpha, dA.data_ptr(), ct[in_t], lda, m * k,
+                           dB.data_ptr(), ct[in_t], k, beta, dC.data_ptr(), ct[out_t], m)
+    torch.cuda.synchronize()
+    assert st == cb.CUBLAS_STATUS_SUCCESS, st
+    C = host(dC, C0)
+    assert np.array_equal(C[m * n_total:], C0[m * n_total:]), "the guard region after C was written"
+    rows = np.unique(np.concatenate([np.arange(0, m, 11), [m - 1]])).astype(np.int32)
+    clamped = np.maximum.accumulate(np.clip(offs, 0, n_total))
+    for g in range(G):
+        c0, c1 = int(clamped[g]), int(clamped[g + 1])
+        if c1 <= c0:
+            continue
+        n = c1 - c0
+        Ag = A[g * m * k:(g + 1) * m * k]
+        Bg = B[c0 * k:c1 * k]
+        Cg0 = C0[c0 * m:c1 * m]
+        R, S = O.gemm(opA, 0, m, n, k, alpha, Ag, in_t, lda, Bg, in_t, k, beta, Cg0, out_t, m, rows=rows)
+        res = O.check(O.extract(C[c0 * m:c1 * m], out_t, m, n, m, rows=rows), R, S, out_t)
+        assert res["ok"], f"group {g} (columns {c0}..{c1}): {res}"
+
+
+def test_grouped_gemm_moe_unbalanced_routing(lib, h):
+    """Config 5's expert shape (768 x 2048, 128 experts) with 4096 routed tokens spread unevenly: skewed
+    counts, empty experts included, each expert's n different and mostly not a multiple of the tile."""
+    rng = np.random.default_rng(150)
+    p = rng.dirichlet(np.full(128, 0.3))
+    counts = rng.multinomial(4096, p)
+    counts[[0, 17, 127]] = 0
+    assert (counts == 0).sum() >= 3 and counts.max() > 3 * counts.mean()
+    _grouped_case(lib, h, rng, 768, 2048, counts)
+
+
+@pytest.mark.parametrize("in_t,out_t,alpha,beta,opA", [(O.BF16, O.F32, 1.0, 0.0, 1), (O.F16, O.F16, 0.5, 0.75, 1),
+                                                       (O.F16, O.F32, 1.0, 0.0, 0)])
+def test_grouped_gemm_types_epilogue_and_majors(lib, h, in_t, out_t, alpha, beta, opA):
+    rng = np.random.default_rng(151)
+    _grouped_case(lib, h, rng, 1000, 512, [37, 0, 300, 1, 64, 129], in_t=in_t, out_t=out_t, alpha=alpha, beta=beta,
+                  opA=opA)
+
+
+def test_grouped_gemm_clamps_malformed_offsets(lib, h):
+    """Offsets past n_total or decreasing: the kernel clamps them (a decrease is an empty group) and never
+    writes outside C."""
+    rng = np.random.default_rng(152)
+    counts = [40, 40, 40, 40]  # n_total = 160
+    _grouped_case(lib, h, rng, 256, 256, counts, offsets=[0, 60, 30, 500, 160])
+
+
 def test_two_streams_no_shared_state(lib):
     """The reference's BURST arm (splitk-20260923/test_splitk.cu:153-175) with two streams fails 8/8 because
     its split-K workspace is per handle. Here: 8 decode GEMMs and 8 prefill GEMMs on two streams and two
