@@ -12,9 +12,11 @@ Inputs are larger than L2 (1.9 GB touched per step), so no flush is needed betwe
 
 At N > 1 (torchrun, one process per GPU, NCCL): every projection is N-sharded along m (the weight's
 output features); each rank computes its m/N rows and its GEMM epilogue stores them into every rank's
-C over NVLink (CUDA IPC mappings, macuda_b200.dist.FusedShardedGemm), with one 4-byte NCCL all-reduce
-per step as the completion barrier; --exchange allgather uses an NCCL all-gather + layout kernel
-instead. Total work is fixed, so scaling is "strong".
+C over NVLink P2P (CUDA IPC mappings, macuda_b200.dist.FusedShardedGemm), with one 4-byte NCCL
+all-reduce per step as the completion barrier. --exchange multicast stores each element once to an
+NVLink multicast address instead (symmetric memory; slower for this all-gather, see macuda_b200/dist.py);
+--exchange allgather uses an NCCL all-gather + layout kernel. Total work is fixed, so scaling is
+"strong".
 
 Keys beyond the base contract: roofline (dominant kernel = the lm_head GEMM), cpu_baseline (the
 oracle's multithreaded fp16 GEMM on the host, a stand-in for ggml-cpu), e2e (the same step through the
@@ -421,12 +423,13 @@ def run(args):
     h = lib.handle()
     h.set_stream(stream.cuda_stream)
     sharded = []
-    fused = world > 1 and args.exchange == "fused"
+    fused = world > 1 and args.exchange != "allgather"
     if world > 1:
         from macuda_b200.dist import FusedShardedGemm, ShardedGemm, step_barrier
         for L in layers:
             if fused:
-                sharded.append(FusedShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype))
+                sharded.append(FusedShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype,
+                                                exchange={"fused": "p2p"}.get(args.exchange, args.exchange)))
             else:
                 sharded.append(ShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype))
     # Inside the timed region the only events are the two around the dominant GEMM (lm_head, the roofline
@@ -616,9 +619,11 @@ def run(args):
             "dtype": args.dtype, "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) activations; no checkpoint)",
             "config": {"workload": "llama3.1-8b prefill projections q,k,v,o,gate,up,down,lm_head @ 512 tokens "
                                    "(BASELINE configs[1])", "tokens": TOKENS, "step_gflop": round(STEP_FLOP / 1e9, 1),
-                       "parallelism": (f"N-shard x{world}, C exchanged by " + ("P2P stores from the GEMM epilogue "
-                                       "(NVLink) + one NCCL barrier per step" if fused else "NCCL all-gather + "
-                                       "layout kernel")) if world > 1 else "single GPU",
+                       "parallelism": (f"N-shard x{world}, C exchanged by " + (
+                                       ("NVLink multicast stores" if sharded[0].exchange == "multicast" else
+                                        "P2P stores over NVLink") + " from the GEMM epilogue + one NCCL barrier per "
+                                       "step" if fused else "NCCL all-gather + layout kernel")) if world > 1
+                                       else "single GPU",
                        "l2": "inputs larger than L2 (1.9 GB per step); no flush"},
             "frac_of_peak": round(value / pk["bf16_tflops_sustained"], 4),
             "roofline": roofline, "shapes": shapes,
@@ -671,8 +676,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true", help="skip the config 3 and 5 figures")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--gemm", default=None, help="MxNxK: time one T,N GEMM alone (profiling)")
-    ap.add_argument("--exchange", choices=["fused", "allgather"], default="fused",
-                    help="N > 1: how the sharded C is replicated")
+    ap.add_argument("--exchange", choices=["fused", "multicast", "p2p", "allgather"], default="fused",
+                    help="N > 1: how the sharded C is replicated (fused = p2p stores from the epilogue)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -201,6 +201,16 @@ cublasStatus_t tb200_gemm_ex_allgather(cublasHandle_t handle, cublasOperation_t 
                                        int lda, const void *B, cudaDataType Btype, int ldb, void *const *C_replicas,
                                        int P, cudaDataType Ctype, int ldc, int row0, cublasComputeType_t computeType);
 
+/* The same N-sharded GEMM with the exchange through NVLink multicast (NVSwitch): C_multicast is the multicast
+ * address of a buffer every rank holds (one multicast object bound to all of them); each element of this
+ * rank's rows is stored once there and the switch writes it into every rank's C at row offset row0, so a
+ * rank sends its own rows once instead of once per peer. f32 C, beta = 0; the caller orders the stores
+ * before any rank reads C (a collective after the launch). No counterpart in the reference (single-GPU). */
+cublasStatus_t tb200_gemm_ex_multicast(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb,
+                                       int m_local, int n, int k, const void *alpha, const void *A, cudaDataType Atype,
+                                       int lda, const void *B, cudaDataType Btype, int ldb, void *C_multicast,
+                                       cudaDataType Ctype, int ldc, int row0, cublasComputeType_t computeType);
+
 /* Set-up helpers for the replicas (not on the GEMM path): device memory another process of the node can
  * map. tb200_ipc_alloc returns the pointer and writes the 64-byte CUDA IPC handle to `handle`;
  * tb200_ipc_open maps a peer's handle into this process; tb200_ipc_close unmaps it; tb200_ipc_free

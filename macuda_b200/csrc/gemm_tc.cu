@@ -66,6 +66,7 @@ struct TcParams {
   int bk;    // k elements per stage
   int nrep, row0;  // replicated output: rows go to row0 + row of each of nrep replicas (beta == 0)
   void *rep[8];
+  float *mc;       // or of the multicast address of all ranks' f32 C (one store reaches every replica)
   // pointer-array batches: per batch element b, maps[2b] (A) and maps[2b+1] (B) in global memory, C from
   // Carr[b]; the launch does nothing if *skip != 0 (some pointer unfit for TMA: the general kernel runs)
   const CUtensorMap *maps;
@@ -410,7 +411,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const int col0 = n0 + c * 32;
         if (row_ok && col0 < tc.n_end) {
           const int ncols = tc.n_end - col0 < 32 ? tc.n_end - col0 : 32;
-          if (p.nrep > 0) {
+          if (p.mc) {
+            // N-sharded GEMM, multicast: one store per element, replicated to every rank's C by the switch
+            float *dst = p.mc + p.row0 + row + (long long)col0 * p.ldc;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < ncols) multimem_st_f32(dst + (long long)j * p.ldc, p.alpha * __uint_as_float(r[j]));
+          } else if (p.nrep > 0) {
             // N-sharded GEMM: this rank's rows go straight into every replica of C, peers' over NVLink
             for (int q = 0; q < p.nrep; ++q) {
               char *Cq = (char *)p.rep[q] + (long long)p.row0 * osz;
@@ -455,7 +462,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
   }
 
-  if (p.nrep > 0 && warp >= 2 && warp <= 5) __threadfence_system();  // peers' replicas: stores performed
+  if ((p.nrep > 0 || p.mc) && warp >= 2 && warp <= 5) __threadfence_system();  // peers' replicas: stores performed
   tc_fence_before();
   __syncwarp();
   if (CG == 2) cluster_sync();  // neither CTA leaves while its pair may still touch its memory or barriers
@@ -641,7 +648,7 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   }
   if (!ok && ptr_ws) return (int)cudaErrorNotSupported;  // the caller takes the general kernel
   if (!ok) {
-    if (g->nrep || g->groups) return (int)cudaErrorNotSupported;  // tensor-core only: replication, groups
+    if (g->nrep || g->mc || g->groups) return (int)cudaErrorNotSupported;  // tensor-core only
     if (tb200_trace()) fprintf(stderr, "[trace] tensor map refused; SIMT kernel instead\n");
     return tb200_launch_simt(g, s);
   }
@@ -658,6 +665,7 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   p.C = g->C; p.ldc = g->ldc; p.sC = g->sC; p.out_type = g->out_type;
   p.nrep = g->nrep;
   p.row0 = g->row0;
+  p.mc = (float *)g->mc;
   // grouped GEMM: the tile count is known only on the device; total_tiles (m-tiles x n-tiles over all columns,
   // per group) bounds it and sizes the grid
   p.groups = g->groups;
@@ -726,7 +734,8 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
 
 extern "C" int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s) {
   // only the tensor-core epilogue replicates rows, and only this kernel runs grouped GEMMs
-  if (!tb200_tc_ok(g)) return (g->nrep || g->groups) ? (int)cudaErrorNotSupported : tb200_launch_simt(g, s);
+  if (!tb200_tc_ok(g))
+    return (g->nrep || g->mc || g->groups) ? (int)cudaErrorNotSupported : tb200_launch_simt(g, s);
   return launch_tc_impl(g, tile_n, pair, num_sms, nullptr, s);
 }
 

@@ -95,6 +95,13 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// ---- NVLink multicast (NVSwitch) -------------------------------------------------------------------------
+// One store to a multicast address: the switch writes it to the buffer of every GPU bound to the multicast
+// object (this one's included)
+__device__ __forceinline__ void multimem_st_f32(float *mc_addr, float v) {
+  asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(mc_addr), "f"(v) : "memory");
+}
+
 // ---- programmatic dependent launch ------------------------------------------------------------------
 // Blocks until the grids this one depends on (the kernel before it in the stream, when it was launched with
 // programmatic stream serialization) have completed and their memory operations are visible. Returns at

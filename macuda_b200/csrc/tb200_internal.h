@@ -31,6 +31,9 @@ typedef struct {
    * process, peers' buffers included) instead of C; tensor-core kernel only, beta == 0, batch == 1 */
   int nrep, row0;
   void *rep[8];
+  /* the same with one multicast address instead of replicas: every f32 store of the epilogue goes to the
+   * multicast object of all ranks' C (NVSwitch fans it out); row offset row0 */
+  void *mc;
   /* the general kernel runs only if *run_if != 0 (NULL: always): the fallback launch behind a
    * pointer-array tensor-core launch, taken when some batch pointer is not 16-byte aligned */
   const int *run_if;

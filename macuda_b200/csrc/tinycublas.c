@@ -515,6 +515,52 @@ cublasStatus_t tb200_gemm_ex_allgather(cublasHandle_t handle, cublasOperation_t 
   return rc == 0 ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
 }
 
+/* The N-sharded GEMM with its output exchange through NVLink multicast: this rank's m_local rows are stored
+ * once per element to C_multicast (the multicast address of a buffer every rank holds, bound to one
+ * multicast object), and the switch writes them into every rank's C at row offset row0. f32 C only (the
+ * multimem store is f32), beta = 0. The caller orders the stores before any rank reads its C (a collective
+ * after the launch). */
+cublasStatus_t tb200_gemm_ex_multicast(cublasHandle_t handle, cublasOperation_t transa, cublasOperation_t transb,
+                                       int m_local, int n, int k, const void *alpha, const void *A, cudaDataType Atype,
+                                       int lda, const void *B, cudaDataType Btype, int ldb, void *C_multicast,
+                                       cudaDataType Ctype, int ldc, int row0, cublasComputeType_t ct) {
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  tb200_gemm_t g;
+  memset(&g, 0, sizeof g);
+  int tf32 = 0;
+  if (gemm_contract(Atype, Btype, Ctype, ct, &g.in_type, &g.out_type, &tf32)) return CUBLAS_STATUS_NOT_SUPPORTED;
+  if (g.out_type != TB200_F32) return CUBLAS_STATUS_NOT_SUPPORTED;
+  g.opA = op_code(transa);
+  g.opB = op_code(transb);
+  if (!C_multicast || row0 < 0 || !alpha) return CUBLAS_STATUS_INVALID_VALUE;
+  cublasStatus_t st = check_args(g.opA, g.opB, m_local, n, k, lda, ldb, ldc, 1);
+  if (st != CUBLAS_STATUS_SUCCESS) return st;
+  if ((long long)row0 + m_local > ldc) return CUBLAS_STATUS_INVALID_VALUE; /* rows stay inside C's columns */
+  if (m_local == 0 || n == 0) return CUBLAS_STATUS_SUCCESS;
+  g.tf32 = tf32;
+  g.m = m_local;
+  g.n = n;
+  g.k = k;
+  g.batch = 1;
+  g.alpha = read_scalar(alpha, ct);
+  g.beta = 0.f;
+  g.A = A; g.lda = lda;
+  g.B = B; g.ldb = ldb;
+  g.C = C_multicast; g.ldc = ldc;
+  g.mc = C_multicast;
+  g.row0 = row0;
+  if (!operands_aligned(&g) || !tb200_tc_ok(&g)) return CUBLAS_STATUS_NOT_SUPPORTED;
+  int sms = tb200_num_sms(), pair = 0;
+  int bn = tb200_tc_tile_n(m_local, n, 1, sms, &pair);
+  if (tb200_trace())
+    fprintf(stderr, "[trace] gemm tc-multicast m_local=%d n=%d k=%d row0=%d BN=%d pair=%d\n", m_local, n, k, row0, bn,
+            pair);
+  int rc = tb200_launch_tc(&g, bn, pair, sms, h->stream);
+  if (rc == (int)cudaErrorNotSupported) return CUBLAS_STATUS_NOT_SUPPORTED;
+  return rc == 0 ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
 /* One launch of the tensor-core kernel for every group (expert) of a mixture-of-experts layer: group g
  * multiplies A_g = A + g * strideA with the columns [offsets[g], offsets[g + 1]) of B into the same columns
  * of C. offsets is a device array (the per-expert token counts come from the router on the GPU and never

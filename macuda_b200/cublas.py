@@ -84,6 +84,8 @@ EXTENSIONS = [
     ("tb200_version", ctypes.c_char_p, []),
     ("tb200_gemm_ex_allgather", _i,
      [_vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _i, _i, _i, _i]),
+    ("tb200_gemm_ex_multicast", _i,
+     [_vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp, _i, _i, _vp, _i, _i, _i, _i]),
     ("tb200_ipc_alloc", _i, [_sz, ctypes.POINTER(_vp), _vp]),
     ("tb200_ipc_open", _i, [_vp, ctypes.POINTER(_vp)]),
     ("tb200_ipc_close", _i, [_vp]),

@@ -5,10 +5,16 @@ weight's output features - cuBLAS m under ggml's (T, N) call - across P ranks, o
 rank r owns weight rows [r*mp, r*mp + rows_r) with mp = ceil(m / P) (the last rank may own fewer).
 Two ways to replicate C:
 
-  FusedShardedGemm (default): every rank's C is mapped into every other rank (CUDA IPC); the tensor-core
-    epilogue of tb200_gemm_ex_allgather stores this rank's rows into all P replicas, the peers' over
-    NVLink P2P, overlapping the exchange with the remaining tiles; one 4-byte NCCL all-reduce per step
-    tells each rank that its peers' stores have landed.
+  FusedShardedGemm (default): the exchange is done by the tensor-core epilogue while later tiles still
+    compute. By default every rank's C is mapped into every other rank (CUDA IPC) and the epilogue stores
+    this rank's rows into all P replicas over NVLink P2P (tb200_gemm_ex_allgather). exchange="multicast"
+    instead stores each element once to an NVLink multicast address (NVSwitch; every rank's C in symmetric
+    memory bound to one multicast object) and the switch writes it into every rank's C
+    (tb200_gemm_ex_multicast). That sends a rank's rows once instead of once per peer, but every rank then
+    also receives its own rows back through its NVLink port: inbound traffic is all of C instead of
+    (P-1)/P of it, and inbound is the bound of an all-gather, so P2P is the default (measured at P = 2:
+    0.586 vs 0.778 ms per step). Either way one 4-byte NCCL all-reduce per step tells each rank that its
+    peers' stores have landed.
   ShardedGemm: the GEMM writes a local mp x n block, an NCCL all-gather on a communication stream
     concatenates the P blocks, and tb200_gather_row_blocks lays them out as the column-major C.
 
@@ -100,16 +106,20 @@ class _DeviceArray:
 class FusedShardedGemm:
     """N-sharded GEMM with the output exchange fused into the tensor-core epilogue.
 
-    Every rank allocates its full C (m x n, f32) with tb200_ipc_alloc, the 64-byte IPC handles are
-    all-gathered, and each rank maps every peer's C (tb200_ipc_open). `run` launches
-    tb200_gemm_ex_allgather: this rank's rows are stored into all P replicas of C by the epilogue, the
-    peers' over NVLink P2P while later tiles still compute - no all-gather call, no layout kernel.
-    After the last GEMM of a step, `step_barrier` (a 4-byte NCCL all-reduce on the compute stream) tells
-    every rank that all peers' kernels, and so their stores into its C, have completed.
+    exchange="multicast": every rank's full C (m x n, f32) is one symmetric-memory buffer (torch's CUDA
+    symmetric memory, bound to an NVLink multicast object); `run` launches tb200_gemm_ex_multicast, whose
+    epilogue stores each element of this rank's rows once to the multicast address.
+    exchange="p2p": every rank allocates its C with tb200_ipc_alloc, the 64-byte IPC handles are
+    all-gathered, each rank maps every peer's C (tb200_ipc_open), and `run` launches
+    tb200_gemm_ex_allgather, whose epilogue stores this rank's rows into all P replicas.
+    exchange="auto": multicast when every rank has a multicast address, else p2p. Default: "p2p".
+    No all-gather call, no layout kernel. After the last GEMM of a step, `step_barrier` (a 4-byte NCCL
+    all-reduce on the compute stream) tells every rank that all peers' kernels, and so their stores into
+    its C, have completed.
     """
 
     def __init__(self, lib, handle, m: int, n: int, k: int, rank: int, world: int, w_local, dtype_code: int,
-                 group=None):
+                 group=None, exchange: str = "p2p"):
         import ctypes
 
         import torch
@@ -120,6 +130,28 @@ class FusedShardedGemm:
         self.first, self.rows, self.mp = shard_rows(m, world, rank)
         self.w = w_local
         self.dtype_code = dtype_code
+        self.mc, self._symm, self.own, self.opened = 0, None, 0, []
+        if exchange not in ("auto", "multicast", "p2p"):
+            raise ValueError(f"exchange {exchange!r}")
+        if exchange != "p2p":
+            buf, hdl, mc = None, None, 0
+            try:
+                import torch.distributed._symmetric_memory as symm_mem
+                buf = symm_mem.empty(m * n, dtype=torch.float32, device=torch.device("cuda", torch.cuda.current_device()))
+                hdl = symm_mem.rendezvous(buf, group if group is not None else dist.group.WORLD)
+                mc = int(getattr(hdl, "multicast_ptr", 0) or 0)
+            except Exception:
+                mc = 0
+            have = torch.tensor([1 if mc else 0], dtype=torch.int32, device="cuda")
+            dist.all_reduce(have, op=dist.ReduceOp.MIN, group=group)  # every rank takes the same exchange
+            if int(have.item()) == 1:
+                self.mc, self._symm, self.c = mc, (buf, hdl), buf
+                self.exchange = "multicast"
+                return
+            if exchange == "multicast":
+                raise RuntimeError("NVLink multicast is not available on every rank")
+            del buf, hdl
+        self.exchange = "p2p"
         own = ctypes.c_void_p()
         hbuf = ctypes.create_string_buffer(64)
         st = lib.lib.tb200_ipc_alloc(m * n * 4, ctypes.byref(own), hbuf)
@@ -148,6 +180,11 @@ class FusedShardedGemm:
         if self.rows == 0:
             return 0
         one = ctypes.c_float(1.0)
+        if self.mc:
+            return self.lib.lib.tb200_gemm_ex_multicast(
+                self.h.h, cb.CUBLAS_OP_T, cb.CUBLAS_OP_N, self.rows, self.n, self.k, ctypes.byref(one),
+                self.w.data_ptr(), self.dtype_code, self.k, x.data_ptr(), self.dtype_code, self.k, self.mc,
+                cb.CUDA_R_32F, self.m, self.first, cb.CUBLAS_COMPUTE_32F)
         return self.lib.lib.tb200_gemm_ex_allgather(
             self.h.h, cb.CUBLAS_OP_T, cb.CUBLAS_OP_N, self.rows, self.n, self.k, ctypes.byref(one), self.w.data_ptr(),
             self.dtype_code, self.k, x.data_ptr(), self.dtype_code, self.k, self.rep_array, self.world, cb.CUDA_R_32F,
@@ -158,6 +195,10 @@ class FusedShardedGemm:
         import torch.distributed as dist
         torch.cuda.synchronize()
         dist.barrier(group=self.group)
+        if self._symm is not None:  # symmetric memory: released once no rank can still write into it
+            self._symm, self.c, self.mc = None, None, 0
+            dist.barrier(group=self.group)
+            return
         for p in self.opened:
             self.lib.lib.tb200_ipc_close(p)
         self.opened = []

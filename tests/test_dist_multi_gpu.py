@@ -27,7 +27,7 @@ def _worker(rank, world, port, mode, m, n, k, q):
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
-    ok, info = False, ""
+    ok, info, used = False, "", mode
     try:
         from macuda_b200 import cublas as cb
         from macuda_b200.dist import FusedShardedGemm, ShardedGemm, shard_rows, step_barrier
@@ -42,8 +42,10 @@ def _worker(rank, world, port, mode, m, n, k, q):
         first, rows, _ = shard_rows(m, world, rank)
         w_local = torch.from_numpy(W[first * k:(first + rows) * k].view(np.int16).copy()).cuda()
         x = torch.from_numpy(X.view(np.int16)).cuda()
-        if mode == "fused":
-            g = FusedShardedGemm(lib, h, m, n, k, rank, world, w_local, cb.CUDA_R_16F)
+        if mode in ("multicast", "p2p"):
+            g = FusedShardedGemm(lib, h, m, n, k, rank, world, w_local, cb.CUDA_R_16F,
+                                 exchange="auto" if mode == "multicast" else "p2p")  # auto: multicast if present
+            used = g.exchange
             g.c.fill_(float("nan"))
             torch.cuda.synchronize()
             dist.barrier()
@@ -62,16 +64,16 @@ def _worker(rank, world, port, mode, m, n, k, q):
         R, S = O.gemm(1, 0, m, n, k, 1.0, W, O.F16, k, X, O.F16, k, rows=rows_s)
         res = O.check(O.extract(C, O.F32, m, n, m, rows=rows_s), R, S, O.F32)
         ok, info = (st == 0 and res["ok"]), f"st={st} {res}"
-        if mode == "fused":
+        if mode in ("multicast", "p2p"):
             g.close()
         h.close()
     except Exception as ex:
         info = repr(ex)
-    q.put((rank, ok, info))
+    q.put((rank, ok, info, used))
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["fused", "allgather"])
+@pytest.mark.parametrize("mode", ["multicast", "p2p", "allgather"])
 def test_sharded_gemm_on_all_gpus(mode):
     import torch
     world = min(torch.cuda.device_count(), 8)
@@ -90,5 +92,7 @@ def test_sharded_gemm_on_all_gpus(mode):
         p.join(timeout=120)
         if p.is_alive():
             p.kill()
-    for rank, ok, info in out:
+    for rank, ok, info, used in out:
         assert ok, f"rank {rank}: {info}"
+    if mode == "multicast" and any(u != "multicast" for _, _, _, u in out):
+        pytest.skip("no NVLink multicast on this box (the p2p exchange ran and passed)")
