@@ -128,7 +128,8 @@ class ClockSampler:
 
 
 def make_inputs(torch, rank, world, dtype, seed=1234):
-    """Weights (this rank's m/world rows of each projection, stored k x m: op T, lda = k) and activations."""
+    """Weights (each projection's full matrix, the same on every rank, stored k x m: op T, lda = k; "w" is
+    this rank's m/world rows of it) and activations."""
     g = torch.Generator(device="cuda")
     g.manual_seed(seed)
     acts = {
@@ -139,12 +140,12 @@ def make_inputs(torch, rank, world, dtype, seed=1234):
     layers = []
     for name, m, k, src in PROJECTIONS:
         first, rows, mp = shard_rows(m, world, rank)
-        w = torch.empty(max(rows, 1), k, device="cuda", dtype=dtype)  # row r = output feature first + r
         gw = torch.Generator(device="cuda")
-        gw.manual_seed(seed * 131 + sum(map(ord, name)) * 7 + rank)
-        w.copy_(torch.randn(w.shape[0], k, device="cuda", generator=gw) * 0.02)
+        gw.manual_seed(seed * 131 + sum(map(ord, name)) * 7)
+        w_full = (torch.randn(m, k, device="cuda", generator=gw) * 0.02).to(dtype)  # row r = output feature r
+        w = w_full if world == 1 else w_full[first:first + max(rows, 1)].clone()
         c = torch.empty(m * TOKENS, device="cuda", dtype=torch.float32) if world == 1 else None
-        layers.append({"name": name, "m": m, "mp": rows, "k": k, "src": src, "w": w, "c_local": c})
+        layers.append({"name": name, "m": m, "mp": rows, "k": k, "src": src, "w": w, "w_full": w_full, "c_local": c})
     return acts, layers
 
 
@@ -424,14 +425,26 @@ def run(args):
     h.set_stream(stream.cuda_stream)
     sharded = []
     fused = world > 1 and args.exchange != "allgather"
+    any_shard = True
     if world > 1:
-        from macuda_b200.dist import FusedShardedGemm, ShardedGemm, step_barrier
+        from macuda_b200.dist import FusedShardedGemm, ReplicatedGemm, ShardedGemm, pick_fastest, step_barrier
         for L in layers:
             if fused:
-                sharded.append(FusedShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype,
-                                                exchange={"fused": "p2p"}.get(args.exchange, args.exchange)))
+                # N-sharded (rows exchanged by the epilogue) or whole on every rank (nothing exchanged): the
+                # faster of the two, timed on every rank (max over ranks) during set-up
+                cands = {"sharded": FusedShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype,
+                                                     exchange={"fused": "p2p"}.get(args.exchange, args.exchange)),
+                         "whole": ReplicatedGemm(lib, h, L["m"], TOKENS, L["k"], L["w_full"], ctype)}
+                choice = pick_fastest(cands, acts[L["src"]], stream) if args.shard == "auto" else args.shard
+                for key, c in cands.items():
+                    if key != choice:
+                        c.close()
+                sharded.append(cands[choice])
             else:
                 sharded.append(ShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype))
+        any_shard = any(getattr(g, "exchange", "allgather") != "replicated" for g in sharded)
+    for L in layers:
+        L.pop("w_full", None)  # whole weights stay only where a projection runs whole on every rank
     # Inside the timed region the only events are the two around the dominant GEMM (lm_head, the roofline
     # kernel): an event between two kernels would also stop the next one from being scheduled while the
     # previous one finishes (programmatic dependent launch). The per-projection breakdown comes from a
@@ -456,9 +469,9 @@ def run(args):
                 ev[i + 1].record(stream)
             if st != 0:
                 raise RuntimeError(f"{L['name']}: status {st}")
-        if fused:
+        if fused and any_shard:
             step_barrier(stream)  # every peer's stores into this rank's C have landed
-        elif world > 1:
+        elif world > 1 and not fused:
             stream.wait_stream(comm)
 
     # warm-up
@@ -561,9 +574,9 @@ def run(args):
                 st = sharded[j].run(act, stream, comm)
             if st != 0:
                 raise RuntimeError("e2e gemm failed")
-        if fused:
+        if fused and any_shard:
             step_barrier(stream)
-        elif world > 1:
+        elif world > 1 and not fused:
             stream.wait_stream(comm)
         free[b].record(stream)
         c_lm = lm["c_local"] if world == 1 else sharded[dom].c
@@ -619,11 +632,15 @@ def run(args):
             "dtype": args.dtype, "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) activations; no checkpoint)",
             "config": {"workload": "llama3.1-8b prefill projections q,k,v,o,gate,up,down,lm_head @ 512 tokens "
                                    "(BASELINE configs[1])", "tokens": TOKENS, "step_gflop": round(STEP_FLOP / 1e9, 1),
-                       "parallelism": (f"N-shard x{world}, C exchanged by " + (
-                                       ("NVLink multicast stores" if sharded[0].exchange == "multicast" else
-                                        "P2P stores over NVLink") + " from the GEMM epilogue + one NCCL barrier per "
-                                       "step" if fused else "NCCL all-gather + layout kernel")) if world > 1
-                                       else "single GPU",
+                       "parallelism": ((f"x{world}: " + ", ".join(
+                                           f"{L['name']} " + ("whole on every rank" if g.exchange == "replicated"
+                                                              else "N-sharded, rows exchanged by " +
+                                                              ("NVLink multicast" if g.exchange == "multicast" else
+                                                               "P2P") + " stores from the GEMM epilogue")
+                                           for L, g in zip(layers, sharded)) +
+                                        ("; one NCCL barrier per step" if any_shard else "")) if fused else
+                                       f"N-shard x{world}, C exchanged by NCCL all-gather + layout kernel")
+                                      if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (1.9 GB per step); no flush"},
             "frac_of_peak": round(value / pk["bf16_tflops_sustained"], 4),
             "roofline": roofline, "shapes": shapes,
@@ -676,6 +693,9 @@ def main():
     ap.add_argument("--no-configs", action="store_true", help="skip the config 3 and 5 figures")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--gemm", default=None, help="MxNxK: time one T,N GEMM alone (profiling)")
+    ap.add_argument("--shard", choices=["auto", "sharded", "whole"], default="auto",
+                    help="N > 1, fused exchange: per projection N-sharded or whole on every rank (auto: the faster, "
+                         "timed on every rank at set-up)")
     ap.add_argument("--exchange", choices=["fused", "multicast", "p2p", "allgather"], default="fused",
                     help="N > 1: how the sharded C is replicated (fused = p2p stores from the epilogue)")
     args = ap.parse_args()

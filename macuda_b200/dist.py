@@ -218,3 +218,56 @@ def step_barrier(stream, group=None, _flag={}):
         _flag[dev] = torch.zeros(1, dtype=torch.int32, device="cuda")
     with torch.cuda.stream(stream):
         dist.all_reduce(_flag[dev], group=group)
+
+
+class ReplicatedGemm:
+    """The whole GEMM on this rank (the full weight, the full C): every rank computes the same C and nothing
+    is exchanged. For projections whose shards would be too small to use the GPU, or whose C costs more to
+    exchange than to compute again (see pick_fastest)."""
+
+    exchange = "replicated"
+
+    def __init__(self, lib, handle, m: int, n: int, k: int, w_full, dtype_code: int):
+        import torch
+        self.lib, self.h = lib, handle
+        self.m, self.n, self.k = m, n, k
+        self.w = w_full
+        self.dtype_code = dtype_code
+        self.c = torch.empty(m * n, device="cuda", dtype=torch.float32)
+
+    def run(self, x, stream=None) -> int:
+        from . import cublas as cb
+        return self.h.gemm_ex(cb.CUBLAS_OP_T, cb.CUBLAS_OP_N, self.m, self.n, self.k, 1.0, self.w.data_ptr(),
+                              self.dtype_code, self.k, x.data_ptr(), self.dtype_code, self.k, 0.0, self.c.data_ptr(),
+                              cb.CUDA_R_32F, self.m, cb.CUBLAS_COMPUTE_32F)
+
+    def close(self):
+        self.c = None
+
+
+def pick_fastest(candidates: dict, x, stream, group=None, warmup: int = 3, iters: int = 10) -> str:
+    """Time each candidate's run(x, stream) on this rank (CUDA events around `iters` back-to-back calls after
+    `warmup`), take the maximum over ranks, and return the key of the fastest: the same on every rank.
+    Every rank must call it with the same candidates in the same order."""
+    import torch
+    import torch.distributed as dist
+    keys = list(candidates)
+    times = torch.zeros(len(keys), dtype=torch.float64, device="cuda")
+    for i, key in enumerate(keys):
+        c = candidates[key]
+        for _ in range(warmup):
+            if c.run(x, stream) != 0:
+                raise RuntimeError(f"{key}: GEMM failed")
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(iters):
+            c.run(x, stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        times[i] = e0.elapsed_time(e1) / iters
+        dist.barrier(group=group)  # peers' stores into this rank's buffers are done before the next candidate
+    dist.all_reduce(times, op=dist.ReduceOp.MAX, group=group)
+    return keys[int(torch.argmin(times).item())]
+
