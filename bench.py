@@ -323,6 +323,46 @@ def config_figures(torch, lib, cb, dtype_code, dtype):
             dtype_code, Hd, 0.0, Call.data_ptr(), f32, Fe), 10, flop5,
             (used * Fe * Hd + Xe.numel()) * 2 + Call.numel() * 4, "hbm")
         out[f"c5_moe_gate_up_grouped_{label}"]["experts_with_tokens"] = used
+    if grouped:
+        # a routed layer end to end with the skewed routing, top-8 over 128 experts for 512 tokens: tokens
+        # gathered into expert order, up projection (all experts, one launch), down projection (its 16-bit
+        # input stands in for the activation's output), outputs combined back per token with the weights
+        T, topk = 512, 8
+        rng = np.random.default_rng(7)
+        share = rng.dirichlet(np.full(E, 0.3))
+        ex = np.stack([rng.choice(E, topk, replace=False, p=share) for _ in range(T)]).astype(np.int32)
+        wts = rng.uniform(0.1, 1.0, (T, topk)).astype(np.float32)
+        wts /= wts.sum(axis=1, keepdims=True)
+        order = np.argsort(ex.ravel(), kind="stable")
+        pos = np.empty(T * topk, np.int32)
+        pos[order] = np.arange(T * topk, dtype=np.int32)
+        offs = torch.from_numpy(np.concatenate([[0], np.cumsum(np.bincount(ex.ravel(), minlength=E))])
+                                .astype(np.int32)).cuda()
+        ids = torch.from_numpy((order // topk).astype(np.int32)).cuda()
+        d_pos, d_w = torch.from_numpy(pos).cuda(), torch.from_numpy(wts.ravel().copy()).cuda()
+        Xtok = rnd(T, Hd)
+        Xp = torch.empty(T * topk, Hd, device="cuda", dtype=dtype)
+        Cup = torch.empty(T * topk * Fe, device="cuda")
+        Hp = rnd(T * topk, Fe)
+        Cdn = torch.empty(T * topk * Hd, device="cuda")
+        Y = torch.empty(T * Hd, device="cuda")
+        n_tot = T * topk
+        used = int(np.count_nonzero(np.bincount(ex.ravel(), minlength=E)))
+
+        def layer():
+            st = lib.lib.tb200_moe_gather(h.h, Xtok.data_ptr(), dtype_code, Hd, Hd, T, ids.data_ptr(), n_tot,
+                                          Xp.data_ptr(), Hd)
+            st = st or h.gemm_grouped_ex(1, 0, Fe, n_tot, Hd, E, offs.data_ptr(), 1.0, Wgu.data_ptr(), dtype_code, Hd,
+                                         Fe * Hd, Xp.data_ptr(), dtype_code, Hd, 0.0, Cup.data_ptr(), f32, Fe)
+            st = st or h.gemm_grouped_ex(1, 0, Hd, n_tot, Fe, E, offs.data_ptr(), 1.0, Wd.data_ptr(), dtype_code, Fe,
+                                         Hd * Fe, Hp.data_ptr(), dtype_code, Fe, 0.0, Cdn.data_ptr(), f32, Hd)
+            return st or lib.lib.tb200_moe_combine(h.h, Hd, Cdn.data_ptr(), Hd, n_tot, d_pos.data_ptr(),
+                                                   d_w.data_ptr(), topk, T, Y.data_ptr(), Hd)
+        layer_bytes = (2 * used * Fe * Hd + T * Hd + 2 * n_tot * Hd + n_tot * Fe) * 2 + (n_tot * (Fe + 2 * Hd)
+                                                                                          + T * Hd) * 4
+        measure("c5_moe_routed_layer_skewed", layer, 10, 2 * flop5, layer_bytes, "hbm")
+        out["c5_moe_routed_layer_skewed"]["experts_with_tokens"] = used
+        out["c5_moe_routed_layer_skewed"]["launches"] = "gather + grouped up + grouped down + combine"
     del Wgu, Wd, Xe, He, Cgu, Cd, Xall, Call
 
     # config 5 squares, both 16-bit input types

@@ -137,6 +137,20 @@ cublasStatus_t tb200_gemm_grouped_ex(cublasHandle_t handle, cublasOperation_t tr
                                      cudaDataType Btype, int ldb, const void *beta, void *C, cudaDataType Ctype,
                                      int ldc, cublasComputeType_t computeType);
 
+/* The data movement of a routed mixture-of-experts layer around tb200_gemm_grouped_ex, on the handle's
+ * stream, deterministic, no allocation. tb200_moe_gather: column p of Xp (ld ldxp) = column token_ids[p] of X
+ * (k elements of `type`, ld ldx, n_src columns) for p < n_total, which lays out each expert's tokens one
+ * expert after another (token_ids device array; an id outside [0, n_src) gives a zero column).
+ * tb200_moe_combine: column t of Y (f32, ld ldy) = sum over j < topk, in j order, of
+ * weights[t * topk + j] * column positions[t * topk + j] of Cp (f32, ld ldc, n_total columns) for
+ * t < n_tokens (device arrays; a position outside [0, n_total) contributes nothing). No counterpart in the
+ * reference. */
+cublasStatus_t tb200_moe_gather(cublasHandle_t handle, const void *X, cudaDataType type, int k, int ldx, int n_src,
+                                const int *token_ids, int n_total, void *Xp, int ldxp);
+cublasStatus_t tb200_moe_combine(cublasHandle_t handle, int m, const float *Cp, int ldc, int n_total,
+                                 const int *positions, const float *weights, int topk, int n_tokens, float *Y,
+                                 int ldy);
+
 /* The persistent tensor-core kernel's tile choice for an m x n x batch GEMM on `num_sms` SMs: returns the
  * tile width (32, 64, 128 or 256) and sets *pair (if not NULL) to 1 for the 256 x 256 tile of a CTA pair.
  * Pure function, pinned by host-only tests. */

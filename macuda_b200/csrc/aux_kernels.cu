@@ -107,6 +107,66 @@ extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_gather_ro
   return cudaGetLastError() == cudaSuccess ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
 }
 
+// ---- mixture of experts: tokens into expert order, and expert outputs back to tokens ----------------
+// Xp column p = X column ids[p] (row_bytes bytes each; ld in bytes): one warp per column, 16-byte copies
+// when every address and stride allows, else bytes. An id outside [0, n_src) gives a zero column.
+__global__ void tb200_moe_gather_kernel(const char *X, long long ldx, int n_src, const int *ids, int n_total,
+                                        int row_bytes, char *Xp, long long ldp, int vec) {
+  const int lane = threadIdx.x & 31;
+  const long long warps = (long long)gridDim.x * (blockDim.x >> 5);
+  for (long long p = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); p < n_total; p += warps) {
+    const int t = ids[p];
+    const bool ok = t >= 0 && t < n_src;
+    char *dst = Xp + p * ldp;
+    const char *src = X + (ok ? (long long)t * ldx : 0);
+    if (vec) {
+      for (int o = lane * 16; o < row_bytes; o += 32 * 16)
+        *(uint4 *)(dst + o) = ok ? __ldg((const uint4 *)(src + o)) : make_uint4(0, 0, 0, 0);
+    } else {
+      for (int o = lane; o < row_bytes; o += 32) dst[o] = ok ? src[o] : 0;
+    }
+  }
+}
+
+// Y column t = sum over j < topk, in j order, of w[t * topk + j] * Cp column pos[t * topk + j] (m f32 rows);
+// a position outside [0, n_total) contributes nothing. Deterministic: no atomics.
+__global__ void tb200_moe_combine_kernel(const float *Cp, int m, long long ldc, int n_total, const int *pos,
+                                         const float *w, int topk, int n_tokens, float *Y, long long ldy) {
+  const long long rows_blocks = (m + blockDim.x - 1) / blockDim.x;
+  for (long long bt = blockIdx.x; bt < rows_blocks * n_tokens; bt += gridDim.x) {
+    const int t = (int)(bt / rows_blocks);
+    const int row = (int)(bt % rows_blocks) * blockDim.x + threadIdx.x;
+    if (row >= m) continue;
+    float acc = 0.f;
+    for (int j = 0; j < topk; ++j) {
+      const int p = pos[(long long)t * topk + j];
+      if (p >= 0 && p < n_total) acc = fmaf(w[(long long)t * topk + j], Cp[row + (long long)p * ldc], acc);
+    }
+    Y[row + (long long)t * ldy] = acc;
+  }
+}
+
+extern "C" int tb200_launch_moe_gather(const void *X, long long ldx_bytes, int n_src, const int *ids, int n_total,
+                                       int row_bytes, void *Xp, long long ldp_bytes, cudaStream_t s) {
+  if (n_total <= 0 || row_bytes <= 0) return 0;
+  const int vec = ((((uintptr_t)X) | ((uintptr_t)Xp)) & 15) == 0 && ldx_bytes % 16 == 0 && ldp_bytes % 16 == 0 &&
+                  row_bytes % 16 == 0;
+  const unsigned blocks = (unsigned)((n_total + 7) / 8 < 4096 ? (n_total + 7) / 8 : 4096);  // 8 warps per block
+  tb200_moe_gather_kernel<<<blocks, 256, 0, s>>>((const char *)X, ldx_bytes, n_src, ids, n_total, row_bytes,
+                                                 (char *)Xp, ldp_bytes, vec);
+  return (int)cudaGetLastError();
+}
+
+extern "C" int tb200_launch_moe_combine(const float *Cp, int m, long long ldc, int n_total, const int *pos,
+                                        const float *w, int topk, int n_tokens, float *Y, long long ldy,
+                                        cudaStream_t s) {
+  if (m <= 0 || n_tokens <= 0) return 0;
+  const long long work = (long long)((m + 255) / 256) * n_tokens;
+  const unsigned blocks = (unsigned)(work < 8192 ? work : 8192);
+  tb200_moe_combine_kernel<<<blocks, 256, 0, s>>>(Cp, m, ldc, n_total, pos, w, topk, n_tokens, Y, ldy);
+  return (int)cudaGetLastError();
+}
+
 extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_bw_write(void *p, long long n4, float v, cudaStream_t stream) {
   if (n4 <= 0) return CUBLAS_STATUS_SUCCESS;
   tb200_bw_write_kernel<<<grid_for(n4, 256), 256, 0, stream>>>((float4 *)p, n4, v);

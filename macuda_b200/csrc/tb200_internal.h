@@ -59,6 +59,13 @@ int tb200_launch_tc_ptr_noalloc(const tb200_gemm_t *g, int tile_n, int pair, int
 int tb200_launch_trsm_rupn(const float *const *A, float *const *B, int rows, int n, int lda, int ldb, float alpha,
                            int batch, cudaStream_t s);
 
+/* mixture-of-experts data movement (aux_kernels.cu): columns gathered into expert order; expert outputs
+ * combined back into token order with the routing weights */
+int tb200_launch_moe_gather(const void *X, long long ldx_bytes, int n_src, const int *ids, int n_total, int row_bytes,
+                            void *Xp, long long ldp_bytes, cudaStream_t s);
+int tb200_launch_moe_combine(const float *Cp, int m, long long ldc, int n_total, const int *pos, const float *w,
+                             int topk, int n_tokens, float *Y, long long ldy, cudaStream_t s);
+
 /* properties of the current device, cached per device ordinal */
 int tb200_num_sms(void);
 

@@ -615,6 +615,39 @@ cublasStatus_t tb200_gemm_grouped_ex(cublasHandle_t handle, cublasOperation_t tr
   return CUBLAS_STATUS_SUCCESS;
 }
 
+/* The routed layer's data movement around tb200_gemm_grouped_ex: tb200_moe_gather copies column
+ * token_ids[p] of X (k elements of `type`, ld ldx, n_src columns) to column p of Xp (ld ldxp) for every
+ * p < n_total, putting each expert's tokens one expert after another; tb200_moe_combine sums, for every
+ * token t, weights[t * topk + j] * column positions[t * topk + j] of Cp over j in order into column t of Y
+ * (f32). Ids and positions outside their range contribute zeros. On the handle's stream; no allocation. */
+cublasStatus_t tb200_moe_gather(cublasHandle_t handle, const void *X, cudaDataType type, int k, int ldx, int n_src,
+                                const int *token_ids, int n_total, void *Xp, int ldxp) {
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  const int code = dtype_code(type);
+  if (code < 0) return CUBLAS_STATUS_NOT_SUPPORTED;
+  if (k < 0 || n_src < 0 || n_total < 0 || ldx < (k > 1 ? k : 1) || ldxp < (k > 1 ? k : 1)) return CUBLAS_STATUS_INVALID_VALUE;
+  if (k == 0 || n_total == 0) return CUBLAS_STATUS_SUCCESS;
+  if (!X || !token_ids || !Xp) return CUBLAS_STATUS_INVALID_VALUE;
+  const int es = code == TB200_F32 ? 4 : 2;
+  int rc = tb200_launch_moe_gather(X, (long long)ldx * es, n_src, token_ids, n_total, k * es, Xp, (long long)ldxp * es,
+                                   h->stream);
+  return rc == 0 ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
+cublasStatus_t tb200_moe_combine(cublasHandle_t handle, int m, const float *Cp, int ldc, int n_total,
+                                 const int *positions, const float *weights, int topk, int n_tokens, float *Y,
+                                 int ldy) {
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  if (m < 0 || n_total < 0 || topk < 0 || n_tokens < 0 || ldc < (m > 1 ? m : 1) || ldy < (m > 1 ? m : 1))
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (m == 0 || n_tokens == 0) return CUBLAS_STATUS_SUCCESS;
+  if (!Cp || !positions || !weights || !Y) return CUBLAS_STATUS_INVALID_VALUE;
+  int rc = tb200_launch_moe_combine(Cp, m, ldc, n_total, positions, weights, topk, n_tokens, Y, ldy, h->stream);
+  return rc == 0 ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
+}
+
 /* cublasGemmBatchedEx without any device allocation: same arguments, same results; where the pointer-array
  * tensor-core path needs scratch it takes the library's fixed device array (tb200_launch_tc_ptr_noalloc)
  * instead of the handle's lazily allocated buffer. batchCount is bounded by that array. */

@@ -96,6 +96,8 @@ EXTENSIONS = [
     ("tb200_noalloc_max_batch", _i, []),
     ("tb200_gemm_grouped_ex", _i,
      [_vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _ll, _vp, _i, _i, _vp, _vp, _i, _i, _i]),
+    ("tb200_moe_gather", _i, [_vp, _vp, _i, _i, _i, _i, _vp, _i, _vp, _i]),
+    ("tb200_moe_combine", _i, [_vp, _i, _vp, _i, _i, _vp, _vp, _i, _i, _vp, _i]),
 ]
 
 
