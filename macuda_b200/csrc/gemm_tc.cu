@@ -6,23 +6,35 @@
 // (cuda-shim/libtinycublas/gemm.cu:241-415) and the first-cut tinyblas_gemm_f16_tc / f32_tc
 // (gemm.cu:61-221) for every aligned operand.
 //
-// Shape of one CTA (one per SM, persistent over output tiles of 128 x BN):
-//   warp 0      TMA producer: one thread streams A and B k-blocks (128-byte rows, 128B swizzle)
-//               into a STAGES-deep shared-memory ring, signalling full[s] by transaction count.
-//   warp 1      owns tensor memory (allocates 2*BN columns: two accumulators) and one thread issues
-//               tcgen05.mma for each k-block, then tcgen05.commit frees the smem stage (empty[s]);
-//               after a tile's last k-block a commit publishes the accumulator (tfull[a]).
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time from the accumulator, apply
-//               alpha/beta, convert, store straight to column-major C (consecutive lanes hold
-//               consecutive rows, so every store instruction of a warp is contiguous), then release
-//               the accumulator (tempty[a]) so the MMA warp can start the tile after next.
+// Shape of one CTA (224 threads, one per SM, persistent over output tiles):
+//   warp 0      TMA producer of A, warp 6 TMA producer of B: one thread each streams its operand's k-blocks
+//               (128-byte rows, 128B swizzle) into a STAGES-deep shared-memory ring; the bytes complete
+//               full[s] by transaction count.
+//   warp 1      owns tensor memory (2 x BN columns: two accumulators); one thread issues tcgen05.mma for
+//               each k-block, then tcgen05.commit frees the smem stage (empty[s]); after a tile's last
+//               k-block a commit publishes the accumulator (tfull[a]).
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time from the accumulator, apply alpha/beta,
+//               convert, store straight to column-major C (consecutive lanes hold consecutive rows, so every
+//               store instruction of a warp is contiguous), then release the accumulator (tempty[a]).
 // The two accumulators let the epilogue of tile i overlap the main loop of tile i+1.
+//
+// Tiles: 128 x BN on one CTA (BN 32..256), or 256 x BN (BN 128 or 256) on a cluster of two CTAs with
+// tcgen05.mma.cta_group::2 (each CTA loads its 128 rows of A and half of B's BN columns; the even CTA's
+// MMA thread drives both tensor cores; each CTA drains its own rows). Work units, walked identically by
+// every role: output tiles of a plain GEMM, of a strided batch (rank-3 tensor maps, batch = third
+// coordinate; stride 0 broadcasts) or of a pointer-array batch (per-element maps written on the device by
+// tb200_ptr_maps_kernel), or the per-expert tiles of a grouped GEMM (tile_coord). The epilogue can also
+// store each tile into several replicas of C (peers' memory over NVLink) or to an NVLink multicast
+// address: the N-sharded GEMM's exchange.
 //
 // Operand layouts (no transposes materialised): op(A) is K-major when A is stored k x m (op T, the
 // ggml call) and MN-major when stored m x k (op N); op(B) is K-major when B is stored k x n (op N)
 // and MN-major when stored n x k (op T). Both majors are fed to the tensor core through the
-// instruction descriptor's major bits and matching smem descriptors. Strided batches use rank-3
-// tensor maps (batch = third coordinate); a stride of 0 broadcasts through a rank-2 map.
+// instruction descriptor's major bits and matching smem descriptors.
+//
+// Every wait is bounded (an abort flag, an error word, drained copies, freed tensor memory), and the
+// kernel is launched with programmatic stream serialization: its set-up overlaps the previous kernel's
+// tail and its first memory access waits in griddepcontrol.wait.
 //
 // No TMA multicast anywhere: every CTA loads its own tiles, and L2 absorbs the reuse.
 #include <cuda.h>
