@@ -213,12 +213,13 @@ def decode_figures(torch, lib, cb, dtype_code, dtype):
     return out
 
 
-def config_figures(torch, lib, cb, dtype_code, dtype):
+def config_figures(torch, lib, cb, dtype_code, dtype, only=None, reps_override=None):
     """Configs 3 and 5: attention batched GEMMs (strided with the GQA heads folded into n, and pointer arrays
     with each KV head's pointer repeated for its 4 query heads), MoE expert GEMMs (pointer arrays over 128
     experts, 32 tokens each) and square GEMMs, all T,N with f32 C as ggml issues them. Per case: device
     time (CUDA events around back-to-back calls, median of 3 repeats), TFLOP/s, compulsory bytes / time, and
-    the fraction of the measured peak of its bound (HBM copy bandwidth, or burst bf16 tensor throughput)."""
+    the fraction of the measured peak of its bound (HBM copy bandwidth, or burst bf16 tensor throughput).
+    only: run just the case of that name (bench.py --case, for profiling one kernel)."""
     pk = peaks()
     out = {}
     h = lib.handle()
@@ -233,6 +234,10 @@ def config_figures(torch, lib, cb, dtype_code, dtype):
         return torch.tensor(ptrs, dtype=torch.int64, device="cuda")
 
     def measure(name, call, reps, flop, byts, bound):
+        if only is not None and name != only:
+            return
+        if reps_override:
+            reps = reps_override
         for _ in range(2):
             st = call()
             if st != 0:
@@ -322,7 +327,8 @@ def config_figures(torch, lib, cb, dtype_code, dtype):
             1, 0, Fe, E * Te, Hd, E, offs.data_ptr(), 1.0, Wgu.data_ptr(), dtype_code, Hd, Fe * Hd, Xall.data_ptr(),
             dtype_code, Hd, 0.0, Call.data_ptr(), f32, Fe), 10, flop5,
             (used * Fe * Hd + Xe.numel()) * 2 + Call.numel() * 4, "hbm")
-        out[f"c5_moe_gate_up_grouped_{label}"]["experts_with_tokens"] = used
+        if f"c5_moe_gate_up_grouped_{label}" in out:
+            out[f"c5_moe_gate_up_grouped_{label}"]["experts_with_tokens"] = used
     if grouped:
         # a routed layer end to end with the skewed routing, top-8 over 128 experts for 512 tokens: tokens
         # gathered into expert order, up projection (all experts, one launch), down projection (its 16-bit
@@ -361,12 +367,13 @@ def config_figures(torch, lib, cb, dtype_code, dtype):
         layer_bytes = (2 * used * Fe * Hd + T * Hd + 2 * n_tot * Hd + n_tot * Fe) * 2 + (n_tot * (Fe + 2 * Hd)
                                                                                           + T * Hd) * 4
         measure("c5_moe_routed_layer_skewed", layer, 10, 2 * flop5, layer_bytes, "hbm")
-        out["c5_moe_routed_layer_skewed"]["experts_with_tokens"] = used
-        out["c5_moe_routed_layer_skewed"]["launches"] = "gather + grouped up + grouped down + combine"
+        if "c5_moe_routed_layer_skewed" in out:
+            out["c5_moe_routed_layer_skewed"]["experts_with_tokens"] = used
+            out["c5_moe_routed_layer_skewed"]["launches"] = "gather + grouped up + grouped down + combine"
     del Wgu, Wd, Xe, He, Cgu, Cd, Xall, Call
 
     # config 5 squares, both 16-bit input types
-    for S in (4096, 8192, 16384):
+    for S in (4096, 8192, 16384) if only is None or only.startswith("c5_square") else ():
         for tname, tdt, tcode in (("f16", torch.float16, cb.CUDA_R_16F), ("bf16", torch.bfloat16, cb.CUDA_R_16BF)):
             A = (torch.randn(S, S, device="cuda") * 0.02).to(tdt)
             B = torch.randn(S, S, device="cuda").to(tdt)
@@ -378,6 +385,25 @@ def config_figures(torch, lib, cb, dtype_code, dtype):
     torch.cuda.empty_cache()
     h.close()
     return out
+
+
+def run_case(args):
+    """--case NAME: one config 3/5 figure alone (its inputs, 2 warm-up calls, 3 x --steps timed calls)."""
+    import torch
+    from macuda_b200 import cublas as cb
+    if args.impl == "reference":
+        from oracle import oracle as O
+        lib = O.reference_library()
+    else:
+        lib = cb.library()
+    dtype = torch.float16 if args.dtype == "f16" else torch.bfloat16
+    ctype = cb.CUDA_R_16F if args.dtype == "f16" else cb.CUDA_R_16BF
+    out = config_figures(torch, lib, cb, ctype, dtype, only=args.case, reps_override=args.steps)
+    if args.case not in out:
+        print(json.dumps({"case": args.case, "error": "no such case (see configs_3_5 in a full run)"}))
+        return 1
+    print(json.dumps({"case": args.case, "impl": args.impl, **out[args.case]}))
+    return 0
 
 
 def run_single(args):
@@ -733,6 +759,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true", help="skip the config 3 and 5 figures")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--gemm", default=None, help="MxNxK: time one T,N GEMM alone (profiling)")
+    ap.add_argument("--case", default=None, help="run one config 3/5 figure alone, by its name in configs_3_5 "
+                                                 "(profiling); --steps sets its back-to-back calls")
     ap.add_argument("--shard", choices=["auto", "sharded", "whole"], default="auto",
                     help="N > 1, fused exchange: per projection N-sharded or whole on every rank (auto: the faster, "
                          "timed on every rank at set-up)")
@@ -743,6 +771,8 @@ def main():
         args.warmup = 3
     if args.gemm:
         return run_single(args)
+    if args.case:
+        return run_case(args)
     return run(args)
 
 
