@@ -7,7 +7,9 @@ Each .cu file is compiled by nvcc for sm_100a only (-gencode arch=compute_100a,c
 host layer by gcc against CUDA's own cublas_v2.h, and everything is linked into one shared library
 with the static CUDA runtime. A linker version script exports exactly the cuBLAS ABI subset and the
 documented tb200_* extensions; -Bsymbolic binds the library's internal calls to its own definitions
-even when the process has also loaded NVIDIA's libcublas (as PyTorch does).
+even when the process has also loaded NVIDIA's libcublas (as PyTorch does). The static symbol table is
+stripped (the exported dynamic symbols stay): it names nvcc's temporary files, whose names carry a
+process id, and without it two builds of the same sources are byte-identical (tests/test_build.py).
 """
 from __future__ import annotations
 
@@ -56,39 +58,42 @@ def _stale(outputs: list[str], inputs: list[str]) -> bool:
     return newest_in > oldest_out
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    """Compile and link the library if needed; returns its path."""
+def build(force: bool = False, verbose: bool = False, lib_path: str = None, build_dir: str = None) -> str:
+    """Compile and link the library if needed; returns its path. lib_path / build_dir put a build somewhere
+    else than the package (the reproducible-build test builds a second copy and compares the bytes)."""
+    LIB_OUT = lib_path or LIB
+    BUILD_DIR = build_dir or BUILD
     srcs = [os.path.join(CSRC, f) for f in CU_SOURCES + C_SOURCES + HEADERS]
     srcs.append(os.path.join(ROOT, "include", "tinycublas_b200.h"))
     srcs.append(os.path.abspath(__file__))
-    if not force and not _stale([LIB], srcs):
-        return LIB
+    if not force and not _stale([LIB_OUT], srcs):
+        return LIB_OUT
     if shutil.which(NVCC) is None and not os.path.exists(NVCC):
         raise RuntimeError(f"nvcc not found at {NVCC}")
-    os.makedirs(BUILD, exist_ok=True)
+    os.makedirs(BUILD_DIR, exist_ok=True)
     inc = ["-I", CSRC, "-I", os.path.join(ROOT, "include"), "-I", os.path.join(CUDA_HOME, "include")]
     jobs = []
     for f in CU_SOURCES:
-        obj = os.path.join(BUILD, f + ".o")
+        obj = os.path.join(BUILD_DIR, f + ".o")
         cmd = [NVCC, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
                "--expt-relaxed-constexpr", *inc, "-c", os.path.join(CSRC, f), "-o", obj]
         if verbose:
             cmd.insert(1, "-Xptxas=-v")
         jobs.append((cmd, obj))
     for f in C_SOURCES:
-        obj = os.path.join(BUILD, f + ".o")
+        obj = os.path.join(BUILD_DIR, f + ".o")
         cmd = ["gcc", "-O2", "-fPIC", "-std=c11", "-Wall", "-Wextra", "-Wno-unused-parameter",
                f'-DTB200_GIT_DESCRIBE="{_git_describe()}"', *inc, "-c", os.path.join(CSRC, f), "-o", obj]
         jobs.append((cmd, obj))
     with cf.ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         list(ex.map(lambda j: _run(j[0]), jobs))
-    tmp = LIB + ".tmp"
+    tmp = LIB_OUT + ".tmp"
     link = [NVCC, *ARCH, "-shared", "-cudart", "static", "-o", tmp, *[o for _, o in jobs],
             "-Xlinker", "-Bsymbolic", "-Xlinker", "--version-script=" + os.path.join(CSRC, "exports.map"),
-            "-Xlinker", "--no-undefined", "-lpthread", "-ldl", "-lrt"]
+            "-Xlinker", "--no-undefined", "-Xlinker", "--strip-all", "-lpthread", "-ldl", "-lrt"]
     _run(link)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, LIB_OUT)
+    return LIB_OUT
 
 
 if __name__ == "__main__":
