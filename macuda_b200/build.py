@@ -71,6 +71,7 @@ def build(force: bool = False, verbose: bool = False, lib_path: str = None, buil
     if shutil.which(NVCC) is None and not os.path.exists(NVCC):
         raise RuntimeError(f"nvcc not found at {NVCC}")
     os.makedirs(BUILD_DIR, exist_ok=True)
+    os.makedirs(os.path.dirname(os.path.abspath(LIB_OUT)), exist_ok=True)
     inc = ["-I", CSRC, "-I", os.path.join(ROOT, "include"), "-I", os.path.join(CUDA_HOME, "include")]
     jobs = []
     for f in CU_SOURCES:
