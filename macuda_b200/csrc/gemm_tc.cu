@@ -179,15 +179,21 @@ __device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *tm
   }
 }
 
+// KS = 2 (with CG = 1): a cluster of two CTAs per 128 x BN tile, one tile per cluster, each CTA with its own
+// half of the k-blocks and its own accumulator. The second CTA parks its partial sums in its idle operand ring
+// and the first reads them over distributed shared memory, adds them to its own in that order, and stores
+// C: the k-loop halves without a global workspace.
 // CG = 1: one CTA per 128 x BN tile. CG = 2: a cluster of two CTAs per 256 x BN tile (2-SM UMMA): each
 // CTA loads its 128 rows of A and BN/2 rows of B, the even CTA's MMA thread drives both tensor cores,
 // and each CTA's epilogue drains its own 128 rows from its own tensor memory.
-template <int KIND, int BN, int KC, int CG>
+template <int KIND, int BN, int KC, int CG, int KS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tb200_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const TcParams p) {
   using Cfg = TcCfg<BN, KC, CG>;
   constexpr int STAGES = Cfg::STAGES;
+  static_assert(KS == 1 || (CG == 1 && STAGES * Cfg::STAGE_BYTES >= TC_BM * BN * 4),
+                "k split: the operand ring must hold a 128 x BN f32 tile of partial sums");
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment of the shared-window offset: the 128B swizzle atom is 8 rows x 128 bytes. The
   // offset is the same in both CTAs of a pair, as the 2-SM UMMA requires.
@@ -200,7 +206,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t *tfull = bars + 2 * STAGES;
   uint64_t *tempty = tfull + 2;
   uint64_t *drain = tempty + 2;
-  uint32_t *tmem_slot = (uint32_t *)(drain + 1);
+  uint64_t *xfull = drain + 1;  // KS = 2, first CTA: the partner's partial sums are parked
+  uint64_t *xdone = drain + 2;  // KS = 2, second CTA: the first has read them
+  uint32_t *tmem_slot = (uint32_t *)(drain + 3);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
   int *g_off = (int *)((uint8_t *)bars + Cfg::BAR_BYTES);  // grouped GEMM: clamped column offsets ...
   int *g_pre = g_off + TC_MAX_GROUPS + 1;                  // ... and tile-count prefix
@@ -213,11 +221,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const uint32_t rank = CG == 2 ? cluster_ctarank() : 0u;
+  constexpr bool CL2 = CG == 2 || KS == 2;  // launched in clusters of two CTAs
+  const uint32_t crank = CL2 ? cluster_ctarank() : 0u;
+  const uint32_t rank = CG == 2 ? crank : 0u;     // the CTA's half of a pair tile's rows
+  const uint32_t kslice = KS == 2 ? crank : 0u;  // the CTA's half of the k-blocks
   const bool leader = rank == 0;
-  // tile index stream: one per CTA, or one per pair
-  const long long t_first = CG == 2 ? (long long)(blockIdx.x >> 1) : (long long)blockIdx.x;
-  const long long t_step = CG == 2 ? (long long)(gridDim.x >> 1) : (long long)gridDim.x;
+  // tile index stream: one per CTA, or one per cluster
+  const long long t_first = CL2 ? (long long)(blockIdx.x >> 1) : (long long)blockIdx.x;
+  const long long t_step = CL2 ? (long long)(gridDim.x >> 1) : (long long)gridDim.x;
+  const int kb_lo = KS == 2 ? (int)((long long)kslice * p.num_kb / 2) : 0;
+  const int kb_hi = KS == 2 ? (int)((long long)(kslice + 1) * p.num_kb / 2) : p.num_kb;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -229,6 +242,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&tempty[a], 4 * CG);  // every epilogue warp of the tile
     }
     mbar_init(drain, 1);
+    mbar_init(xfull, 128);  // every epilogue thread of the partner
+    mbar_init(xdone, 4);    // every epilogue warp of the first CTA
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -245,7 +260,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   tc_fence_before();
   __syncwarp();                 // barrier.cluster.*.aligned wants every warp converged
-  if (CG == 2) cluster_sync();  // the peer's loads and arrivals target the even CTA's barriers: all initialised
+  if (CL2) cluster_sync();  // the partner's loads and arrivals target this CTA's barriers: all initialised
   else __syncthreads();
   tc_fence_after();
   // Everything above touched only this CTA's own resources and the kernel parameters, and may overlap the
@@ -304,7 +319,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           tm = p.maps + 2 * b + (is_a ? 0 : 1);
           fence_tensormap_acquire(tm);
         }
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, WAIT_BUDGET_CYC)) break;
           // the even CTA announces the bytes of both CTAs; the odd CTA's copies only complete them
           if (leader) mbar_arrive_expect_tx(&full[s], (uint32_t)(stage_bytes * CG));
@@ -350,7 +365,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
-        for (int kb = 0; kb < p.num_kb; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait(&full[s], ph, abort_flag, WAIT_BUDGET_CYC)) {
             ok = false;
             break;
@@ -360,7 +375,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           const uint64_t bd0 = b_desc0 + (uint64_t)((uint32_t)(s * Cfg::B_BYTES) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 4 * KC; ++kk) {  // UMMA_K = 16 (f16/bf16) or 8 (tf32): 4 steps per chunk
-            const uint32_t en = (kb | kk) != 0;
+            const uint32_t en = kb != kb_lo || kk != 0;  // the first k-block of the slice overwrites
             if (CG == 1) {
               if (KIND == 0) umma_f16(d_tmem, ad0 + a_off[kk], bd0 + b_off[kk], p.idesc, en);
               else umma_tf32(d_tmem, ad0 + a_off[kk], bd0 + b_off[kk], p.idesc, en);
@@ -400,7 +415,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     int acc = 0;
-    uint32_t aph = 0;
+    uint32_t aph = 0, xph = 0;
     const int osz = p.out_type == 0 ? 4 : 2;
     for (long long t = t_first; t < total_tiles; t += t_step) {
       const TileCoord tc = tile_coord<BN>(p, t, g_off, g_pre);
@@ -411,6 +426,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
       tc_fence_after();
+      if (KS == 2) {
+        // Partial sums of the two k-slices: the second CTA parks its sums in its operand ring (one tile per
+        // cluster: its MMAs are done and no load follows) and waits until the first has read them; the first
+        // waits for them, then adds them chunk by chunk below.
+        if (kslice == 1) {
+          float4 *park = (float4 *)smem;  // [chunk][4 columns][quadrant][lane]: a warp's stores are contiguous
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+              park[((c * 8 + q) * 4 + quad) * 32 + lane] =
+                  make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                              __uint_as_float(r[4 * q + 3]));
+          }
+          mbar_arrive_cluster(mapa_shared(smem_u32(xfull), 0));  // every thread releases its own stores
+          int done = 0;
+          if (lane == 0) done = mbar_wait(xdone, xph, abort_flag, WAIT_BUDGET_CYC) ? 1 : 0;
+          done = __shfl_sync(0xffffffffu, done, 0);
+          xph ^= 1u;
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+          acc ^= 1;
+          if (acc == 0) aph ^= 1u;
+          if (!done) break;
+          continue;
+        }
+        int parked = 0;
+        if (lane == 0) parked = mbar_wait_cluster(xfull, xph, abort_flag, WAIT_BUDGET_CYC) ? 1 : 0;
+        parked = __shfl_sync(0xffffffffu, parked, 0);
+        __syncwarp();  // lane 0's acquire orders the partner's parked sums before every lane's reads
+        xph ^= 1u;
+        if (!parked) break;
+      }
       const int row = mt * (TC_BM * CG) + (int)rank * TC_BM + quad * 32 + lane;
       const int n0 = tc.n0;
       char *Cb = p.Carr ? (char *)p.Carr[b] : (char *)p.C + (p.groups > 0 ? 0ll : (long long)b * p.sC * osz);
@@ -420,6 +472,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
         tmem_ld_wait();
+        if (KS == 2) {  // this slice's sums first, then the partner's: a fixed order
+          const uint32_t pk = mapa_shared(smem_u32(smem), 1);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 v = ld_shared_cluster_f4(pk + (uint32_t)((((c * 8 + q) * 4 + quad) * 32 + lane) * 16));
+            r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + v.x);
+            r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + v.y);
+            r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + v.z);
+            r[4 * q + 3] = __float_as_uint(__uint_as_float(r[4 * q + 3]) + v.w);
+          }
+        }
         const int col0 = n0 + c * 32;
         if (row_ok && col0 < tc.n_end) {
           const int ncols = tc.n_end - col0 < 32 ? tc.n_end - col0 : 32;
@@ -466,6 +529,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
+        if (KS == 2) mbar_arrive_cluster(mapa_shared(smem_u32(xdone), 1));  // the partner's ring is read
         if (CG == 1) mbar_arrive(&tempty[acc]);
         else mbar_arrive_cluster(lead_tempty0 + (uint32_t)(acc * 8));
       }
@@ -477,7 +541,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if ((p.nrep > 0 || p.mc) && warp >= 2 && warp <= 5) __threadfence_system();  // peers' replicas: stores performed
   tc_fence_before();
   __syncwarp();
-  if (CG == 2) cluster_sync();  // neither CTA leaves while its pair may still touch its memory or barriers
+  if (CL2) cluster_sync();  // neither CTA leaves while its partner may still touch its memory or barriers
   else __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_tb200_err, 1);
   if (warp == 1) {
@@ -542,10 +606,11 @@ bool make_map(CUtensorMap *tm, CUtensorMapDataType dt, int esz, const void *base
   return r == CUDA_SUCCESS;
 }
 
-template <int KIND, int BN, int KC, int CG>
+template <int KIND, int BN, int KC, int CG, int KS = 1>
 int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, int num_sms, cudaStream_t s) {
   using Cfg = TcCfg<BN, KC, CG>;
-  auto kern = tb200_gemm_tc_kernel<KIND, BN, KC, CG>;
+  constexpr bool CL2 = CG == 2 || KS == 2;
+  auto kern = tb200_gemm_tc_kernel<KIND, BN, KC, CG, KS>;
   static int attr_done[64], max_pairs[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -553,7 +618,7 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, i
   if (!attr_done[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
-    if (CG == 2) {
+    if (CL2) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
       cudaLaunchConfig_t cfg = {};
       cudaLaunchAttribute at[1];
@@ -573,21 +638,24 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, i
     }
     attr_done[dev] = 1;
   }
-  const long long slots = CG == 2 ? max_pairs[dev] : num_sms;
+  const long long slots = CL2 ? max_pairs[dev] : num_sms;
+  // KS = 2 runs one tile per cluster (its partner parks partial sums in the operand ring after its only tile)
+  if (KS == 2 && p.total_tiles > slots) return (int)cudaErrorNotSupported;
   const long long units = p.total_tiles < slots ? p.total_tiles : slots;
-  const unsigned grid = (unsigned)(units * CG);
+  const unsigned grid = (unsigned)(units * (CL2 ? 2 : 1));
   if (tb200_trace())
     fprintf(stderr,
-            "[trace] launch tb200_gemm_tc<%s,BN=%d,KC=%d,CG=%d> grid=(%u,1,1) block=(%d,1,1) smem=%d stages=%d m=%d n=%d "
-            "k=%d batch=%d\n",
-            KIND ? "tf32" : "f16", BN, KC, CG, grid, TC_THREADS, Cfg::SMEM_BYTES, Cfg::STAGES, p.m, p.n, p.k, p.batch);
+            "[trace] launch tb200_gemm_tc<%s,BN=%d,KC=%d,CG=%d%s> grid=(%u,1,1) block=(%d,1,1) smem=%d stages=%d m=%d "
+            "n=%d k=%d batch=%d\n",
+            KIND ? "tf32" : "f16", BN, KC, CG, KS == 2 ? ",KS=2" : "", grid, TC_THREADS, Cfg::SMEM_BYTES, Cfg::STAGES,
+            p.m, p.n, p.k, p.batch);
   // Programmatic stream serialization: this grid may be scheduled while the kernel before it in the stream
   // finishes (the kernel waits for it with griddep_wait before touching memory), which hides the launch and
   // the set-up of barriers and tensor memory behind that kernel's last tiles.
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[2];
   int na = 0;
-  if (CG == 2) {
+  if (CL2) {
     at[na].id = cudaLaunchAttributeClusterDimension;
     at[na].val.clusterDim.x = 2;
     at[na].val.clusterDim.y = 1;
@@ -634,7 +702,7 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   const int epr = 128 / es;
   int bn = tile_n;
   if (bn != 32 && bn != 64 && bn != 128 && bn != 256) bn = 128;
-  const int cg = pair ? 2 : 1;
+  const int cg = pair == 1 ? 2 : 1;  // pair: 0 one CTA per tile, 1 a CTA pair (2-SM UMMA), 2 the k split
   if (cg == 2 && bn != 128) bn = 256;  // the pair tiles are 256 x 256 and 256 x 128
   const int b_mn = g->opB == 1, a_mn = g->opA == 0;
   if (b_mn && bn / cg < epr) bn = epr * cg;  // an MN-major B tile holds whole 128-byte rows
@@ -716,8 +784,27 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
             ((uint32_t)(bn >> 3) << 17) | ((uint32_t)((TC_BM * cg) >> 4) << 24);
 
-  int rc;
-  if (cg == 2) {
+  // k split between the two CTAs of a cluster (KS = 2, the planner's mode 2): one tile per cluster, each CTA
+  // half the k-blocks, for 16-bit GEMMs whose tiles leave at least half of the SMs idle. TB200_KSPLIT=0 never,
+  // =1 whenever allowed, whatever the planner chose (tests, bisecting; read per call).
+  int rc = (int)cudaErrorNotSupported;
+  {
+    const char *e = getenv("TB200_KSPLIT");
+    const int want = e && *e ? atoi(e) : -1;
+    const bool allowed = !f32in && !ptr_ws && !g->groups && !g->nrep && !g->mc && p.num_kb >= 2 &&
+                         (bn == 64 || bn == 128 || bn == 256) && p.total_tiles * 2 <= num_sms &&
+                         (pair == 2 || (pair == 0 && want == 1));
+    if (allowed && want != 0) {
+      switch (bn) {
+        case 64: rc = launch_bn<0, 64, kc_for(64), 1, 2>(ta, tb, p, num_sms, s); break;
+        case 128: rc = launch_bn<0, 128, kc_for(128), 1, 2>(ta, tb, p, num_sms, s); break;
+        default: rc = launch_bn<0, 256, kc_for(256), 1, 2>(ta, tb, p, num_sms, s); break;
+      }
+    }
+  }
+  if (rc != (int)cudaErrorNotSupported) {
+    // launched (or failed) with the k split
+  } else if (cg == 2) {
     if (bn == 128)
       rc = f32in ? launch_bn<1, 128, 2, 2>(ta, tb, p, num_sms, s) : launch_bn<0, 128, 2, 2>(ta, tb, p, num_sms, s);
     else

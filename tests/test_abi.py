@@ -131,14 +131,22 @@ def test_trsm_refuses_unserved_cases(lib):
         assert h.strsm_batched(cb.CUBLAS_SIDE_RIGHT, 1, 0, 1, 4, 4, 1.0, 256, 4, 256, 4, 2) == 15
 
 
-# (transa, transb, m, n, k, batch, in, tf32, ptr, aligned) -> (kernel, BN) on 148 SMs
+# (transa, transb, m, n, k, batch, in, tf32, ptr, aligned) -> (kernel, BN) on 148 SMs; a CTA-pair tile is
+# 256 + BN, a k-split tile -BN
 PLAN_ROWS = [
     ("config 1: ggml fp16 T,N 4096x512x4096", (1, 0, 4096, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 128)),
-    ("config 2 K/V 1024x512x4096", (1, 0, 1024, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 32)),
+    ("config 2 K/V 1024x512x4096: k split", (1, 0, 1024, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, -64)),
+    ("K/V in bf16: k split", (1, 0, 1024, 512, 4096, 1, 2, 0, 0, 1), (cb.TB200_KERNEL_TC, -64)),
+    ("K/V with k < 1024 stays unsplit", (1, 0, 1024, 512, 960, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 32)),
+    ("K/V through pointer arrays stays unsplit", (1, 0, 1024, 512, 4096, 1, 1, 0, 1, 1), (cb.TB200_KERNEL_TC, 32)),
     ("config 2 gate/up 14336x512x4096: CTA-pair tile", (1, 0, 14336, 512, 4096, 1, 2, 0, 0, 1), (cb.TB200_KERNEL_TC, 512)),
     ("config 2 lm_head 128256x512x4096: CTA-pair tile", (1, 0, 128256, 512, 4096, 1, 1, 0, 0, 1),
      (cb.TB200_KERNEL_TC, 512)),
-    ("config 2 down 4096x512x14336", (1, 0, 4096, 512, 14336, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 128)),
+    ("config 2 down 4096x512x14336: k split", (1, 0, 4096, 512, 14336, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, -256)),
+    ("down, 256 tokens: k split", (1, 0, 4096, 256, 14336, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, -128)),
+    ("down, 128 tokens: k split", (1, 0, 4096, 128, 14336, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, -64)),
+    ("down, 4 sequences of 512: enough tiles unsplit", (1, 0, 4096, 512, 14336, 4, 1, 0, 0, 1),
+     (cb.TB200_KERNEL_TC, 512)),
     ("config 5 square 8192: CTA-pair tile", (1, 0, 8192, 8192, 8192, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 512)),
     ("config 4 decode n=1", (1, 0, 4096, 1, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_SKINNY, 0)),
     ("config 4 decode n=8", (1, 0, 14336, 8, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_SKINNY, 0)),

@@ -96,6 +96,29 @@ def test_tensor_core_alpha_beta_and_16bit_out(lib, h, monkeypatch, bn):
         assert_ok(run_and_check(lib, h, m=700, n=300, k=512, out_t=out_t, alpha=-0.75, beta=0.5, seed=3), out_t)
 
 
+# k split between the two CTAs of a cluster (TB200_KSPLIT=1 takes it wherever the tiles leave at least half of
+# the SMs idle): odd and tiny k-block counts, tails in m, n and k, both majors, bf16, alpha/beta with 16-bit C,
+# strided batches; a GEMM with a single k-block stays on the unsplit kernel
+KS_CASES = [
+    dict(opA=1, opB=0, m=1000, n=300, k=4160),
+    dict(opA=0, opB=1, m=520, n=200, k=136),
+    dict(opA=1, opB=1, m=300, n=190, k=100),
+    dict(opA=1, opB=0, m=256, n=129, k=64),
+    dict(opA=1, opB=0, m=700, n=256, k=1000, in_t=O.BF16),
+    dict(opA=1, opB=0, m=640, n=250, k=2048, out_t=O.F16, alpha=-0.75, beta=0.5),
+    dict(opA=1, opB=0, m=640, n=250, k=2048, out_t=O.BF16, in_t=O.BF16, alpha=2.0, beta=-1.0),
+    dict(opA=0, opB=0, m=300, n=200, k=520, batch=3),
+]
+
+
+@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("case", KS_CASES, ids=[f"{c['m']}x{c['n']}x{c['k']}-{i}" for i, c in enumerate(KS_CASES)])
+def test_k_split_cluster(lib, h, monkeypatch, bn, case):
+    monkeypatch.setenv("TB200_KSPLIT", "1")
+    monkeypatch.setenv("TB200_TC_BN", str(bn))
+    assert_ok(run_and_check(lib, h, seed=case["m"] + case["k"] + bn, **case), f"k split BN {bn}")
+
+
 def test_pair_tile_large_and_batched(lib, h):
     """The CTA-pair (2-SM UMMA) tile as the planner picks it: gate/up shape, and a strided batch."""
     assert lib.plan(1, 0, 14336, 512, 4096, 1, 1, 0, 0, 0, 1, 148)[1] == 512
@@ -266,7 +289,8 @@ def test_trsm_batched(lib, h):
 def test_deterministic(lib, h):
     import torch
     rng = np.random.default_rng(110)
-    for (m, n, k) in [(4096, 512, 1024), (4096, 8, 4096)]:
+    # unsplit tensor-core tile, the k split (fixed order of the two slices' sums), decode
+    for (m, n, k) in [(4096, 512, 1024), (1024, 512, 4096), (4096, 8, 4096)]:
         A, B = storage(rng, m * k, O.F16, 0.02), storage(rng, k * n, O.F16)
         dA, dB = dev(A), dev(B)
         outs = []
