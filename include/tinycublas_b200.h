@@ -115,9 +115,9 @@ cublasStatus_t cublasStrsmBatched(cublasHandle_t handle, cublasSideMode_t side, 
  * launching anything. Mirrors the role of the reference's test hook tinycublas_splitk_plan
  * (cublas.c:69-78): a pure function the host-only tests pin row by row.
  * Returns one of the TB200_KERNEL_* values; *tile_n receives the tensor-core tile width (0 if none) and
- * *pair the tile's mode: 0 one CTA per 128-row tile, 1 the 256-row tile of a CTA pair (2-SM UMMA), 2 the k
- * split (two CTAs per 128-row tile, each with half of the k-blocks; 16-bit strided GEMMs whose tiles leave
- * half of the SMs idle, with at least 1024 in k). */
+ * *pair the tile's mode: 0 one CTA per 128-row tile, 1 the 256-row tile of a CTA pair (2-SM UMMA), 2 and 3
+ * the k split of those (two CTAs, or two CTA pairs, per tile, each half with half of the k-blocks; 16-bit
+ * strided GEMMs whose tiles leave half of the SMs idle, with at least 1024 in k). */
 enum { TB200_KERNEL_NONE = 0, TB200_KERNEL_SIMT = 1, TB200_KERNEL_SKINNY = 2, TB200_KERNEL_TC = 3 };
 int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_type, int out_type,
                int tf32, int ptr_array, int aligned, int num_sms, int *tile_n, int *pair);

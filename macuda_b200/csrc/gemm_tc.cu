@@ -179,21 +179,23 @@ __device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *tm
   }
 }
 
-// KS = 2 (with CG = 1): a cluster of two CTAs per 128 x BN tile, one tile per cluster, each CTA with its own
-// half of the k-blocks and its own accumulator. The second CTA parks its partial sums in its idle operand ring
-// and the first reads them over distributed shared memory, adds them to its own in that order, and stores
-// C: the k-loop halves without a global workspace.
-// CG = 1: one CTA per 128 x BN tile. CG = 2: a cluster of two CTAs per 256 x BN tile (2-SM UMMA): each
-// CTA loads its 128 rows of A and BN/2 rows of B, the even CTA's MMA thread drives both tensor cores,
-// and each CTA's epilogue drains its own 128 rows from its own tensor memory.
+// CG = 1: one CTA per 128 x BN tile. CG = 2: two CTAs per 256 x BN tile (2-SM UMMA, the pair of cluster ranks
+// that differ in bit 0): each CTA loads its 128 rows of A and BN/2 rows of B, the even CTA's MMA thread
+// drives both tensor cores, and each CTA's epilogue drains its own 128 rows from its own tensor memory.
+// KS = 2: the k split. Each tile gets a second CTA (CG = 1) or a second pair (CG = 2), one tile per cluster,
+// and each half of the cluster runs half of the k-blocks into its own accumulator. Each CTA then finalises
+// half of its rows' columns: it parks its partial sums of the other half in its idle operand ring (one tile:
+// every load consumed, every MMA committed), and reads the peer's parked sums of its own half over
+// distributed shared memory, adds them and stores C. No workspace and no L2 round trip, and each CTA
+// drains half of the tile.
 template <int KIND, int BN, int KC, int CG, int KS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tb200_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const TcParams p) {
   using Cfg = TcCfg<BN, KC, CG>;
   constexpr int STAGES = Cfg::STAGES;
-  static_assert(KS == 1 || (CG == 1 && STAGES * Cfg::STAGE_BYTES >= TC_BM * BN * 4),
-                "k split: the operand ring must hold a 128 x BN f32 tile of partial sums");
+  static_assert(KS == 1 || (BN >= 64 && STAGES * Cfg::STAGE_BYTES >= TC_BM * (BN / 2) * 4),
+                "k split: the operand ring must hold 128 x BN/2 f32 partial sums");
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment of the shared-window offset: the 128B swizzle atom is 8 rows x 128 bytes. The
   // offset is the same in both CTAs of a pair, as the 2-SM UMMA requires.
@@ -206,9 +208,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t *tfull = bars + 2 * STAGES;
   uint64_t *tempty = tfull + 2;
   uint64_t *drain = tempty + 2;
-  uint64_t *xfull = drain + 1;  // KS = 2, first CTA: the partner's partial sums are parked
-  uint64_t *xdone = drain + 2;  // KS = 2, second CTA: the first has read them
-  uint32_t *tmem_slot = (uint32_t *)(drain + 3);
+  uint64_t *xfull = drain + 1;  // KS = 2: the k-split peer has parked its partial sums of this CTA's columns
+  uint32_t *tmem_slot = (uint32_t *)(drain + 2);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
   int *g_off = (int *)((uint8_t *)bars + Cfg::BAR_BYTES);  // grouped GEMM: clamped column offsets ...
   int *g_pre = g_off + TC_MAX_GROUPS + 1;                  // ... and tile-count prefix
@@ -221,14 +222,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  constexpr bool CL2 = CG == 2 || KS == 2;  // launched in clusters of two CTAs
-  const uint32_t crank = CL2 ? cluster_ctarank() : 0u;
-  const uint32_t rank = CG == 2 ? crank : 0u;     // the CTA's half of a pair tile's rows
-  const uint32_t kslice = KS == 2 ? crank : 0u;  // the CTA's half of the k-blocks
+  constexpr int CSIZE = CG * KS;   // CTAs per tile, launched as one cluster
+  constexpr bool CL = CSIZE > 1;
+  const uint32_t crank = CL ? cluster_ctarank() : 0u;
+  const uint32_t rank = CG == 2 ? (crank & 1u) : 0u;                  // the CTA's half of a pair tile's rows
+  const uint32_t kslice = KS == 2 ? (CG == 2 ? crank >> 1 : crank) : 0u;  // the CTA's half of the k-blocks
+  const uint32_t pair_even = crank & ~1u, pair_odd = crank | 1u;      // cluster ranks of the CTA's pair
+  const uint32_t xpeer = crank ^ (CG == 2 ? 2u : 1u);                 // the CTA with the same rows, other k half
   const bool leader = rank == 0;
   // tile index stream: one per CTA, or one per cluster
-  const long long t_first = CL2 ? (long long)(blockIdx.x >> 1) : (long long)blockIdx.x;
-  const long long t_step = CL2 ? (long long)(gridDim.x >> 1) : (long long)gridDim.x;
+  const long long t_first = (long long)(blockIdx.x / CSIZE);
+  const long long t_step = (long long)(gridDim.x / CSIZE);
   const int kb_lo = KS == 2 ? (int)((long long)kslice * p.num_kb / 2) : 0;
   const int kb_hi = KS == 2 ? (int)((long long)(kslice + 1) * p.num_kb / 2) : p.num_kb;
 
@@ -242,8 +246,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&tempty[a], 4 * CG);  // every epilogue warp of the tile
     }
     mbar_init(drain, 1);
-    mbar_init(xfull, 128);  // every epilogue thread of the partner
-    mbar_init(xdone, 4);    // every epilogue warp of the first CTA
+    mbar_init(xfull, 128);  // every epilogue thread of the k-split peer
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   tc_fence_before();
   __syncwarp();                 // barrier.cluster.*.aligned wants every warp converged
-  if (CL2) cluster_sync();  // the partner's loads and arrivals target this CTA's barriers: all initialised
+  if (CL) cluster_sync();  // peers' loads, commits and arrivals target this CTA's barriers: all initialised
   else __syncthreads();
   tc_fence_after();
   // Everything above touched only this CTA's own resources and the kernel parameters, and may overlap the
@@ -294,8 +297,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
   const uint32_t tmem_base = *tmem_slot;
   // shared::cluster addresses of the even CTA's barriers (CG == 2)
-  const uint32_t lead_full0 = CG == 2 ? mapa_shared(smem_u32(full), 0) : 0u;
-  const uint32_t lead_tempty0 = CG == 2 ? mapa_shared(smem_u32(tempty), 0) : 0u;
+  const uint32_t lead_full0 = CG == 2 ? mapa_shared(smem_u32(full), pair_even) : 0u;
+  const uint32_t lead_tempty0 = CG == 2 ? mapa_shared(smem_u32(tempty), pair_even) : 0u;
 
   if (warp == 0 || warp == 6) {
     // ------------------------------------------------------------------ TMA producers (A: warp 0, B: warp 6)
@@ -358,8 +361,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       }
       // commit targets: this CTA's barriers, and for a pair the odd CTA's too
       const uint32_t empty0_l = smem_u32(empty), tfull0_l = smem_u32(tfull), drain_l = smem_u32(drain);
-      const uint32_t empty0_p = CG == 2 ? mapa_shared(empty0_l, 1) : 0u;
-      const uint32_t tfull0_p = CG == 2 ? mapa_shared(tfull0_l, 1) : 0u;
+      const uint32_t empty0_p = CG == 2 ? mapa_shared(empty0_l, pair_odd) : 0u;
+      const uint32_t tfull0_p = CG == 2 ? mapa_shared(tfull0_l, pair_odd) : 0u;
       for (long long t = t_first; t < total_tiles && !*abort_flag; t += t_step) {
         if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, WAIT_BUDGET_CYC)) break;
         tc_fence_after();
@@ -414,6 +417,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    // 32-column chunks this CTA stores: all, or (k split) its half [c_lo, c_lo + HCH); the peer stores
+    // [o_lo, o_lo + HCH)
+    constexpr int HCH = KS == 2 ? BN / 64 : BN / 32;
+    const int c_lo = (int)kslice * HCH;
+    const int o_lo = HCH - c_lo;
     int acc = 0;
     uint32_t aph = 0, xph = 0;
     const int osz = p.out_type == 0 ? 4 : 2;
@@ -427,39 +435,24 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       if (!got) break;
       tc_fence_after();
       if (KS == 2) {
-        // Partial sums of the two k-slices: the second CTA parks its sums in its operand ring (one tile per
-        // cluster: its MMAs are done and no load follows) and waits until the first has read them; the first
-        // waits for them, then adds them chunk by chunk below.
-        if (kslice == 1) {
-          float4 *park = (float4 *)smem;  // [chunk][4 columns][quadrant][lane]: a warp's stores are contiguous
+        // park the partial sums of the peer's columns, announce them, wait for the peer's of this CTA's own
+        float4 *park = (float4 *)smem;  // [chunk][4 columns][quadrant][lane]: a warp's stores are contiguous
 #pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-            tmem_ld_wait();
+        for (int c = 0; c < HCH; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + (o_lo + c) * 32), r);
+          tmem_ld_wait();
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-              park[((c * 8 + q) * 4 + quad) * 32 + lane] =
-                  make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
-                              __uint_as_float(r[4 * q + 3]));
-          }
-          mbar_arrive_cluster(mapa_shared(smem_u32(xfull), 0));  // every thread releases its own stores
-          int done = 0;
-          if (lane == 0) done = mbar_wait(xdone, xph, abort_flag, WAIT_BUDGET_CYC) ? 1 : 0;
-          done = __shfl_sync(0xffffffffu, done, 0);
-          xph ^= 1u;
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tempty[acc]);
-          acc ^= 1;
-          if (acc == 0) aph ^= 1u;
-          if (!done) break;
-          continue;
+          for (int q = 0; q < 8; ++q)
+            park[((c * 8 + q) * 4 + quad) * 32 + lane] =
+                make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                            __uint_as_float(r[4 * q + 3]));
         }
+        mbar_arrive_cluster(mapa_shared(smem_u32(xfull), xpeer));  // every thread releases its own stores
         int parked = 0;
         if (lane == 0) parked = mbar_wait_cluster(xfull, xph, abort_flag, WAIT_BUDGET_CYC) ? 1 : 0;
         parked = __shfl_sync(0xffffffffu, parked, 0);
-        __syncwarp();  // lane 0's acquire orders the partner's parked sums before every lane's reads
+        __syncwarp();  // lane 0's acquire orders the peer's parked sums before every lane's reads
         xph ^= 1u;
         if (!parked) break;
       }
@@ -468,15 +461,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       char *Cb = p.Carr ? (char *)p.Carr[b] : (char *)p.C + (p.groups > 0 ? 0ll : (long long)b * p.sC * osz);
       const bool row_ok = row < p.m;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = c_lo; c < c_lo + HCH; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
         tmem_ld_wait();
-        if (KS == 2) {  // this slice's sums first, then the partner's: a fixed order
-          const uint32_t pk = mapa_shared(smem_u32(smem), 1);
+        if (KS == 2) {  // own sum + the peer's (two terms: the same value whichever CTA adds them)
+          const uint32_t pk = mapa_shared(smem_u32(smem), xpeer);
 #pragma unroll
           for (int q = 0; q < 8; ++q) {
-            const float4 v = ld_shared_cluster_f4(pk + (uint32_t)((((c * 8 + q) * 4 + quad) * 32 + lane) * 16));
+            const float4 v =
+                ld_shared_cluster_f4(pk + (uint32_t)(((((c - c_lo) * 8 + q) * 4 + quad) * 32 + lane) * 16));
             r[4 * q] = __float_as_uint(__uint_as_float(r[4 * q]) + v.x);
             r[4 * q + 1] = __float_as_uint(__uint_as_float(r[4 * q + 1]) + v.y);
             r[4 * q + 2] = __float_as_uint(__uint_as_float(r[4 * q + 2]) + v.z);
@@ -529,7 +523,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        if (KS == 2) mbar_arrive_cluster(mapa_shared(smem_u32(xdone), 1));  // the partner's ring is read
         if (CG == 1) mbar_arrive(&tempty[acc]);
         else mbar_arrive_cluster(lead_tempty0 + (uint32_t)(acc * 8));
       }
@@ -541,7 +534,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   if ((p.nrep > 0 || p.mc) && warp >= 2 && warp <= 5) __threadfence_system();  // peers' replicas: stores performed
   tc_fence_before();
   __syncwarp();
-  if (CL2) cluster_sync();  // neither CTA leaves while its partner may still touch its memory or barriers
+  if (CL) cluster_sync();  // no CTA leaves while a peer may still read its memory or signal its barriers
   else __syncthreads();
   if (threadIdx.x == 0 && *abort_flag) atomicExch(&g_tb200_err, 1);
   if (warp == 1) {
@@ -609,40 +602,40 @@ bool make_map(CUtensorMap *tm, CUtensorMapDataType dt, int esz, const void *base
 template <int KIND, int BN, int KC, int CG, int KS = 1>
 int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, int num_sms, cudaStream_t s) {
   using Cfg = TcCfg<BN, KC, CG>;
-  constexpr bool CL2 = CG == 2 || KS == 2;
+  constexpr int CSIZE = CG * KS;  // CTAs per tile: one cluster
   auto kern = tb200_gemm_tc_kernel<KIND, BN, KC, CG, KS>;
-  static int attr_done[64], max_pairs[64];
+  static int attr_done[64], max_clusters[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
   if (!attr_done[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
-    if (CL2) {
+    if (CSIZE > 1) {
       e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
       cudaLaunchConfig_t cfg = {};
       cudaLaunchAttribute at[1];
       at[0].id = cudaLaunchAttributeClusterDimension;
-      at[0].val.clusterDim.x = 2;
+      at[0].val.clusterDim.x = CSIZE;
       at[0].val.clusterDim.y = 1;
       at[0].val.clusterDim.z = 1;
-      cfg.gridDim = dim3(2 * (num_sms / 2), 1, 1);
+      cfg.gridDim = dim3(CSIZE * (num_sms / CSIZE), 1, 1);
       cfg.blockDim = dim3(TC_THREADS, 1, 1);
       cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
       cfg.attrs = at;
       cfg.numAttrs = 1;
       int nc = 0;
-      if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess || nc <= 0) nc = num_sms / 2;
+      if (cudaOccupancyMaxActiveClusters(&nc, kern, &cfg) != cudaSuccess || nc <= 0) nc = num_sms / CSIZE;
       (void)cudaGetLastError();
-      max_pairs[dev] = nc;
+      max_clusters[dev] = nc;
     }
     attr_done[dev] = 1;
   }
-  const long long slots = CL2 ? max_pairs[dev] : num_sms;
-  // KS = 2 runs one tile per cluster (its partner parks partial sums in the operand ring after its only tile)
+  const long long slots = CSIZE > 1 ? max_clusters[dev] : num_sms;
+  // KS = 2 runs one tile per cluster (partial sums are parked in the operand ring after the only tile)
   if (KS == 2 && p.total_tiles > slots) return (int)cudaErrorNotSupported;
   const long long units = p.total_tiles < slots ? p.total_tiles : slots;
-  const unsigned grid = (unsigned)(units * (CL2 ? 2 : 1));
+  const unsigned grid = (unsigned)(units * CSIZE);
   if (tb200_trace())
     fprintf(stderr,
             "[trace] launch tb200_gemm_tc<%s,BN=%d,KC=%d,CG=%d%s> grid=(%u,1,1) block=(%d,1,1) smem=%d stages=%d m=%d "
@@ -655,9 +648,9 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, i
   cudaLaunchConfig_t cfg = {};
   cudaLaunchAttribute at[2];
   int na = 0;
-  if (CL2) {
+  if (CSIZE > 1) {
     at[na].id = cudaLaunchAttributeClusterDimension;
-    at[na].val.clusterDim.x = 2;
+    at[na].val.clusterDim.x = CSIZE;
     at[na].val.clusterDim.y = 1;
     at[na].val.clusterDim.z = 1;
     ++na;
@@ -702,7 +695,9 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   const int epr = 128 / es;
   int bn = tile_n;
   if (bn != 32 && bn != 64 && bn != 128 && bn != 256) bn = 128;
-  const int cg = pair == 1 ? 2 : 1;  // pair: 0 one CTA per tile, 1 a CTA pair (2-SM UMMA), 2 the k split
+  // pair: 0 one CTA per tile, 1 a CTA pair (2-SM UMMA), 2 one CTA per tile with the k split, 3 a CTA pair with
+  // the k split
+  const int cg = pair == 1 || pair == 3 ? 2 : 1;
   if (cg == 2 && bn != 128) bn = 256;  // the pair tiles are 256 x 256 and 256 x 128
   const int b_mn = g->opB == 1, a_mn = g->opA == 0;
   if (b_mn && bn / cg < epr) bn = epr * cg;  // an MN-major B tile holds whole 128-byte rows
@@ -784,17 +779,20 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
             ((uint32_t)(bn >> 3) << 17) | ((uint32_t)((TC_BM * cg) >> 4) << 24);
 
-  // k split between the two CTAs of a cluster (KS = 2, the planner's mode 2): one tile per cluster, each CTA
-  // half the k-blocks, for 16-bit GEMMs whose tiles leave at least half of the SMs idle. TB200_KSPLIT=0 never,
-  // =1 whenever allowed, whatever the planner chose (tests, bisecting; read per call).
+  // the k split (KS = 2, the planner's modes 2 and 3): two halves of a cluster per tile (two CTAs, or two CTA
+  // pairs), one tile per cluster, each half with half the k-blocks, for 16-bit GEMMs whose tiles leave at
+  // least half of the SMs idle. TB200_KSPLIT=0 never, =1 whenever allowed, whatever the planner chose (tests,
+  // bisecting; read per call).
   int rc = (int)cudaErrorNotSupported;
   {
     const char *e = getenv("TB200_KSPLIT");
     const int want = e && *e ? atoi(e) : -1;
     const bool allowed = !f32in && !ptr_ws && !g->groups && !g->nrep && !g->mc && p.num_kb >= 2 &&
-                         (bn == 64 || bn == 128 || bn == 256) && p.total_tiles * 2 <= num_sms &&
-                         (pair == 2 || (pair == 0 && want == 1));
-    if (allowed && want != 0) {
+                         (cg == 2 ? bn == 256 : bn == 64 || bn == 128 || bn == 256) &&
+                         p.total_tiles * 2 * cg <= num_sms && (pair >= 2 || want == 1);
+    if (allowed && want != 0 && cg == 2) {
+      rc = launch_bn<0, 256, 1, 2, 2>(ta, tb, p, num_sms, s);
+    } else if (allowed && want != 0) {
       switch (bn) {
         case 64: rc = launch_bn<0, 64, kc_for(64), 1, 2>(ta, tb, p, num_sms, s); break;
         case 128: rc = launch_bn<0, 128, kc_for(128), 1, 2>(ta, tb, p, num_sms, s); break;

@@ -206,37 +206,44 @@ int tb200_tc_tile_n(int m, int n, int batch, int num_sms, int *pair) {
   return best;
 }
 
-/* The k split: a cluster of two CTAs per 128 x BN tile, each CTA with half of the k-blocks, the second CTA's
- * partial sums added by the first through distributed shared memory. One tile per cluster, so only for GEMMs
- * of at most num_sms / 2 tiles of that width (the GEMMs that leave SMs idle unsplit). The planner compares
- * modelled times: per tile a fixed cost plus a cost per 128-byte k-block on one SM, both fitted to f16 GEMMs
- * measured on the B200 (4096 and 1024 rows, 128..512 columns, k 4096 and 14336, CUDA-graph replay). The split
- * tile's fixed cost holds the cluster launch and the exchange of the partial sums. It is taken when it saves
- * at least 5 %. Returns the split tile's width, or 0. */
+/* The k split: two halves of a cluster per tile (two CTAs on a 128 x BN tile, or two CTA pairs on a 256 x 256
+ * tile), each half with half of the k-blocks; each CTA adds the other half's partial sums for half of its
+ * columns through distributed shared memory. One tile per cluster, so only for GEMMs whose tiles leave at
+ * least half of the SMs idle. The planner compares modelled times: per tile a fixed cost plus a cost per
+ * 64-deep k-block on one SM, fitted to f16 GEMMs measured on the B200 (4096 and 1024 rows, 128..512 columns,
+ * k 4096 and 14336, CUDA-graph replay), and a floor of the compulsory bytes at 6 TB/s. It is taken when it
+ * saves at least 5 %. Returns the split tile's width and sets *pair_out (2: single-CTA halves, 3: pair
+ * halves), or returns 0. */
 static double unsplit_kb_us(int bn, int pair) {
   if (pair) return bn == 256 ? 0.32 : 0.273;
   return bn == 256 ? 0.45 : bn == 128 ? 0.273 : bn == 64 ? 0.22 : 0.215;
 }
-static int ksplit_tile(int m, int n, int k, int batch, int num_sms, int bn0, int pair0) {
-  static const int bns[3] = {64, 128, 256};
-  static const double kb_us[3] = {0.229, 0.284, 0.45}, fixed_us[3] = {8.2, 9.2, 10.8};
+static int ksplit_tile(int m, int n, int k, int batch, int num_sms, int bn0, int pair0, int *pair_out) {
+  static const int bns[4] = {64, 128, 256, 256};
+  static const int cgs[4] = {1, 1, 1, 2};
+  static const double kb_us[4] = {0.225, 0.285, 0.46, 0.388}, fixed_us[4] = {6.0, 7.0, 6.9, 8.1};
   const long long nkb = ((long long)k + 63) / 64;
-  if (nkb < 16 || num_sms < 2) return 0;
+  if (nkb < 16 || num_sms < 4) return 0;
+  /* f16 operands read once, f32 C written once */
+  const double floor_us = ((double)m * k * 2 + (double)k * n * 2 + (double)m * n * 4) * batch / 6.0e6;
   const int cg0 = pair0 ? 2 : 1;
   const long long tiles0 = (long long)((m + 128 * cg0 - 1) / (128 * cg0)) * ((n + bn0 - 1) / bn0) * batch;
   const long long slots0 = num_sms / cg0;
-  const double t0 = (double)((tiles0 + slots0 - 1) / slots0) * (5.0 + (double)nkb * unsplit_kb_us(bn0, pair0));
+  double t0 = (double)((tiles0 + slots0 - 1) / slots0) * (5.0 + (double)nkb * unsplit_kb_us(bn0, pair0));
+  if (t0 < floor_us) t0 = floor_us;
   int best = 0;
   double best_t = 0.95 * t0;
-  for (int i = 0; i < 3; i++) {
-    const int bn = bns[i];
+  for (int i = 0; i < 4; i++) {
+    const int bn = bns[i], cg = cgs[i];
     if (n <= bn / 2) continue; /* a tile at least half full */
-    const long long tiles = (long long)((m + 127) / 128) * ((n + bn - 1) / bn) * batch;
-    if (tiles * 2 > num_sms) continue;
-    const double t = fixed_us[i] + (double)((nkb + 1) / 2) * kb_us[i];
+    const long long tiles = (long long)((m + 128 * cg - 1) / (128 * cg)) * ((n + bn - 1) / bn) * batch;
+    if (tiles * 2 * cg > num_sms) continue;
+    double t = fixed_us[i] + (double)((nkb + 1) / 2) * kb_us[i];
+    if (t < floor_us) t = floor_us;
     if (t < best_t) {
       best_t = t;
       best = bn;
+      *pair_out = cg == 2 ? 3 : 2;
     }
   }
   return best;
@@ -259,10 +266,11 @@ int tb200_plan(int transa, int transb, int m, int n, int k, int batch, int in_ty
     int pr = 0;
     int bn = tb200_tc_tile_n(m, n, batch, num_sms, &pr);
     if (sixteen && !ptr_array) { /* the split kernel reads plain strided operands */
-      const int ks = ksplit_tile(m, n, k, batch, num_sms <= 0 ? 148 : num_sms, bn, pr);
+      int kpr = 0;
+      const int ks = ksplit_tile(m, n, k, batch, num_sms <= 0 ? 148 : num_sms, bn, pr, &kpr);
       if (ks) {
         bn = ks;
-        pr = 2;
+        pr = kpr;
       }
     }
     if (tile_n) *tile_n = bn;

@@ -132,9 +132,12 @@ def test_trsm_refuses_unserved_cases(lib):
 
 
 # (transa, transb, m, n, k, batch, in, tf32, ptr, aligned) -> (kernel, BN) on 148 SMs; a CTA-pair tile is
-# 256 + BN, a k-split tile -BN
+# 256 + BN, a k-split tile minus that (-BN: two CTAs per 128-row tile; -512: two CTA pairs per 256 x 256 tile)
 PLAN_ROWS = [
-    ("config 1: ggml fp16 T,N 4096x512x4096", (1, 0, 4096, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 128)),
+    ("config 1: ggml fp16 T,N 4096x512x4096: k split of the pair tile", (1, 0, 4096, 512, 4096, 1, 1, 0, 0, 1),
+     (cb.TB200_KERNEL_TC, -512)),
+    ("Q/O, 256 tokens: k split", (1, 0, 4096, 256, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, -128)),
+    ("config 3 KQV folded: HBM-bound, unsplit", (1, 0, 128, 2048, 4096, 8, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 128)),
     ("config 2 K/V 1024x512x4096: k split", (1, 0, 1024, 512, 4096, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, -64)),
     ("K/V in bf16: k split", (1, 0, 1024, 512, 4096, 1, 2, 0, 0, 1), (cb.TB200_KERNEL_TC, -64)),
     ("K/V with k < 1024 stays unsplit", (1, 0, 1024, 512, 960, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, 32)),
@@ -142,7 +145,8 @@ PLAN_ROWS = [
     ("config 2 gate/up 14336x512x4096: CTA-pair tile", (1, 0, 14336, 512, 4096, 1, 2, 0, 0, 1), (cb.TB200_KERNEL_TC, 512)),
     ("config 2 lm_head 128256x512x4096: CTA-pair tile", (1, 0, 128256, 512, 4096, 1, 1, 0, 0, 1),
      (cb.TB200_KERNEL_TC, 512)),
-    ("config 2 down 4096x512x14336: k split", (1, 0, 4096, 512, 14336, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, -256)),
+    ("config 2 down 4096x512x14336: k split of the pair tile", (1, 0, 4096, 512, 14336, 1, 1, 0, 0, 1),
+     (cb.TB200_KERNEL_TC, -512)),
     ("down, 256 tokens: k split", (1, 0, 4096, 256, 14336, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, -128)),
     ("down, 128 tokens: k split", (1, 0, 4096, 128, 14336, 1, 1, 0, 0, 1), (cb.TB200_KERNEL_TC, -64)),
     ("down, 4 sequences of 512: enough tiles unsplit", (1, 0, 4096, 512, 14336, 4, 1, 0, 0, 1),

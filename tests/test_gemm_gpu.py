@@ -96,9 +96,10 @@ def test_tensor_core_alpha_beta_and_16bit_out(lib, h, monkeypatch, bn):
         assert_ok(run_and_check(lib, h, m=700, n=300, k=512, out_t=out_t, alpha=-0.75, beta=0.5, seed=3), out_t)
 
 
-# k split between the two CTAs of a cluster (TB200_KSPLIT=1 takes it wherever the tiles leave at least half of
-# the SMs idle): odd and tiny k-block counts, tails in m, n and k, both majors, bf16, alpha/beta with 16-bit C,
-# strided batches; a GEMM with a single k-block stays on the unsplit kernel
+# the k split, on single-CTA tiles (two CTAs per tile) and on the CTA-pair tile (two pairs per tile):
+# TB200_KSPLIT=1 takes it wherever the tiles leave at least half of the SMs idle. Odd and tiny k-block counts,
+# tails in m, n and k, both majors, bf16, alpha/beta with 16-bit C, strided batches; a GEMM with a single
+# k-block stays on the unsplit kernel
 KS_CASES = [
     dict(opA=1, opB=0, m=1000, n=300, k=4160),
     dict(opA=0, opB=1, m=520, n=200, k=136),
@@ -111,12 +112,12 @@ KS_CASES = [
 ]
 
 
-@pytest.mark.parametrize("bn", [64, 128, 256])
+@pytest.mark.parametrize("bn", [64, 128, 256, "pair"])
 @pytest.mark.parametrize("case", KS_CASES, ids=[f"{c['m']}x{c['n']}x{c['k']}-{i}" for i, c in enumerate(KS_CASES)])
 def test_k_split_cluster(lib, h, monkeypatch, bn, case):
     monkeypatch.setenv("TB200_KSPLIT", "1")
     monkeypatch.setenv("TB200_TC_BN", str(bn))
-    assert_ok(run_and_check(lib, h, seed=case["m"] + case["k"] + bn, **case), f"k split BN {bn}")
+    assert_ok(run_and_check(lib, h, seed=case["m"] + case["k"] + len(str(bn)), **case), f"k split BN {bn}")
 
 
 def test_pair_tile_large_and_batched(lib, h):
