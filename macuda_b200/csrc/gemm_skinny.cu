@@ -15,8 +15,16 @@
 // shared memory in warp order, so the result is deterministic, needs no global workspace, no
 // counters and no second launch (the reference's split-K needed all three, and its per-handle
 // workspace raced across streams: splitk-20260923/burst-3090.out).
+//
+// k split across a cluster: with S > 1 the S CTAs of a cluster share one 16-row block, CTA rank r taking
+// the r-th of S contiguous ranges of 32-wide chunks (the last also takes the k % 32 tail). Each CTA sums
+// its warps as above into shared memory; after a cluster barrier rank 0 adds the S partial tiles in rank
+// order over distributed shared memory (deterministic) and stores C, and a second barrier keeps the other
+// CTAs resident until it has read them. The host picks S so that the units of work (16-row blocks x S)
+// spread evenly over the SMs: one CTA per block leaves 4096-row weights on 256 CTAs over 148 SMs.
 #include <cuda_runtime.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include "tb200_internal.h"
 #include "tb200_device.cuh"
 
@@ -61,8 +69,9 @@ __device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t 
 }
 
 template <typename T>
-__global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gemm_t g, int z0) {
+__global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gemm_t g, int z0, int S) {
   __shared__ float red[SK_WARPS][SK_ROWS][8];
+  __shared__ float part[SK_ROWS * 8];  // this CTA's k-slice sums, read by cluster rank 0 (S > 1)
   // launched with programmatic stream serialization: wait for the kernel before this one in the stream to
   // complete before touching memory, then let the next one be scheduled on SMs this grid leaves free
   griddep_wait();
@@ -74,7 +83,8 @@ __global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gem
   char *C = g.Carr ? (char *)g.Carr[b] : (char *)g.C + (long long)b * g.sC * osz;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int gi = lane >> 2, ci = lane & 3;
-  const int row0 = blockIdx.x * SK_ROWS;
+  const int slice = S > 1 ? (int)(blockIdx.x % (unsigned)S) : 0;  // = the CTA's cluster rank
+  const int row0 = (int)(blockIdx.x / (unsigned)S) * SK_ROWS;
   const int ra = row0 + gi, rb = row0 + gi + 8;
   const bool ok_a = ra < g.m, ok_b = rb < g.m, ok_col = gi < g.n;
   // rows past m and columns past n read row/column 0 (always valid) and are discarded
@@ -83,10 +93,11 @@ __global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gem
   const T *pB = B + (long long)(ok_col ? gi : 0) * g.ldb + 8 * ci;
   float d[4] = {0.f, 0.f, 0.f, 0.f};
   const int nchunks = g.k >> 5;  // whole 32-wide chunks; the host guarantees k % 8 == 0
+  const int c_lo = (int)((long long)slice * nchunks / S), c_hi = (int)((long long)(slice + 1) * nchunks / S);
   const bool vec = (((uintptr_t)A | (uintptr_t)B) & 15) == 0;  // pointer-array elements may be unaligned
   if (vec) {
-    int j = warp;
-    for (; j + (SK_UNROLL - 1) * SK_WARPS < nchunks; j += SK_UNROLL * SK_WARPS) {
+    int j = c_lo + warp;
+    for (; j + (SK_UNROLL - 1) * SK_WARPS < c_hi; j += SK_UNROLL * SK_WARPS) {
       uint4 va[SK_UNROLL], vb[SK_UNROLL], vB[SK_UNROLL];
 #pragma unroll
       for (int u = 0; u < SK_UNROLL; ++u) {
@@ -102,7 +113,7 @@ __global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gem
         mma16816<T>(d, va[u].z, vb[u].z, va[u].w, vb[u].w, vB[u].z, vB[u].w);
       }
     }
-    for (; j < nchunks; j += SK_WARPS) {
+    for (; j < c_hi; j += SK_WARPS) {
       const long long off = (long long)j * 32;
       uint4 va = ld_stream_v4(pa + off), vb = ld_stream_v4(pb + off), vB = ld_cached_v4(pB + off);
       if (!ok_col) vB = make_uint4(0, 0, 0, 0);
@@ -111,7 +122,7 @@ __global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gem
     }
     // tail of k % 32 (a multiple of 8): lanes whose 8-wide group lies inside k load it, others zero
     const int kt = nchunks * 32;
-    if (warp == 0 && kt < g.k) {
+    if (warp == 0 && kt < g.k && slice == S - 1) {
       const bool in = kt + 8 * ci < g.k;
       uint4 va = in ? ld_stream_v4(pa + kt) : make_uint4(0, 0, 0, 0);
       uint4 vb = in ? ld_stream_v4(pb + kt) : make_uint4(0, 0, 0, 0);
@@ -123,7 +134,8 @@ __global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gem
     // unaligned pointer-array element: scalar fp32 dot products, same reduction below
     float acc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};
     const int c0 = 2 * ci;
-    for (int kk = warp; kk < g.k; kk += SK_WARPS) {
+    const int k_lo = (int)((long long)slice * g.k / S), k_hi = (int)((long long)(slice + 1) * g.k / S);
+    for (int kk = k_lo + warp; kk < k_hi; kk += SK_WARPS) {
       const float x0 = ok_a ? to_f32(A[(long long)ra * g.lda + kk]) : 0.f;
       const float x1 = ok_b ? to_f32(A[(long long)rb * g.lda + kk]) : 0.f;
       const float y0 = c0 < g.n ? to_f32(B[(long long)c0 * g.ldb + kk]) : 0.f;
@@ -141,13 +153,25 @@ __global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gem
   red[warp][gi + 8][2 * ci] = d[2];
   red[warp][gi + 8][2 * ci + 1] = d[3];
   __syncthreads();
+  const int r = threadIdx.x & 15, col = threadIdx.x >> 4;
+  float sum = 0.f;
   if (threadIdx.x < SK_ROWS * 8) {
-    const int r = threadIdx.x & 15, col = threadIdx.x >> 4;
+#pragma unroll
+    for (int w = 0; w < SK_WARPS; ++w) sum += red[w][r][col];
+  }
+  if (S > 1) {
+    if (threadIdx.x < SK_ROWS * 8) part[threadIdx.x] = sum;
+    cluster_sync();  // every slice's sums are in its shared memory
+    if (slice == 0 && threadIdx.x < SK_ROWS * 8) {
+      sum = part[threadIdx.x];
+      for (int q = 1; q < S; ++q) sum += ld_shared_cluster_f32(mapa_shared(smem_u32(&part[threadIdx.x]), (uint32_t)q));
+    }
+    cluster_sync();  // rank 0 has read them: the others may leave
+    if (slice != 0) return;
+  }
+  if (threadIdx.x < SK_ROWS * 8) {
     const int row = row0 + r;
     if (row < g.m && col < g.n) {
-      float sum = 0.f;
-#pragma unroll
-      for (int w = 0; w < SK_WARPS; ++w) sum += red[w][r][col];
       const long long idx = row + (long long)col * g.ldc;
       float v = g.alpha * sum;
       if (g.beta != 0.f) v += g.beta * load_out(C, idx, g.out_type);
@@ -167,26 +191,57 @@ extern "C" int tb200_skinny_ok(const tb200_gemm_t *g) {
   return 1;
 }
 
+// k slices per 16-row block: the smallest S in {1, 2, 4, 8} that gives at least two CTAs per SM, while every
+// warp keeps at least one full unrolled pass (4 chunks of 32) per slice. Measured on the B200 (f16, n 1..8):
+// 4096 x 4096 and 4096 x 14336 run best at S = 2 (1.25x and 1.4x), 1024 x 4096 at S = 4 (1.9x); 14336 x 4096
+// (896 blocks) and the 128256-row lm_head lose with any split, which this rule never gives them. Smaller
+// slices pay a per-CTA cost (launch, reductions, cluster barriers) and keep fewer loads in flight.
+// TB200_SKINNY_SPLIT=1|2|4|8 forces S where each slice keeps at least 16 chunks (tests, bisecting; read per
+// call).
+static int skinny_slices(long long blocks, int k, int num_sms) {
+  const int chunks = k >> 5;
+  const char *e = getenv("TB200_SKINNY_SPLIT");
+  const int want = e && *e ? atoi(e) : 0;
+  if (want == 1 || want == 2 || want == 4 || want == 8) return chunks / want >= 16 || want == 1 ? want : 1;
+  if (num_sms <= 0) num_sms = 148;
+  int S = 1;
+  while (S < 8 && blocks * S < 2LL * num_sms && chunks / (2 * S) >= 4 * SK_WARPS) S *= 2;
+  return S;
+}
+
 extern "C" int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s) {
   if (!tb200_skinny_ok(g)) return tb200_launch_simt(g, s);
-  const long long gx = (g->m + SK_ROWS - 1) / SK_ROWS;
+  const long long blocks = (g->m + SK_ROWS - 1) / SK_ROWS;
+  const int S = skinny_slices(blocks * (g->batch < 65535 ? g->batch : 65535), g->k, tb200_num_sms());
+  const long long gx = blocks * S;
   if (gx > 0x7fffffffLL) return (int)cudaErrorInvalidConfiguration;
   for (int z0 = 0; z0 < g->batch; z0 += 65535) {
     const unsigned gy = (unsigned)(g->batch - z0 < 65535 ? g->batch - z0 : 65535);
     if (tb200_trace())
-      fprintf(stderr, "[trace] launch tb200_gemm_skinny grid=(%lld,%u,1) block=(%d,1,1) m=%d n=%d k=%d out=%d\n", gx, gy,
-              SK_T, g->m, g->n, g->k, g->out_type);
+      fprintf(stderr, "[trace] launch tb200_gemm_skinny<S=%d> grid=(%lld,%u,1) block=(%d,1,1) m=%d n=%d k=%d out=%d\n", S,
+              gx, gy, SK_T, g->m, g->n, g->k, g->out_type);
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (S > 1) {  // the k slices of a block form one cluster
+      at[na].id = cudaLaunchAttributeClusterDimension;
+      at[na].val.clusterDim.x = (unsigned)S;
+      at[na].val.clusterDim.y = 1;
+      at[na].val.clusterDim.z = 1;
+      ++na;
+    }
+    if (tb200_pdl()) {
+      at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      at[na].val.programmaticStreamSerializationAllowed = 1;
+      ++na;
+    }
     cfg.gridDim = dim3((unsigned)gx, gy, 1);
     cfg.blockDim = dim3(SK_T, 1, 1);
     cfg.stream = s;
     cfg.attrs = at;
-    cfg.numAttrs = tb200_pdl() ? 1 : 0;
-    cudaError_t e = g->in_type == TB200_F16 ? cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_kernel<__half>, *g, z0)
-                                            : cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_kernel<__nv_bfloat16>, *g, z0);
+    cfg.numAttrs = na;
+    cudaError_t e = g->in_type == TB200_F16 ? cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_kernel<__half>, *g, z0, S)
+                                            : cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_kernel<__nv_bfloat16>, *g, z0, S);
     if (e != cudaSuccess) return (int)e;
   }
   return 0;

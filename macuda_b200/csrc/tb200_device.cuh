@@ -121,6 +121,12 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t local, uint32_t rank) {
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+// 4-byte load from a shared::cluster address (another CTA of the cluster)
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t cluster_addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(cluster_addr) : "memory");
+  return v;
+}
 // 16-byte load from a shared::cluster address (another CTA of the cluster)
 __device__ __forceinline__ float4 ld_shared_cluster_f4(uint32_t cluster_addr) {
   float4 v;

@@ -152,6 +152,27 @@ def test_skinny_tails_and_epilogue(lib, h, in_t, out_t, alpha, beta):
                             seed=50))
 
 
+# the decode kernel's k split across a cluster (TB200_SKINNY_SPLIT forces the slices per 16-row block):
+# m not a multiple of 16, k % 32 in {8, 16, 24} (the tail in the last slice), every n, alpha/beta with
+# 16-bit C, strided and pointer-array batches, and unaligned pointer-array elements (the scalar path)
+SKINNY_SPLIT_CASES = [
+    dict(m=1000, n=1, k=4104),
+    dict(m=4096, n=8, k=4096),
+    dict(m=520, n=5, k=4112, in_t=O.BF16, out_t=O.BF16, alpha=-1.0, beta=1.0),
+    dict(m=300, n=3, k=4120, out_t=O.F16, alpha=0.5, beta=2.0, batch=3),
+    dict(m=768, n=8, k=4096, batch=4, mode="ptr", broadcast_a=2),
+    dict(m=256, n=2, k=4096, batch=4, mode="ptr", a_ptr_shift=2),
+]
+
+
+@pytest.mark.parametrize("S", [2, 4, 8])
+@pytest.mark.parametrize("case", SKINNY_SPLIT_CASES,
+                         ids=[f"{c['m']}x{c['n']}x{c['k']}-{i}" for i, c in enumerate(SKINNY_SPLIT_CASES)])
+def test_skinny_k_split(lib, h, monkeypatch, S, case):
+    monkeypatch.setenv("TB200_SKINNY_SPLIT", str(S))
+    assert_ok(run_and_check(lib, h, seed=case["m"] + case["k"] + S, **case), f"S={S}")
+
+
 def test_skinny_pointer_arrays_gqa(lib, h):
     assert_ok(run_and_check(lib, h, m=768, n=8, k=2048, batch=8, mode="ptr", broadcast_a=4, seed=60), "ptr n=8")
 
