@@ -173,6 +173,27 @@ def test_skinny_k_split(lib, h, monkeypatch, S, case):
     assert_ok(run_and_check(lib, h, seed=case["m"] + case["k"] + S, **case), f"S={S}")
 
 
+# batch-1 decode GEMMs (cublasGemmEx): k not a multiple of 32, m not a multiple of 16, every n, alpha/beta with
+# 16-bit C, bf16, a single 16-row block, few blocks (the k split across a cluster), and the same GEMM twice
+DECODE_CASES = [
+    dict(m=4096, n=1, k=4096),
+    dict(m=14336, n=8, k=4096, sample=128),
+    dict(m=4096, n=3, k=14336),
+    dict(m=1000, n=7, k=1000, out_t=O.F16, alpha=0.5, beta=2.0),
+    dict(m=520, n=2, k=4104, in_t=O.BF16, out_t=O.BF16, alpha=-1.0, beta=1.0),
+    dict(m=64, n=8, k=4096),
+    dict(m=16, n=1, k=8),
+    dict(m=33, n=5, k=520, in_t=O.BF16),
+]
+
+
+@pytest.mark.parametrize("case", DECODE_CASES,
+                         ids=[f"{c['m']}x{c['n']}x{c['k']}-{i}" for i, c in enumerate(DECODE_CASES)])
+def test_decode_gemm_ex(lib, h, case):
+    for rep in range(2):
+        assert_ok(run_and_check(lib, h, mode="ex", seed=case["m"] + case["k"] + rep, **case), f"rep {rep}")
+
+
 def test_skinny_pointer_arrays_gqa(lib, h):
     assert_ok(run_and_check(lib, h, m=768, n=8, k=2048, batch=8, mode="ptr", broadcast_a=4, seed=60), "ptr n=8")
 
