@@ -6,12 +6,12 @@
 // the critical path. Replaces the reference's split-K tc2k kernels (cuda-shim/libtinycublas/
 // gemm.cu:317-348, :408-415) and their plan (cublas.c:69-78) for these shapes.
 //
-// Decomposition: one CTA per 16 output rows (and batch element), 8 warps splitting k in 32-wide
-// chunks (warp w takes chunks w, w+8, ...). Per chunk a lane (g = lane/4, c = lane%4) issues two
+// Decomposition: one CTA per 16 output rows (and batch element), W warps splitting k in 32-wide
+// chunks (warp w takes chunks w, w+W, ...; W = 4, 8 or 16 by the GEMM's shape, below). Per chunk a lane (g = lane/4, c = lane%4) issues two
 // 16-byte loads of A (rows g and g+8, k = 8c..8c+7) and one 16-byte load of B (column g), and the
 // warp multiplies them on the tensor cores with two mma.m16n8k16 (fp32 accumulate). The k order
 // inside a chunk is permuted identically for A and B, which leaves every dot product unchanged and
-// lets the fragments come straight from 128-bit loads. The 8 warps' partial tiles are summed in
+// lets the fragments come straight from 128-bit loads. The warps' partial tiles are summed in
 // shared memory in warp order, so the result is deterministic, needs no global workspace, no
 // counters and no second launch (the reference's split-K needed all three, and its per-handle
 // workspace raced across streams: splitk-20260923/burst-3090.out).
@@ -25,6 +25,7 @@
 #include <cuda_runtime.h>
 #include <stdio.h>
 #include <stdlib.h>
+#include <string.h>
 #include "tb200_internal.h"
 #include "tb200_device.cuh"
 
@@ -32,10 +33,7 @@ using namespace tb200;
 
 namespace {
 
-constexpr int SK_WARPS = 8;
-constexpr int SK_T = SK_WARPS * 32;
 constexpr int SK_ROWS = 16;
-constexpr int SK_UNROLL = 4;
 
 __device__ __forceinline__ uint4 ld_stream_v4(const void *p) {  // read once: no L1 allocation
   uint4 v;
@@ -68,8 +66,9 @@ __device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], uint32_t 
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-template <typename T>
-__global__ void __launch_bounds__(SK_T) tb200_gemm_skinny_kernel(const tb200_gemm_t g, int z0, int S) {
+// SK_WARPS warps per CTA split the block's k; each keeps SK_UNROLL 32-wide chunks of loads in flight
+template <typename T, int SK_WARPS, int SK_UNROLL>
+__global__ void __launch_bounds__(SK_WARPS * 32) tb200_gemm_skinny_kernel(const tb200_gemm_t g, int z0, int S) {
   __shared__ float red[SK_WARPS][SK_ROWS][8];
   __shared__ float part[SK_ROWS * 8];  // this CTA's k-slice sums, read by cluster rank 0 (S > 1)
   // launched with programmatic stream serialization: wait for the kernel before this one in the stream to
@@ -191,35 +190,68 @@ extern "C" int tb200_skinny_ok(const tb200_gemm_t *g) {
   return 1;
 }
 
-// k slices per 16-row block: the smallest S in {1, 2, 4, 8} that gives at least two CTAs per SM, while every
-// warp keeps at least one full unrolled pass (4 chunks of 32) per slice. Measured on the B200 (f16, n 1..8):
-// 4096 x 4096 and 4096 x 14336 run best at S = 2 (1.25x and 1.4x), 1024 x 4096 at S = 4 (1.9x); 14336 x 4096
-// (896 blocks) and the 128256-row lm_head lose with any split, which this rule never gives them. Smaller
-// slices pay a per-CTA cost (launch, reductions, cluster barriers) and keep fewer loads in flight.
-// TB200_SKINNY_SPLIT=1|2|4|8 forces S where each slice keeps at least 16 chunks (tests, bisecting; read per
-// call).
-static int skinny_slices(long long blocks, int k, int num_sms) {
+// Kernel shape and k slices per 16-row block, from sweeps on the B200 (f16, n 1 and 8, CUDA-graph replay):
+// * many blocks (at least six per SM): 4 warps x 8 chunks in flight, 128-thread CTAs, eight per SM, no
+//   split. 14336 x 4096 and the 128256-row lm_head ran 15 % and 11 % faster than with 8 warps x 4 (5.2 and
+//   6.4-6.5 TB/s), and lost with any split;
+// * two to six blocks per SM: 8 warps x 4, no split (the 4 x 8 shape leaves these SMs short of warps:
+//   6144 x 4096 ran 3.4 against 3.9 TB/s, 8192 x 1024 2.9 against 3.2);
+// * fewer blocks: 16 warps x 2, and S the smallest power of two that gives a CTA to every other SM, each
+//   warp keeping at least 2 chunks a slice: 4096 x 14336 and 4096 x 4096 unsplit (5.5 and 3.7 TB/s, 10 %
+//   and 6 % faster than 8 x 4 with S = 2), 1024 x 4096 at S = 2.
+// Smaller slices pay a per-CTA cost (launch, reductions, cluster barriers). TB200_SKINNY_SPLIT=1|2|4|8 forces
+// S and TB200_SKINNY_CFG=4x8|8x4|16x2 the kernel shape (tests, bisecting; read per call); a forced S is
+// taken where each warp keeps at least one chunk a slice.
+enum { SK_CFG_4x8 = 0, SK_CFG_8x4 = 1, SK_CFG_16x2 = 2 };
+static int skinny_plan(long long blocks, int k, int num_sms, int *S_out) {
   const int chunks = k >> 5;
+  if (num_sms <= 0) num_sms = 148;
+  const char *ce = getenv("TB200_SKINNY_CFG");
+  int cfg = blocks >= 6LL * num_sms ? SK_CFG_4x8 : blocks >= 2LL * num_sms ? SK_CFG_8x4 : SK_CFG_16x2;
+  if (ce && !strcmp(ce, "4x8")) cfg = SK_CFG_4x8;
+  if (ce && !strcmp(ce, "8x4")) cfg = SK_CFG_8x4;
+  if (ce && !strcmp(ce, "16x2")) cfg = SK_CFG_16x2;
+  const int warps = cfg == SK_CFG_4x8 ? 4 : cfg == SK_CFG_8x4 ? 8 : 16;
   const char *e = getenv("TB200_SKINNY_SPLIT");
   const int want = e && *e ? atoi(e) : 0;
-  if (want == 1 || want == 2 || want == 4 || want == 8) return chunks / want >= 16 || want == 1 ? want : 1;
-  if (num_sms <= 0) num_sms = 148;
   int S = 1;
-  while (S < 8 && blocks * S < 2LL * num_sms && chunks / (2 * S) >= 4 * SK_WARPS) S *= 2;
-  return S;
+  if (want == 1 || want == 2 || want == 4 || want == 8) {
+    S = chunks / want >= warps ? want : 1;
+  } else if (cfg == SK_CFG_16x2) {
+    while (S < 8 && blocks * S < num_sms / 2 && chunks / (2 * S) >= 2 * warps) S *= 2;
+  }
+  *S_out = S;
+  return cfg;
+}
+
+template <typename T, int W, int U>
+static cudaError_t launch_skinny_cfg(const tb200_gemm_t *g, int z0, int S, dim3 grid, cudaLaunchConfig_t cfg) {
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(W * 32, 1, 1);
+  return cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_kernel<T, W, U>, *g, z0, S);
+}
+
+template <typename T>
+static cudaError_t launch_skinny_t(const tb200_gemm_t *g, int z0, int S, int shape, dim3 grid,
+                                   const cudaLaunchConfig_t &cfg) {
+  if (shape == SK_CFG_4x8) return launch_skinny_cfg<T, 4, 8>(g, z0, S, grid, cfg);
+  if (shape == SK_CFG_8x4) return launch_skinny_cfg<T, 8, 4>(g, z0, S, grid, cfg);
+  return launch_skinny_cfg<T, 16, 2>(g, z0, S, grid, cfg);
 }
 
 extern "C" int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s) {
   if (!tb200_skinny_ok(g)) return tb200_launch_simt(g, s);
   const long long blocks = (g->m + SK_ROWS - 1) / SK_ROWS;
-  const int S = skinny_slices(blocks * (g->batch < 65535 ? g->batch : 65535), g->k, tb200_num_sms());
+  int S = 1;
+  const int shape = skinny_plan(blocks * (g->batch < 65535 ? g->batch : 65535), g->k, tb200_num_sms(), &S);
+  const int threads = shape == SK_CFG_4x8 ? 128 : shape == SK_CFG_8x4 ? 256 : 512;
   const long long gx = blocks * S;
   if (gx > 0x7fffffffLL) return (int)cudaErrorInvalidConfiguration;
   for (int z0 = 0; z0 < g->batch; z0 += 65535) {
     const unsigned gy = (unsigned)(g->batch - z0 < 65535 ? g->batch - z0 : 65535);
     if (tb200_trace())
       fprintf(stderr, "[trace] launch tb200_gemm_skinny<S=%d> grid=(%lld,%u,1) block=(%d,1,1) m=%d n=%d k=%d out=%d\n", S,
-              gx, gy, SK_T, g->m, g->n, g->k, g->out_type);
+              gx, gy, threads, g->m, g->n, g->k, g->out_type);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[2];
     int na = 0;
@@ -235,13 +267,12 @@ extern "C" int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s) {
       at[na].val.programmaticStreamSerializationAllowed = 1;
       ++na;
     }
-    cfg.gridDim = dim3((unsigned)gx, gy, 1);
-    cfg.blockDim = dim3(SK_T, 1, 1);
     cfg.stream = s;
     cfg.attrs = at;
     cfg.numAttrs = na;
-    cudaError_t e = g->in_type == TB200_F16 ? cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_kernel<__half>, *g, z0, S)
-                                            : cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_kernel<__nv_bfloat16>, *g, z0, S);
+    const dim3 grid((unsigned)gx, gy, 1);
+    cudaError_t e = g->in_type == TB200_F16 ? launch_skinny_t<__half>(g, z0, S, shape, grid, cfg)
+                                            : launch_skinny_t<__nv_bfloat16>(g, z0, S, shape, grid, cfg);
     if (e != cudaSuccess) return (int)e;
   }
   return 0;

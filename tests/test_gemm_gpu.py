@@ -152,7 +152,8 @@ def test_skinny_tails_and_epilogue(lib, h, in_t, out_t, alpha, beta):
                             seed=50))
 
 
-# the decode kernel's k split across a cluster (TB200_SKINNY_SPLIT forces the slices per 16-row block):
+# the decode kernel's shapes and its k split across a cluster (TB200_SKINNY_CFG / TB200_SKINNY_SPLIT force the
+# warps x chunks in flight and the slices per 16-row block):
 # m not a multiple of 16, k % 32 in {8, 16, 24} (the tail in the last slice), every n, alpha/beta with
 # 16-bit C, strided and pointer-array batches, and unaligned pointer-array elements (the scalar path)
 SKINNY_SPLIT_CASES = [
@@ -165,12 +166,15 @@ SKINNY_SPLIT_CASES = [
 ]
 
 
-@pytest.mark.parametrize("S", [2, 4, 8])
+@pytest.mark.parametrize("cfg", ["4x8", "8x4", "16x2"])
+@pytest.mark.parametrize("S", [1, 2, 4, 8])
 @pytest.mark.parametrize("case", SKINNY_SPLIT_CASES,
                          ids=[f"{c['m']}x{c['n']}x{c['k']}-{i}" for i, c in enumerate(SKINNY_SPLIT_CASES)])
-def test_skinny_k_split(lib, h, monkeypatch, S, case):
+def test_skinny_k_split(lib, h, monkeypatch, cfg, S, case):
+    """every kernel shape (TB200_SKINNY_CFG: warps x chunks in flight) with every k split"""
     monkeypatch.setenv("TB200_SKINNY_SPLIT", str(S))
-    assert_ok(run_and_check(lib, h, seed=case["m"] + case["k"] + S, **case), f"S={S}")
+    monkeypatch.setenv("TB200_SKINNY_CFG", cfg)
+    assert_ok(run_and_check(lib, h, seed=case["m"] + case["k"] + S, **case), f"{cfg} S={S}")
 
 
 # batch-1 decode GEMMs (cublasGemmEx): k not a multiple of 32, m not a multiple of 16, every n, alpha/beta with
