@@ -250,8 +250,9 @@ extern "C" int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s) {
   for (int z0 = 0; z0 < g->batch; z0 += 65535) {
     const unsigned gy = (unsigned)(g->batch - z0 < 65535 ? g->batch - z0 : 65535);
     if (tb200_trace())
-      fprintf(stderr, "[trace] launch tb200_gemm_skinny<S=%d> grid=(%lld,%u,1) block=(%d,1,1) m=%d n=%d k=%d out=%d\n", S,
-              gx, gy, threads, g->m, g->n, g->k, g->out_type);
+      fprintf(stderr, "[trace] launch tb200_gemm_skinny<W=%d,U=%d,S=%d> grid=(%lld,%u,1) block=(%d,1,1) m=%d n=%d k=%d out=%d\n",
+              threads / 32, shape == SK_CFG_4x8 ? 8 : shape == SK_CFG_8x4 ? 4 : 2, S, gx, gy, threads, g->m, g->n, g->k,
+              g->out_type);
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute at[2];
     int na = 0;

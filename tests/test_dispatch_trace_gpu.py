@@ -32,7 +32,8 @@ for name, m, n, k in [("q", 4096, 512, 4096), ("k", 1024, 512, 4096), ("v", 1024
 '''
 
 # projection -> (kernel configuration in the launch line, grid x) on 148 SMs (74 CTA pairs); KS=2 is the k
-# split (one cluster per tile: two CTAs, or with CG=2 two CTA pairs)
+# split (one cluster per tile: two CTAs, or with CG=2 two CTA pairs); the decode kernel's W warps x U chunks
+# in flight and S k slices
 EXPECTED = {
     "q": ("tb200_gemm_tc<f16,BN=256,KC=1,CG=2,KS=2>", 128),
     "k": ("tb200_gemm_tc<f16,BN=64,KC=2,CG=1,KS=2>", 128),
@@ -42,7 +43,7 @@ EXPECTED = {
     "up": ("tb200_gemm_tc<f16,BN=256,KC=1,CG=2>", 148),
     "down": ("tb200_gemm_tc<f16,BN=256,KC=1,CG=2,KS=2>", 128),
     "lm_head": ("tb200_gemm_tc<f16,BN=256,KC=1,CG=2>", 148),
-    "decode": ("tb200_gemm_skinny", 256),
+    "decode": ("tb200_gemm_skinny<W=16,U=2,S=1>", 256),
 }
 
 
