@@ -20,7 +20,9 @@
 //
 // Tiles: 128 x BN on one CTA (BN 32..256), or 256 x BN (BN 128 or 256) on a cluster of two CTAs with
 // tcgen05.mma.cta_group::2 (each CTA loads its 128 rows of A and half of B's BN columns; the even CTA's
-// MMA thread drives both tensor cores; each CTA drains its own rows). Work units, walked identically by
+// MMA thread drives both tensor cores; each CTA drains its own rows). For GEMMs whose tiles leave SMs
+// idle, the k split doubles the CTAs on a tile: one tile per cluster of two CTAs (or two CTA pairs), each
+// half running half of the k-blocks, the partial sums exchanged through distributed shared memory. Work units, walked identically by
 // every role: output tiles of a plain GEMM, of a strided batch (rank-3 tensor maps, batch = third
 // coordinate; stride 0 broadcasts) or of a pointer-array batch (per-element maps written on the device by
 // tb200_ptr_maps_kernel), or the per-expert tiles of a grouped GEMM (tile_coord). The epilogue can also
