@@ -158,6 +158,12 @@ cublasStatus_t tb200_moe_combine(cublasHandle_t handle, int m, const float *Cp, 
  * Pure function, pinned by host-only tests. */
 int tb200_tc_tile_n(int m, int n, int batch, int num_sms, int *pair);
 
+/* The decode kernel's shape for `blocks` 16-row blocks (m / 16 rounded up, times the batch) and depth k on
+ * `num_sms` SMs: warps per CTA, 32-wide chunks of loads each warp keeps in flight, and k slices per block
+ * (a cluster of that many CTAs; 1 = no split). Pure function of its arguments and the TB200_SKINNY_CFG /
+ * TB200_SKINNY_SPLIT knobs, pinned by host-only tests. Returns 0. */
+int tb200_skinny_shape(long long blocks, int k, int num_sms, int *warps, int *unroll, int *slices);
+
 /* cublasGemmBatchedEx for callers that cannot let a library allocate device memory. No counterpart in the
  * reference (its pointer-array path copies the arrays to the host instead).
  *

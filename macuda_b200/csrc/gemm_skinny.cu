@@ -239,6 +239,16 @@ static cudaError_t launch_skinny_t(const tb200_gemm_t *g, int z0, int S, int sha
   return launch_skinny_cfg<T, 16, 2>(g, z0, S, grid, cfg);
 }
 
+extern "C" __attribute__((visibility("default"))) int tb200_skinny_shape(long long blocks, int k, int num_sms, int *warps,
+                                                                      int *unroll, int *slices) {
+  int S = 1;
+  const int cfg = skinny_plan(blocks, k, num_sms, &S);
+  if (warps) *warps = cfg == SK_CFG_4x8 ? 4 : cfg == SK_CFG_8x4 ? 8 : 16;
+  if (unroll) *unroll = cfg == SK_CFG_4x8 ? 8 : cfg == SK_CFG_8x4 ? 4 : 2;
+  if (slices) *slices = S;
+  return 0;
+}
+
 extern "C" int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s) {
   if (!tb200_skinny_ok(g)) return tb200_launch_simt(g, s);
   const long long blocks = (g->m + SK_ROWS - 1) / SK_ROWS;

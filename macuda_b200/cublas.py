@@ -77,6 +77,7 @@ SIGNATURES = [
 EXTENSIONS = [
     ("tb200_plan", _i, [_i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     ("tb200_tc_tile_n", _i, [_i, _i, _i, _i, ctypes.POINTER(_i)]),
+    ("tb200_skinny_shape", _i, [ctypes.c_longlong, _i, _i, ctypes.POINTER(_i), ctypes.POINTER(_i), ctypes.POINTER(_i)]),
     ("tb200_device_error", _i, []),
     ("tb200_gather_row_blocks", _i, [_vp, _i, _i, _i, _i, _vp, _i, _i, _vp]),
     ("tb200_bw_write", _i, [_vp, _ll, _f, _vp]),
@@ -154,6 +155,13 @@ class CublasLib:
                                    num_sms, ctypes.byref(tn), ctypes.byref(pr))
         w = 256 + tn.value if pr.value in (1, 3) else tn.value
         return kind, (-w if pr.value >= 2 else w)
+
+    def skinny_shape(self, m, k, batch=1, num_sms=148):
+        """the decode kernel's (warps per CTA, chunks in flight per warp, k slices) for an m x n x k GEMM, n <= 8"""
+        w, u, sl = ctypes.c_int(0), ctypes.c_int(0), ctypes.c_int(0)
+        self.lib.tb200_skinny_shape((m + 15) // 16 * batch, k, num_sms, ctypes.byref(w), ctypes.byref(u),
+                                    ctypes.byref(sl))
+        return w.value, u.value, sl.value
 
     def device_error(self) -> int:
         return self.lib.tb200_device_error()

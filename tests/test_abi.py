@@ -184,6 +184,40 @@ def test_tile_choice_is_a_compiled_configuration(lib):
                 assert bn in (128, 256) and n > bn // 2
 
 
+# decode kernel shape (warps x chunks in flight, k slices) on 148 SMs, as measured best on the B200: many 16-row
+# blocks 4 x 8 unsplit, two to six per SM 8 x 4 unsplit, fewer 16 x 2 with the k split up to a CTA for every
+# other SM
+SKINNY_ROWS = [
+    ((128256, 4096, 1), (4, 8, 1)),    # config 4 lm_head: 8016 blocks
+    ((14336, 4096, 1), (4, 8, 1)),     # 896 blocks
+    ((6144, 4096, 1), (8, 4, 1)),      # 384 blocks
+    ((8192, 1024, 1), (8, 4, 1)),      # 512 blocks
+    ((4096, 4096, 1), (16, 2, 1)),     # 256 blocks
+    ((4096, 14336, 1), (16, 2, 1)),
+    ((1024, 4096, 1), (16, 2, 2)),     # 64 blocks
+    ((256, 4096, 1), (16, 2, 4)),      # 16 blocks
+    ((256, 16384, 1), (16, 2, 8)),
+    ((256, 512, 1), (16, 2, 1)),       # too shallow to split
+    ((768, 2048, 128), (4, 8, 1)),     # config 5 MoE experts as a batch of decode GEMMs
+]
+
+
+@pytest.mark.parametrize("args,want", SKINNY_ROWS, ids=[f"{a[0]}x{a[1]}xb{a[2]}" for a, _ in SKINNY_ROWS])
+def test_skinny_shape_rows(lib, monkeypatch, args, want):
+    monkeypatch.delenv("TB200_SKINNY_CFG", raising=False)
+    monkeypatch.delenv("TB200_SKINNY_SPLIT", raising=False)
+    m, k, batch = args
+    assert lib.skinny_shape(m, k, batch) == want
+
+
+def test_skinny_shape_knobs(lib, monkeypatch):
+    monkeypatch.setenv("TB200_SKINNY_CFG", "8x4")
+    monkeypatch.setenv("TB200_SKINNY_SPLIT", "4")
+    assert lib.skinny_shape(128256, 4096) == (8, 4, 4)
+    monkeypatch.setenv("TB200_SKINNY_SPLIT", "8")
+    assert lib.skinny_shape(4096, 1024) == (8, 4, 1)  # 32 chunks: 4 a slice, fewer than the 8 warps
+
+
 def test_grouped_gemm_argument_rules(lib):
     """tb200_gemm_grouped_ex refuses bad arguments before any device work (cuBLAS's rules, plus its own:
     at most 1024 groups, a device offsets array, fp32 inputs only in TF32 mode)."""
