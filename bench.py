@@ -370,6 +370,20 @@ def config_figures(torch, lib, cb, dtype_code, dtype, only=None, reps_override=N
         if "c5_moe_routed_layer_skewed" in out:
             out["c5_moe_routed_layer_skewed"]["experts_with_tokens"] = used
             out["c5_moe_routed_layer_skewed"]["launches"] = "gather + grouped up + grouped down + combine"
+
+        def layer_fused():  # the gather inside the up projection's B loads
+            st = h.gemm_grouped_gather_ex(1, Fe, n_tot, Hd, E, offs.data_ptr(), ids.data_ptr(), 1.0, Wgu.data_ptr(),
+                                          dtype_code, Hd, Fe * Hd, Xtok.data_ptr(), dtype_code, Hd, T, 0.0,
+                                          Cup.data_ptr(), f32, Fe)
+            st = st or h.gemm_grouped_ex(1, 0, Hd, n_tot, Fe, E, offs.data_ptr(), 1.0, Wd.data_ptr(), dtype_code, Fe,
+                                         Hd * Fe, Hp.data_ptr(), dtype_code, Fe, 0.0, Cdn.data_ptr(), f32, Hd)
+            return st or lib.lib.tb200_moe_combine(h.h, Hd, Cdn.data_ptr(), Hd, n_tot, d_pos.data_ptr(),
+                                                   d_w.data_ptr(), topk, T, Y.data_ptr(), Hd)
+        # the expert-order copy of the tokens is neither written nor read back
+        measure("c5_moe_routed_layer_skewed_fused", layer_fused, 10, 2 * flop5, layer_bytes - 2 * n_tot * Hd * 2, "hbm")
+        if "c5_moe_routed_layer_skewed_fused" in out:
+            out["c5_moe_routed_layer_skewed_fused"]["experts_with_tokens"] = used
+            out["c5_moe_routed_layer_skewed_fused"]["launches"] = "grouped up with the gather fused + grouped down + combine"
     del Wgu, Wd, Xe, He, Cgu, Cd, Xall, Call
 
     # config 5 squares, both 16-bit input types

@@ -139,6 +139,21 @@ cublasStatus_t tb200_gemm_grouped_ex(cublasHandle_t handle, cublasOperation_t tr
                                      cudaDataType Btype, int ldb, const void *beta, void *C, cudaDataType Ctype,
                                      int ldc, cublasComputeType_t computeType);
 
+/* tb200_gemm_grouped_ex with the token gather fused into the GEMM: column j of B is column token_ids[j] of X
+ * (k x n_src, ld ldx, op N), where token_ids is a DEVICE array of n_total ids (for a routed layer: each
+ * expert's tokens one expert after another, as tb200_moe_gather would lay them out); an id outside
+ * [0, n_src) gives a zero column of the product. Same result as tb200_moe_gather into a buffer followed by
+ * tb200_gemm_grouped_ex on it, without writing and re-reading that buffer. 16-bit A and X only, operands
+ * 16-byte aligned with lda, ldx, strideA multiples of 16 bytes; otherwise CUBLAS_STATUS_NOT_SUPPORTED.
+ * n_src < 1 or a NULL token_ids: CUBLAS_STATUS_INVALID_VALUE. It needs no n_total x k buffer for the gathered
+ * tokens, but on the B200 it runs slower than the two calls (a routed layer 202 against 175 us): the four-row
+ * gather loads move B more slowly than whole tiles of a contiguous copy. No counterpart in the reference. */
+cublasStatus_t tb200_gemm_grouped_gather_ex(cublasHandle_t handle, cublasOperation_t transa, int m, int n_total, int k,
+                                            int groups, const int *offsets, const int *token_ids, const void *alpha,
+                                            const void *A, cudaDataType Atype, int lda, long long strideA,
+                                            const void *X, cudaDataType Xtype, int ldx, int n_src, const void *beta,
+                                            void *C, cudaDataType Ctype, int ldc, cublasComputeType_t computeType);
+
 /* The data movement of a routed mixture-of-experts layer around tb200_gemm_grouped_ex, on the handle's
  * stream, deterministic, no allocation. tb200_moe_gather: column p of Xp (ld ldxp) = column token_ids[p] of X
  * (k elements of `type`, ld ldx, n_src columns) for p < n_total, which lays out each expert's tokens one

@@ -91,6 +91,11 @@ struct TcParams {
   // are numbered after those of groups 0 .. g-1, m-tile fastest
   const int *grp_off;
   int groups;
+  // grouped GEMM with the token gather fused (K-major B, single-CTA tiles of BN <= 64): column j of B is
+  // column gidx[j] of the n_src-column activations the B map covers, loaded with tile::gather4; an id
+  // outside [0, n_src) is read as column 0 and its column of the product is zero
+  const int *gidx;
+  int n_src;
 };
 
 constexpr int TC_MAX_GROUPS = TB200_MAX_GROUPS;
@@ -302,7 +307,55 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t lead_full0 = CG == 2 ? mapa_shared(smem_u32(full), pair_even) : 0u;
   const uint32_t lead_tempty0 = CG == 2 ? mapa_shared(smem_u32(tempty), pair_even) : 0u;
 
-  if (warp == 0 || warp == 6) {
+  constexpr int NG = KC * BN / 4;  // tile::gather4 loads of B per stage (fused token gather)
+  if (warp == 6 && CG == 1 && NG <= 32 && p.gidx != nullptr) {
+    // ------------------------------------------------------------------ B producer, fused token gather
+    // Lane l < NG issues one gather4 a stage: k-chunk l / (BN / 4), B rows 4 (l % (BN / 4)) .. + 3 of the
+    // tile, i.e. the tile's columns of B, each read from the source column its token id names (an id
+    // outside [0, n_src) reads column 0, and the epilogue zeroes that column; columns past n are not stored).
+    const int gc = lane / (BN / 4), gi = lane % (BN / 4);
+    int s = 0;
+    uint32_t ph = 0;
+    uint32_t issued = 0, issued_par = 0;
+    for (long long t = t_first; t < total_tiles && !*abort_flag; t += t_step) {
+      const TileCoord tc = tile_coord<BN>(p, t, g_off, g_pre);
+      int rid[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int col = tc.n0 + 4 * gi + q;
+        const int id = lane < NG && col < p.n ? __ldg(p.gidx + col) : 0;
+        rid[q] = id >= 0 && id < p.n_src ? id : 0;
+      }
+      bool ok = true;
+      for (int kb = kb_lo; kb < kb_hi; ++kb) {
+        int got = 1;
+        if (lane == 0) {
+          got = mbar_wait(&empty[s], ph ^ 1u, abort_flag, WAIT_BUDGET_CYC) ? 1 : 0;
+          if (got) mbar_arrive_expect_tx(&full[s], (uint32_t)Cfg::B_BYTES);
+        }
+        got = __shfl_sync(0xffffffffu, got, 0);  // also orders the expect_tx before every lane's copy
+        if (!got) {
+          ok = false;
+          break;
+        }
+        if (lane < NG)
+          tma_gather4(smB + s * Cfg::B_BYTES + gc * Cfg::B_ROWS * 128 + gi * 512, &tmB, &full[s],
+                      kb * p.bk + gc * p.epr, rid[0], rid[1], rid[2], rid[3]);
+        issued |= 1u << s;
+        issued_par = (issued_par & ~(1u << s)) | (ph << s);
+        if (++s == STAGES) {
+          s = 0;
+          ph ^= 1u;
+        }
+      }
+      if (!ok) break;
+    }
+    if (lane == 0 && *abort_flag) {  // let every copy still in flight land before shared memory goes away
+      volatile int no_abort = 0;
+      for (int q = 0; q < STAGES; ++q)
+        if (issued & (1u << q)) (void)mbar_wait(&full[q], (issued_par >> q) & 1u, &no_abort, DRAIN_BUDGET_CYC);
+    }
+  } else if (warp == 0 || warp == 6) {
     // ------------------------------------------------------------------ TMA producers (A: warp 0, B: warp 6)
     if (lane == 0) {
       const bool is_a = warp == 0;
@@ -480,6 +533,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
         const int col0 = n0 + c * 32;
+        if (p.gidx && col0 < tc.n_end) {  // fused gather: a column whose token id is out of range is zero
+          const int cj = col0 + lane;
+          const int id = cj < tc.n_end ? __ldg(p.gidx + cj) : 0;
+          const unsigned in_range = __ballot_sync(0xffffffffu, id >= 0 && id < p.n_src);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (!((in_range >> j) & 1u)) r[j] = 0u;
+        }
         if (row_ok && col0 < tc.n_end) {
           const int ncols = tc.n_end - col0 < 32 ? tc.n_end - col0 : 32;
           if (p.mc) {
@@ -697,6 +758,13 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   const int epr = 128 / es;
   int bn = tile_n;
   if (bn != 32 && bn != 64 && bn != 128 && bn != 256) bn = 128;
+  // the fused token gather loads B with tile::gather4 into single-CTA tiles of 32 or 64 columns, K-major
+  if (g->gidx) {
+    if (f32in || !g->groups || g->opB != 0 || ptr_ws || g->nrep || g->mc || g->n_src < 1)
+      return (int)cudaErrorNotSupported;
+    pair = 0;
+    bn = bn <= 32 ? 32 : 64;
+  }
   // pair: 0 one CTA per tile, 1 a CTA pair (2-SM UMMA), 2 one CTA per tile with the k split, 3 a CTA pair with
   // the k split
   const int cg = pair == 1 || pair == 3 ? 2 : 1;
@@ -719,7 +787,9 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   const int mbatch = ptr_ws ? 1 : g->batch;
   if (!a_mn) ok = make_map(&ta, dt, es, baseA, g->k, g->m, g->lda, mbatch, g->sA, epr, TC_BM, &p.a_batched);
   else ok = make_map(&ta, dt, es, baseA, g->m, g->k, g->lda, mbatch, g->sA, epr, epr * kc, &p.a_batched);
-  if (ok) {
+  if (ok && g->gidx) {
+    ok = make_map(&tb, dt, es, g->B, g->k, g->n_src, g->ldb, 1, 0, epr, 1, &p.b_batched);  // box one column
+  } else if (ok) {
     if (!b_mn) ok = make_map(&tb, dt, es, baseB, g->k, g->n, g->ldb, mbatch, g->sB, epr, b_rows, &p.b_batched);
     else ok = make_map(&tb, dt, es, baseB, g->n, g->k, g->ldb, mbatch, g->sB, epr, epr * kc, &p.b_batched);
   }
@@ -747,6 +817,8 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   // per group) bounds it and sizes the grid
   p.groups = g->groups;
   p.grp_off = g->grp_off;
+  p.gidx = g->gidx;
+  p.n_src = g->n_src;
   for (int q = 0; q < g->nrep && q < 8; ++q) p.rep[q] = g->rep[q];
   if (ptr_ws) {
     int *flag = (int *)ptr_ws;

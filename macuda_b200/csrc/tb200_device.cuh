@@ -166,6 +166,16 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, uint64_
       "l"((uint64_t)tmap), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
 }
+// tile::gather4: rows r0..r3 of a rank-2 map (box one row high) at column c0, into four consecutive
+// 128-byte rows of shared memory (the 128B swizzle follows the destination address, as for a tiled box)
+__device__ __forceinline__ void tma_gather4(void *dst, const void *tmap, uint64_t *bar, int c0, int r0, int r1, int r2,
+                                            int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, "
+      "%5, %6, %7}], [%2];" ::"r"(smem_u32(dst)),
+      "l"((uint64_t)tmap), "r"(smem_u32(bar)), "r"(c0), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+      : "memory");
+}
 __device__ __forceinline__ void tma_load_3d(void *dst, const void *tmap, uint64_t *bar, int c0, int c1, int c2) {
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];" ::

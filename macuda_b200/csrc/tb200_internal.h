@@ -42,6 +42,10 @@ typedef struct {
    * of groups + 1 offsets read by the kernel (batch == groups, sB == sC == 0, n = all columns) */
   const int *grp_off;
   int groups;
+  /* grouped GEMM with the token gather fused (16-bit, B under op N): column j of B is column gidx[j] of B's
+   * n_src columns (gidx a device array of n columns; an id outside [0, n_src) gives a zero column) */
+  const int *gidx;
+  int n_src;
 } tb200_gemm_t;
 
 #define TB200_MAX_GROUPS 1024

@@ -666,6 +666,59 @@ cublasStatus_t tb200_gemm_grouped_ex(cublasHandle_t handle, cublasOperation_t tr
   return CUBLAS_STATUS_SUCCESS;
 }
 
+/* tb200_gemm_grouped_ex with the token gather fused into the GEMM's B loads: column j of B is column
+ * token_ids[j] of X (k x n_src, ld ldx, under op N), so the per-expert copy of the tokens is never written.
+ * The tensor-core kernel loads four token columns per TMA (tile::gather4) into its usual shared-memory
+ * tile. 16-bit inputs only. */
+cublasStatus_t tb200_gemm_grouped_gather_ex(cublasHandle_t handle, cublasOperation_t transa, int m, int n_total, int k,
+                                            int groups, const int *offsets, const int *token_ids, const void *alpha,
+                                            const void *A, cudaDataType Atype, int lda, long long strideA,
+                                            const void *X, cudaDataType Xtype, int ldx, int n_src, const void *beta,
+                                            void *C, cudaDataType Ctype, int ldc, cublasComputeType_t computeType) {
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  if (!h) return CUBLAS_STATUS_NOT_INITIALIZED;
+  tb200_gemm_t g;
+  memset(&g, 0, sizeof g);
+  int tf32 = 0;
+  if (gemm_contract(Atype, Xtype, Ctype, computeType, &g.in_type, &g.out_type, &tf32)) return CUBLAS_STATUS_NOT_SUPPORTED;
+  g.opA = op_code(transa);
+  g.opB = 0;
+  cublasStatus_t st = check_args(g.opA, g.opB, m, n_total, k, lda, ldx, ldc, groups);
+  if (st != CUBLAS_STATUS_SUCCESS) return st;
+  if (!alpha || !beta || !offsets || !token_ids || groups > TB200_MAX_GROUPS || strideA < 0 || n_src < 1)
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (m == 0 || n_total == 0 || groups == 0) return CUBLAS_STATUS_SUCCESS;
+  if (g.in_type == TB200_F32) return CUBLAS_STATUS_NOT_SUPPORTED;
+  g.m = m;
+  g.n = n_total;
+  g.k = k;
+  g.batch = groups;
+  g.alpha = read_scalar(alpha, computeType);
+  g.beta = read_scalar(beta, computeType);
+  g.A = A; g.lda = lda; g.sA = strideA;
+  g.B = X; g.ldb = ldx;
+  g.C = C; g.ldc = ldc;
+  g.grp_off = offsets;
+  g.groups = groups;
+  g.gidx = token_ids;
+  g.n_src = n_src;
+  if (!operands_aligned(&g) || !tb200_tc_ok(&g)) return CUBLAS_STATUS_NOT_SUPPORTED;
+  int sms = tb200_num_sms(), pair = 0;
+  int avg_n = n_total / groups > 0 ? n_total / groups : 1;
+  int bn = tb200_tc_tile_n(m, avg_n, groups, sms, &pair);
+  tile_override(&bn, &pair); /* the launcher takes 32 or 64 columns, one CTA per tile */
+  if (tb200_trace())
+    fprintf(stderr, "[trace] gemm tc-grouped-gather op=%cN m=%d n_total=%d k=%d groups=%d n_src=%d BN=%d\n",
+            g.opA ? 'T' : 'N', m, n_total, k, groups, n_src, bn <= 32 ? 32 : 64);
+  int rc = tb200_launch_tc(&g, bn, pair, sms, h->stream);
+  if (rc == (int)cudaErrorNotSupported) return CUBLAS_STATUS_NOT_SUPPORTED;
+  if (rc != 0) {
+    fprintf(stderr, "[tinycublas_b200] grouped gather launch failed: %s\n", cudaGetErrorString((cudaError_t)rc));
+    return CUBLAS_STATUS_EXECUTION_FAILED;
+  }
+  return CUBLAS_STATUS_SUCCESS;
+}
+
 /* The routed layer's data movement around tb200_gemm_grouped_ex: tb200_moe_gather copies column
  * token_ids[p] of X (k elements of `type`, ld ldx, n_src columns) to column p of Xp (ld ldxp) for every
  * p < n_total, putting each expert's tokens one expert after another; tb200_moe_combine sums, for every

@@ -97,6 +97,8 @@ EXTENSIONS = [
     ("tb200_noalloc_max_batch", _i, []),
     ("tb200_gemm_grouped_ex", _i,
      [_vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _ll, _vp, _i, _i, _vp, _vp, _i, _i, _i]),
+    ("tb200_gemm_grouped_gather_ex", _i,
+     [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _i, _i, _ll, _vp, _i, _i, _i, _vp, _vp, _i, _i, _i]),
     ("tb200_moe_gather", _i, [_vp, _vp, _i, _i, _i, _i, _vp, _i, _vp, _i]),
     ("tb200_moe_combine", _i, [_vp, _i, _vp, _i, _i, _vp, _vp, _i, _i, _vp, _i]),
 ]
@@ -226,6 +228,14 @@ class Handle:
         return self.lib.tb200_gemm_grouped_ex(self.h, ta, tb, m, n_total, k, groups, offsets, ctypes.byref(a), A,
                                               Atype, lda, strideA, B, Btype, ldb, ctypes.byref(b), C, Ctype, ldc,
                                               compute_type)
+
+    def gemm_grouped_gather_ex(self, ta, m, n_total, k, groups, offsets, token_ids, alpha, A, Atype, lda, strideA, X,
+                               Xtype, ldx, n_src, beta, C, Ctype, ldc, compute_type=CUBLAS_COMPUTE_32F) -> int:
+        """tb200_gemm_grouped_gather_ex: offsets (groups + 1) and token_ids (n_total) are device int32 arrays"""
+        a, b = scalar(alpha, compute_type), scalar(beta, compute_type)
+        return self.lib.tb200_gemm_grouped_gather_ex(self.h, ta, m, n_total, k, groups, offsets, token_ids,
+                                                     ctypes.byref(a), A, Atype, lda, strideA, X, Xtype, ldx, n_src,
+                                                     ctypes.byref(b), C, Ctype, ldc, compute_type)
 
     def gemm_batched_ex(self, ta, tb, m, n, k, alpha, Aarr, Atype, lda, Barr, Btype, ldb, beta, Carr, Ctype, ldc,
                         batch, compute_type=CUBLAS_COMPUTE_32F, algo=CUBLAS_GEMM_DEFAULT) -> int:

@@ -218,6 +218,21 @@ def test_skinny_shape_knobs(lib, monkeypatch):
     assert lib.skinny_shape(4096, 1024) == (8, 4, 1)  # 32 chunks: 4 a slice, fewer than the 8 warps
 
 
+def test_grouped_gather_argument_rules(lib):
+    """tb200_gemm_grouped_gather_ex refuses bad arguments before any device work: no token ids, no source
+    columns, fp32 inputs (the fused gather is 16-bit only)."""
+    with lib.handle() as h:
+        assert h.gemm_grouped_gather_ex(1, 64, 64, 64, 2, 256, 0, 1.0, 256, cb.CUDA_R_16F, 64, 4096, 256,
+                                        cb.CUDA_R_16F, 64, 8, 0.0, 256, cb.CUDA_R_32F, 64) == cb.CUBLAS_STATUS_INVALID_VALUE
+        assert h.gemm_grouped_gather_ex(1, 64, 64, 64, 2, 256, 256, 1.0, 256, cb.CUDA_R_16F, 64, 4096, 256,
+                                        cb.CUDA_R_16F, 64, 0, 0.0, 256, cb.CUDA_R_32F, 64) == cb.CUBLAS_STATUS_INVALID_VALUE
+        assert h.gemm_grouped_gather_ex(1, 64, 64, 64, 2, 256, 256, 1.0, 256, cb.CUDA_R_32F, 64, 4096, 256,
+                                        cb.CUDA_R_32F, 64, 8, 0.0, 256, cb.CUDA_R_32F, 64,
+                                        cb.CUBLAS_COMPUTE_32F_FAST_TF32) == cb.CUBLAS_STATUS_NOT_SUPPORTED
+        assert h.gemm_grouped_gather_ex(1, 64, 64, 64, 2, 256, 256, 1.0, 256, cb.CUDA_R_16F, 32, 4096, 256,
+                                        cb.CUDA_R_16F, 64, 8, 0.0, 256, cb.CUDA_R_32F, 64) == cb.CUBLAS_STATUS_INVALID_VALUE
+
+
 def test_grouped_gemm_argument_rules(lib):
     """tb200_gemm_grouped_ex refuses bad arguments before any device work (cuBLAS's rules, plus its own:
     at most 1024 groups, a device offsets array, fp32 inputs only in TF32 mode)."""

@@ -420,6 +420,69 @@ def _grouped_case(lib, h, rng, m, k, counts, in_t=O.F16, out_t=O.F32, alpha=1.0,
         assert res["ok"], f"group {g} (columns {c0}..{c1}): {res}"
 
 
+def _grouped_gather_case(lib, h, rng, m, k, counts, n_src, ids=None, in_t=O.F16, out_t=O.F32, alpha=1.0, beta=0.0,
+                         opA=1, guard=64):
+    """One tb200_gemm_grouped_gather_ex call (B = columns ids of X, fused): every group's columns checked
+    against the oracle run on the gathered B (zero columns for ids outside [0, n_src)), and a guard region
+    after C checked untouched."""
+    import torch
+    G = len(counts)
+    offs = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    n_total = int(np.sum(counts))
+    ids = rng.integers(0, n_src, n_total).astype(np.int32) if ids is None else np.asarray(ids, np.int32)
+    lda = k if opA == 1 else m
+    A = storage(rng, G * m * k, in_t, 0.02)
+    X = storage(rng, k * n_src, in_t)
+    C0 = storage(rng, m * n_total + guard, out_t)
+    dA, dX, dC = dev(A), dev(X), dev(C0)
+    d_off, d_ids = torch.from_numpy(offs).cuda(), torch.from_numpy(ids).cuda()
+    ct = {O.F16: cb.CUDA_R_16F, O.BF16: cb.CUDA_R_16BF, O.F32: cb.CUDA_R_32F}
+    st = h.gemm_grouped_gather_ex(opA, m, n_total, k, G, d_off.data_ptr(), d_ids.data_ptr(), alpha, dA.data_ptr(),
+                                  ct[in_t], lda, m * k, dX.data_ptr(), ct[in_t], k, n_src, beta, dC.data_ptr(),
+                                  ct[out_t], m)
+    torch.cuda.synchronize()
+    assert st == cb.CUBLAS_STATUS_SUCCESS, st
+    C = host(dC, C0)
+    assert np.array_equal(C[m * n_total:], C0[m * n_total:]), "the guard region after C was written"
+    Xc = X.reshape(n_src, k)
+    B = np.stack([Xc[t] if 0 <= t < n_src else np.zeros(k, Xc.dtype) for t in ids]).ravel() if n_total else Xc[:0].ravel()
+    rows = np.unique(np.concatenate([np.arange(0, m, 11), [m - 1]])).astype(np.int32)
+    for g in range(G):
+        c0, c1 = int(offs[g]), int(offs[g + 1])
+        if c1 <= c0:
+            continue
+        n = c1 - c0
+        R, S = O.gemm(opA, 0, m, n, k, alpha, A[g * m * k:(g + 1) * m * k], in_t, lda, B[c0 * k:c1 * k], in_t, k,
+                      beta, C0[c0 * m:c1 * m], out_t, m, rows=rows)
+        res = O.check(O.extract(C[c0 * m:c1 * m], out_t, m, n, m, rows=rows), R, S, out_t)
+        assert res["ok"], f"group {g} (columns {c0}..{c1}): {res}"
+
+
+@pytest.mark.parametrize("bn", ["32", "64"])
+def test_grouped_gather_moe_routing(lib, h, monkeypatch, bn):
+    """The fused gather on config 5's expert shape (768 x 2048, 128 experts, 4096 routed copies of 512
+    tokens): skewed counts with empty experts, every tile width the fused path takes."""
+    monkeypatch.setenv("TB200_TC_BN", bn)
+    rng = np.random.default_rng(160)
+    counts = rng.multinomial(4096, rng.dirichlet(np.full(128, 0.3)))
+    counts[[0, 17, 127]] = 0
+    _grouped_gather_case(lib, h, rng, 768, 2048, counts, n_src=512)
+
+
+@pytest.mark.parametrize("in_t,out_t,alpha,beta,opA", [(O.BF16, O.F32, 1.0, 0.0, 1), (O.F16, O.F16, 0.5, 0.75, 1),
+                                                       (O.F16, O.F32, 1.0, 0.0, 0)])
+def test_grouped_gather_types_epilogue_majors_and_bad_ids(lib, h, in_t, out_t, alpha, beta, opA):
+    """tails in m, n and k (k = 200: the last k-chunk half outside X), empty groups, and token ids outside
+    [0, n_src) - negative, n_src itself, far past it - which give zero columns (C = beta C0 there)."""
+    rng = np.random.default_rng(161)
+    counts = [37, 0, 70, 1, 64, 29]
+    n_src = 90
+    ids = rng.integers(0, n_src, sum(counts)).astype(np.int32)
+    ids[[0, 5, 40, 100, 200]] = [-1, n_src, 1 << 30, -(1 << 30), n_src - 1]
+    _grouped_gather_case(lib, h, rng, 1000, 200, counts, n_src, ids=ids, in_t=in_t, out_t=out_t, alpha=alpha,
+                         beta=beta, opA=opA)
+
+
 def test_grouped_gemm_moe_unbalanced_routing(lib, h):
     """Config 5's expert shape (768 x 2048, 128 experts) with 4096 routed tokens spread unevenly: skewed
     counts, empty experts included, each expert's n different and mostly not a multiple of the tile."""

@@ -1,6 +1,7 @@
 """A routed mixture-of-experts layer through the library's extension entry points: tokens gathered into
 expert order (tb200_moe_gather), every expert in one grouped GEMM with its own token count
-(tb200_gemm_grouped_ex), expert outputs combined back into token order with the routing weights
+(tb200_gemm_grouped_ex) - or both in one launch with the gather fused into the GEMM's loads
+(tb200_gemm_grouped_gather_ex) - expert outputs combined back into token order with the routing weights
 (tb200_moe_combine); checked against an fp64 restatement of the layer, Y[:, t] = sum_j w_tj W_{e_tj}^T x_t."""
 import numpy as np
 import pytest
@@ -37,8 +38,9 @@ def _routing(rng, T, E, topk):
     return experts, w, token_ids, offsets, positions.reshape(T, topk)
 
 
+@pytest.mark.parametrize("fused", [False, True], ids=["gather+grouped", "grouped_gather"])
 @pytest.mark.parametrize("in_t", [O.F16, O.BF16])
-def test_routed_moe_layer(lib, h, in_t):
+def test_routed_moe_layer(lib, h, in_t, fused):
     import torch
     rng = np.random.default_rng(400)
     E, topk, T, Hd, F = 32, 4, 384, 1024, 512
@@ -57,9 +59,14 @@ def test_routed_moe_layer(lib, h, in_t):
     C = torch.full((F * n_total,), float("nan"), device="cuda")
     Y = torch.full((F * T,), float("nan"), device="cuda")
     L = lib.lib
-    assert L.tb200_moe_gather(h.h, dX.data_ptr(), ct, Hd, Hd, T, d_ids.data_ptr(), n_total, Xp.data_ptr(), Hd) == 0
-    assert h.gemm_grouped_ex(1, 0, F, n_total, Hd, E, d_off.data_ptr(), 1.0, dW.data_ptr(), ct, Hd, F * Hd,
-                             Xp.data_ptr(), ct, Hd, 0.0, C.data_ptr(), cb.CUDA_R_32F, F) == 0
+    if fused:  # the gather inside the grouped GEMM's B loads
+        assert h.gemm_grouped_gather_ex(1, F, n_total, Hd, E, d_off.data_ptr(), d_ids.data_ptr(), 1.0, dW.data_ptr(),
+                                        ct, Hd, F * Hd, dX.data_ptr(), ct, Hd, T, 0.0, C.data_ptr(), cb.CUDA_R_32F,
+                                        F) == 0
+    else:
+        assert L.tb200_moe_gather(h.h, dX.data_ptr(), ct, Hd, Hd, T, d_ids.data_ptr(), n_total, Xp.data_ptr(), Hd) == 0
+        assert h.gemm_grouped_ex(1, 0, F, n_total, Hd, E, d_off.data_ptr(), 1.0, dW.data_ptr(), ct, Hd, F * Hd,
+                                 Xp.data_ptr(), ct, Hd, 0.0, C.data_ptr(), cb.CUDA_R_32F, F) == 0
     assert L.tb200_moe_combine(h.h, F, C.data_ptr(), F, n_total, d_pos.data_ptr(), d_w.data_ptr(), topk, T,
                                Y.data_ptr(), F) == 0
     torch.cuda.synchronize()
