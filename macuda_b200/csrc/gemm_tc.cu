@@ -317,7 +317,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     int s = 0;
     uint32_t ph = 0;
     uint32_t issued = 0, issued_par = 0;
-    for (long long t = t_first; t < total_tiles && !*abort_flag; t += t_step) {
+    for (long long t = t_first; t < total_tiles; t += t_step) {
+      // lane 0 reads the abort flag for the warp: every lane leaves the loop on the same tile (the loop
+      // body's shuffles need all 32)
+      const int go = __shfl_sync(0xffffffffu, lane == 0 ? (*abort_flag ? 0 : 1) : 0, 0);
+      if (!go) break;
       const TileCoord tc = tile_coord<BN>(p, t, g_off, g_pre);
       int rid[4];
 #pragma unroll
