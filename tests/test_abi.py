@@ -218,6 +218,33 @@ def test_skinny_shape_knobs(lib, monkeypatch):
     assert lib.skinny_shape(4096, 1024) == (8, 4, 1)  # 32 chunks: 4 a slice, fewer than the 8 warps
 
 
+def test_k_split_plan_properties(lib):
+    """Over a grid of shapes and SM counts: the planner picks the k split (a negative width) only for 16-bit
+    strided GEMMs with k >= 1024, with one tile per cluster fitting on the SMs (two CTAs per 128-row tile, or
+    two CTA pairs per 256 x 256 tile), a tile at least half full; pointer arrays and fp32 never split."""
+    seen = 0
+    for sms in (132, 148, 160):
+        for m in (256, 1024, 2048, 4096, 14336):
+            for n in (16, 64, 128, 200, 512, 2048):
+                for k in (512, 1024, 4096, 14336):
+                    for batch in (1, 4):
+                        kind, w = lib.plan(1, 0, m, n, k, batch, 1, 0, 0, 0, 1, sms)
+                        assert kind == cb.TB200_KERNEL_SKINNY if n <= 8 else kind == cb.TB200_KERNEL_TC
+                        if w < 0:
+                            seen += 1
+                            width = -w
+                            pair = width > 256
+                            bn = width - 256 if pair else width
+                            rows = 256 if pair else 128
+                            tiles = -(-m // rows) * -(-n // bn) * batch
+                            assert k >= 1024 and bn in (64, 128, 256) and n > bn // 2
+                            assert tiles * (4 if pair else 2) <= sms, (m, n, k, batch, sms, w)
+                        # the same GEMM through pointer arrays, or in fp32 with TF32, never splits
+                        assert lib.plan(1, 0, m, n, k, batch, 1, 0, 0, 1, 1, sms)[1] >= 0
+                        assert lib.plan(1, 0, m, n, k, batch, 0, 0, 1, 0, 1, sms)[1] >= 0
+    assert seen > 20
+
+
 def test_grouped_gather_argument_rules(lib):
     """tb200_gemm_grouped_gather_ex refuses bad arguments before any device work: no token ids, no source
     columns, fp32 inputs (the fused gather is 16-bit only)."""
