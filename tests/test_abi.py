@@ -210,6 +210,26 @@ def test_skinny_shape_rows(lib, monkeypatch, args, want):
     assert lib.skinny_shape(m, k, batch) == want
 
 
+def test_skinny_shape_properties(lib, monkeypatch):
+    """Over a grid of block counts, depths and SM counts: 4 x 8 from six blocks per SM, 8 x 4 from two, 16 x 2
+    below; only the 16 x 2 shape splits k, and a split keeps at least 2 chunks of 32 per warp a slice and
+    stops once the CTAs reach half the SMs."""
+    monkeypatch.delenv("TB200_SKINNY_CFG", raising=False)
+    monkeypatch.delenv("TB200_SKINNY_SPLIT", raising=False)
+    for sms in (132, 148):
+        for blocks in (1, 7, 16, 64, 73, 74, 200, 295, 296, 500, 887, 888, 5000):
+            for k in (8, 256, 1024, 4096, 14336, 65536):
+                w, u, S = lib.skinny_shape(blocks * 16, k, 1, sms)
+                if blocks >= 6 * sms:
+                    assert (w, u, S) == (4, 8, 1)
+                elif blocks >= 2 * sms:
+                    assert (w, u, S) == (8, 4, 1)
+                else:
+                    assert (w, u) == (16, 2) and S in (1, 2, 4, 8)
+                    if S > 1:
+                        assert (k // 32) // S >= 2 * 16 and blocks * (S // 2) < sms // 2
+
+
 def test_skinny_shape_knobs(lib, monkeypatch):
     monkeypatch.setenv("TB200_SKINNY_CFG", "8x4")
     monkeypatch.setenv("TB200_SKINNY_SPLIT", "4")
