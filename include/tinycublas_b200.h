@@ -182,20 +182,19 @@ int tb200_skinny_shape(long long blocks, int k, int num_sms, int *warps, int *un
 /* cublasGemmBatchedEx for callers that cannot let a library allocate device memory. No counterpart in the
  * reference (its pointer-array path copies the arrays to the host instead).
  *
- * Who needs it: code that must not call cudaMalloc while it runs - a stream capture in global capture
- * mode, where cudaMalloc is not permitted; a server that has given all device memory to its own
- * allocator up front, where a library's cudaMalloc fails or fragments it; a latency-critical loop that
- * cannot afford the implicit synchronisation cudaMalloc and cudaFree bring. cublasGemmBatchedEx itself
- * allocates device scratch once per (handle, stream) for pointer arrays on the tensor cores.
+ * Who needs it: a server that has handed all device memory to its own allocator up front, where a library's
+ * cudaMalloc fails or fragments that memory; a latency-critical loop that cannot afford the implicit
+ * synchronisation cudaMalloc and cudaFree bring. cublasGemmBatchedEx itself allocates device scratch once per
+ * (handle, stream) for pointer arrays on the tensor cores.
  *
- * Same arguments and results as cublasGemmBatchedEx; it allocates nothing. Where device scratch is
- * needed it uses one fixed array inside the library (256 KB + 256 B, held by every GPU that loads the
- * library until the process exits), so batchCount is limited to tb200_noalloc_max_batch() (1024):
+ * Same arguments (minus algo), plan and results as cublasGemmBatchedEx; it allocates nothing. Where device
+ * scratch is needed it uses one fixed array inside the library (256 KB + 256 B, held by every GPU that loads
+ * the library until the process exits), so batchCount is limited to tb200_noalloc_max_batch() (1024):
  * larger batches return CUBLAS_STATUS_INVALID_VALUE with a message on stderr.
- * The first call on a device looks up that array's device address (cudaGetSymbolAddress): make it
- * before any stream capture. All calls share the array and it keeps the last call's contents (each call
- * rewrites what it uses): calls whose launches overlap on the GPU - on different streams, or from
- * different threads - race on it; serialise them. */
+ * The first call on a device looks up that array's device address (cudaGetSymbolAddress): make it before
+ * any stream capture. All calls share the array and it keeps the last call's contents (each call clears the
+ * flag that must start at zero and rewrites the tensor maps it uses): calls whose launches overlap on the GPU
+ * - on different streams, or from different threads - race on it; serialise them. */
 cublasStatus_t tb200_gemm_batched_ex_noalloc(cublasHandle_t handle, cublasOperation_t transa,
                                              cublasOperation_t transb, int m, int n, int k, const void *alpha,
                                              const void *const Aarray[], cudaDataType Atype, int lda,
@@ -205,6 +204,12 @@ cublasStatus_t tb200_gemm_batched_ex_noalloc(cublasHandle_t handle, cublasOperat
 
 /* The largest batchCount tb200_gemm_batched_ex_noalloc accepts. */
 int tb200_noalloc_max_batch(void);
+
+/* Test hook for tb200_gemm_batched_ex_noalloc (no counterpart in the reference): waits for the device and
+ * returns 1 when the last such call on the current device found a batch pointer unfit for the tensor cores'
+ * TMA loads (not 16-byte aligned; the general kernel then computed the batch), 0 when its tensor-core launch
+ * computed it, -1 on error. */
+int tb200_noalloc_last_fallback(void);
 
 /* Device scratch allocations this handle has made so far (test hook, the counterpart of the reference's
  * tinycublas_splitk_ws_allocs, cublas.c:91-92). The library allocates scratch only for pointer-array
@@ -256,6 +261,18 @@ cublasStatus_t tb200_ipc_alloc(size_t bytes, void **ptr, void *handle);
 cublasStatus_t tb200_ipc_open(const void *handle, void **ptr);
 cublasStatus_t tb200_ipc_close(void *ptr);
 cublasStatus_t tb200_ipc_free(void *ptr);
+
+/* The exchange step of a sharded GEMM on the copy engines (no counterpart in the reference, which is
+ * single-GPU): copies this rank's block of C - rows [row0, row0 + rows) of columns [col0, col0 + ncols) of
+ * replicas[self] (elem_bytes per element, leading dimension ldc, column-major) - into the same place of every
+ * other replica (peers' C mapped with tb200_ipc_open), one cudaMemcpy2DAsync per peer, peer q's on
+ * streams[q % nstreams]. No kernel and no SM time: the copies overlap the GEMMs that run meanwhile on other
+ * streams. The caller orders the copies after the GEMM that wrote the block (an event), and every rank's
+ * reads of its C after all peers' copies (a collective after the copies' streams). A contiguous batch slab
+ * is the case ldc = rows = the slab's length, ncols = 1. */
+cublasStatus_t tb200_push_block(void *const *replicas, int P, int self, long long row0, long long rows, long long col0,
+                                long long ncols, long long ldc, int elem_bytes, const cudaStream_t *streams,
+                                int nstreams);
 
 /* HBM probes, the counterparts of gemm.cu:421-431: stream n4 16-byte writes of v, or n4 16-byte
  * reads folded into *sink. Asynchronous on `stream`. */

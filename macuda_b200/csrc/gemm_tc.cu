@@ -947,23 +947,36 @@ extern "C" __attribute__((visibility("default"))) int tb200_device_error(void) {
 static __device__ __align__(256) unsigned char g_tb200_noalloc_scratch[256 + TB200_NOALLOC_MAX_BATCH * 256];
 
 // The host-side name g_tb200_noalloc_scratch is only a stand-in for the symbol, never a device address:
-// the device address comes from cudaGetSymbolAddress, looked up once per device with that device current.
+// the device address comes from cudaGetSymbolAddress, looked up with the device current. The first call on
+// each of the first 64 device ordinals caches it (an atomic store, so concurrent first calls agree); higher
+// ordinals look it up on every call. The cache is not rebuilt after cudaDeviceReset, which unloads the
+// library's device image: a process that resets a device must not call this entry point on it afterwards.
 static void *noalloc_scratch(void) {
   static void *addr[64];
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
-  if (!addr[dev]) {
-    void *p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_tb200_noalloc_scratch);
-    if (e != cudaSuccess || !p) {
-      fprintf(stderr, "[tinycublas_b200] cudaGetSymbolAddress(scratch) failed on device %d: %s\n", dev,
-              cudaGetErrorString(e));
-      (void)cudaGetLastError();
-      return nullptr;
-    }
-    addr[dev] = p;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return nullptr;
+  void *cached = dev < 64 ? __atomic_load_n(&addr[dev], __ATOMIC_ACQUIRE) : nullptr;
+  if (cached) return cached;
+  void *p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_tb200_noalloc_scratch);
+  if (e != cudaSuccess || !p) {
+    fprintf(stderr, "[tinycublas_b200] cudaGetSymbolAddress(scratch) failed on device %d: %s\n", dev,
+            cudaGetErrorString(e));
+    (void)cudaGetLastError();
+    return nullptr;
   }
-  return addr[dev];
+  if (dev < 64) __atomic_store_n(&addr[dev], p, __ATOMIC_RELEASE);
+  return p;
+}
+
+// Test hook: 1 when the last allocation-free call on the current device found some batch pointer unfit for
+// TMA (the general kernel then ran the batch), 0 when its tensor-core launch ran, -1 on error. Waits for the
+// device.
+extern "C" __attribute__((visibility("default"))) int tb200_noalloc_last_fallback(void) {
+  int v = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&v, g_tb200_noalloc_scratch, sizeof v) != cudaSuccess) return -1;
+  return v != 0 ? 1 : 0;
 }
 
 extern "C" __attribute__((visibility("default"))) int tb200_noalloc_max_batch(void) { return TB200_NOALLOC_MAX_BATCH; }

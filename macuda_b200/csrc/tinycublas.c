@@ -311,7 +311,10 @@ static const char *kernel_name(int kind) {
   return kind == TB200_KERNEL_SKINNY ? "skinny" : kind == TB200_KERNEL_TC ? "tc" : kind == TB200_KERNEL_SIMT ? "simt" : "none";
 }
 
-static cublasStatus_t run_gemm(struct tb200_handle *h, tb200_gemm_t *g) {
+/* Plans and launches one validated GEMM on the handle's stream. A pointer-array batch on the tensor cores needs
+ * scratch for its per-element tensor maps: the handle's per-stream buffer (allocated on first use), or with
+ * noalloc the library's fixed device array (tb200_gemm_batched_ex_noalloc). */
+static cublasStatus_t run_gemm_with(struct tb200_handle *h, tb200_gemm_t *g, int noalloc) {
   int tile_n = 0, pair = 0;
   int aligned = operands_aligned(g);
   int ptr_array = g->Aarr != NULL;
@@ -320,15 +323,18 @@ static cublasStatus_t run_gemm(struct tb200_handle *h, tb200_gemm_t *g) {
                         aligned, sms, &tile_n, &pair);
   if (kind == TB200_KERNEL_TC) tile_override(&tile_n, &pair);
   if (tb200_trace())
-    fprintf(stderr, "[trace] gemm %s op=%c%c m=%d n=%d k=%d batch=%d in=%d out=%d tf32=%d ptr=%d aligned=%d BN=%d pair=%d\n",
-            kernel_name(kind), g->opA ? 'T' : 'N', g->opB ? 'T' : 'N', g->m, g->n, g->k, g->batch, g->in_type,
-            g->out_type, g->tf32, ptr_array, aligned, tile_n, pair);
+    fprintf(stderr, "[trace] gemm%s %s op=%c%c m=%d n=%d k=%d batch=%d in=%d out=%d tf32=%d ptr=%d aligned=%d BN=%d pair=%d\n",
+            noalloc ? "-noalloc" : "", kernel_name(kind), g->opA ? 'T' : 'N', g->opB ? 'T' : 'N', g->m, g->n, g->k,
+            g->batch, g->in_type, g->out_type, g->tf32, ptr_array, aligned, tile_n, pair);
   int rc = 0;
   switch (kind) {
     case TB200_KERNEL_NONE: return CUBLAS_STATUS_SUCCESS;
-    case TB200_KERNEL_SKINNY: rc = tb200_launch_skinny(g, h->stream); break;
+    case TB200_KERNEL_SKINNY: rc = tb200_launch_skinny(g, h->stream); break; /* no scratch */
     case TB200_KERNEL_TC:
-      if (ptr_array) {
+      if (ptr_array && noalloc) {
+        rc = tb200_launch_tc_ptr_noalloc(g, tile_n, pair, sms, h->stream);
+        if (rc == (int)cudaErrorNotSupported) rc = tb200_launch_simt(g, h->stream);
+      } else if (ptr_array) {
         void *ws = handle_scratch(h, tb200_tc_ptr_ws_bytes(g->batch));
         rc = ws ? tb200_launch_tc_ptr(g, tile_n, pair, sms, ws, h->stream) : (int)cudaErrorNotSupported;
         if (rc == (int)cudaErrorNotSupported) rc = tb200_launch_simt(g, h->stream); /* no scratch: general kernel */
@@ -339,11 +345,14 @@ static cublasStatus_t run_gemm(struct tb200_handle *h, tb200_gemm_t *g) {
     default: rc = tb200_launch_simt(g, h->stream); break;
   }
   if (rc != 0) {
-    fprintf(stderr, "[tinycublas_b200] %s launch failed: %s\n", kernel_name(kind), cudaGetErrorString((cudaError_t)rc));
+    fprintf(stderr, "[tinycublas_b200] %s%s launch failed: %s\n", noalloc ? "tb200_gemm_batched_ex_noalloc: " : "",
+            kernel_name(kind), cudaGetErrorString((cudaError_t)rc));
     return CUBLAS_STATUS_EXECUTION_FAILED;
   }
   return CUBLAS_STATUS_SUCCESS;
 }
+
+static cublasStatus_t run_gemm(struct tb200_handle *h, tb200_gemm_t *g) { return run_gemm_with(h, g, 0); }
 
 static int op_code(cublasOperation_t op) { return op == CUBLAS_OP_N ? 0 : op == CUBLAS_OP_T ? 1 : -1; }
 static int imax(int a, int b) { return a > b ? a : b; }
@@ -752,9 +761,10 @@ cublasStatus_t tb200_moe_combine(cublasHandle_t handle, int m, const float *Cp, 
   return rc == 0 ? CUBLAS_STATUS_SUCCESS : CUBLAS_STATUS_EXECUTION_FAILED;
 }
 
-/* cublasGemmBatchedEx without any device allocation: same arguments, same results; where the pointer-array
- * tensor-core path needs scratch it takes the library's fixed device array (tb200_launch_tc_ptr_noalloc)
- * instead of the handle's lazily allocated buffer. batchCount is bounded by that array. */
+/* cublasGemmBatchedEx without any device allocation: same arguments, same plan and kernels (the dispatch above,
+ * knobs included); where the pointer-array tensor-core path needs scratch it takes the library's fixed device
+ * array (tb200_launch_tc_ptr_noalloc) instead of the handle's lazily allocated buffer. batchCount is bounded
+ * by that array. */
 cublasStatus_t tb200_gemm_batched_ex_noalloc(cublasHandle_t handle, cublasOperation_t transa,
                                              cublasOperation_t transb, int m, int n, int k, const void *alpha,
                                              const void *const Aarray[], cudaDataType Atype, int lda,
@@ -791,26 +801,7 @@ cublasStatus_t tb200_gemm_batched_ex_noalloc(cublasHandle_t handle, cublasOperat
   g.Aarr = Aarray; g.lda = lda;
   g.Barr = Barray; g.ldb = ldb;
   g.Carr = Carray; g.ldc = ldc;
-  int tile_n = 0, pair = 0;
-  int sms = tb200_num_sms();
-  int kind = tb200_plan(g.opA, g.opB, m, n, k, batchCount, g.in_type, g.out_type, g.tf32, 1, operands_aligned(&g),
-                        sms, &tile_n, &pair);
-  if (tb200_trace())
-    fprintf(stderr, "[trace] gemm-noalloc %s m=%d n=%d k=%d batch=%d BN=%d pair=%d\n", kernel_name(kind), m, n, k,
-            batchCount, tile_n, pair);
-  int rc = 0;
-  if (kind == TB200_KERNEL_NONE) return CUBLAS_STATUS_SUCCESS;
-  if (kind == TB200_KERNEL_SKINNY) rc = tb200_launch_skinny(&g, h->stream); /* no scratch */
-  else if (kind == TB200_KERNEL_TC) {
-    rc = tb200_launch_tc_ptr_noalloc(&g, tile_n, pair, sms, h->stream);
-    if (rc == (int)cudaErrorNotSupported) rc = tb200_launch_simt(&g, h->stream);
-  } else rc = tb200_launch_simt(&g, h->stream);
-  if (rc != 0) {
-    fprintf(stderr, "[tinycublas_b200] tb200_gemm_batched_ex_noalloc launch failed: %s\n",
-            cudaGetErrorString((cudaError_t)rc));
-    return CUBLAS_STATUS_EXECUTION_FAILED;
-  }
-  return CUBLAS_STATUS_SUCCESS;
+  return run_gemm_with(h, &g, 1);
 }
 
 const char *tb200_version(void) { return "tinycublas_b200 " TB200_GIT_DESCRIBE " sm_100a"; }

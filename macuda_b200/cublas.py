@@ -4,7 +4,7 @@ This is the host-side mirror of the reference's interface for the GEMM path: the
 (cublasCreate/Destroy/SetStream/SetMathMode, cublasGemmEx, cublasSgemm, cublasGemmStridedBatchedEx,
 cublasGemmBatchedEx, ...; reference cuda-shim/libtinycublas/cublas.c:242-333), the same argument
 meaning and the same status codes. It is what a Python caller (or a test) uses in place of a C
-caller such as ggml-cuda; INTEGRATION.md shows the equivalent C link line.
+caller such as ggml-cuda (a C caller links -ltinycublas_b200 in place of -lcublas).
 
 `CublasLib(path)` binds any library with that ABI, so the same code drives this library and, in the
 tests and the benchmark's reference arm, the reference's own library built from its sources.
@@ -91,10 +91,12 @@ EXTENSIONS = [
     ("tb200_ipc_open", _i, [_vp, ctypes.POINTER(_vp)]),
     ("tb200_ipc_close", _i, [_vp]),
     ("tb200_ipc_free", _i, [_vp]),
+    ("tb200_push_block", _i, [_vp, _i, _i, _ll, _ll, _ll, _ll, _ll, _i, _vp, _i]),
     ("tb200_scratch_allocs", ctypes.c_uint, [_vp]),
     ("tb200_gemm_batched_ex_noalloc", _i,
      [_vp, _i, _i, _i, _i, _i, _vp, _vp, _i, _i, _vp, _i, _i, _vp, _vp, _i, _i, _i, _i]),
     ("tb200_noalloc_max_batch", _i, []),
+    ("tb200_noalloc_last_fallback", _i, []),
     ("tb200_gemm_grouped_ex", _i,
      [_vp, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _i, _i, _ll, _vp, _i, _i, _vp, _vp, _i, _i, _i]),
     ("tb200_gemm_grouped_gather_ex", _i,

@@ -11,8 +11,12 @@ CUDA_TYPE = {O.F32: cb.CUDA_R_32F, O.F16: cb.CUDA_R_16F, O.BF16: cb.CUDA_R_16BF}
 
 
 def storage(rng, count: int, t: int, sigma: float = 1.0) -> np.ndarray:
-    """count values N(0, sigma^2), rounded to type t (float32 array, or uint16 bit patterns)."""
-    return O.to_bits(rng.normal(0.0, sigma, count).astype(np.float32), t)
+    """count values N(0, sigma^2), rounded to type t (float32 array, or uint16 bit patterns). Drawn in
+    float32 (BASELINE-size operands hold up to 525M values)."""
+    x = rng.standard_normal(count, dtype=np.float32)
+    if sigma != 1.0:
+        x *= np.float32(sigma)
+    return O.to_bits(x, t)
 
 
 def dev(a: np.ndarray):
@@ -32,20 +36,34 @@ def ptr_table(ptrs):
     return torch.tensor(list(ptrs), dtype=torch.int64, device="cuda")
 
 
-def sample_idx(rng, size: int, cap: int):
-    """all indices when small, else a seeded sample that always includes both ends"""
+def sample_idx(rng, size: int, cap: int, extra=()):
+    """all indices when small, else a seeded sample that always includes both ends and `extra`"""
     if size <= cap:
         return None
-    idx = np.unique(np.concatenate([[0, size - 1], rng.choice(size, cap - 2, replace=False)]))
+    extra = [int(e) for e in extra if 0 <= int(e) < size]
+    idx = np.unique(np.concatenate([[0, size - 1], extra, rng.choice(size, cap - 2, replace=False)]))
     return idx.astype(np.int32)
+
+
+def tile_edges(size: int, tiles=(32, 64, 128, 256)):
+    """indices on both sides of the last boundary of every tile width: the first and last row (or column) of
+    each width's last, possibly partial, tile and the one before it"""
+    out = set()
+    for t in tiles:
+        last = (size - 1) // t * t
+        out.update({last - 1, last, min(size - 1, last + t - 1), last - t})
+    return sorted(i for i in out if 0 <= i < size)
 
 
 def run_and_check(lib, h, *, opA=1, opB=0, m, n, k, in_t=O.F16, out_t=O.F32, alpha=1.0, beta=0.0, batch=1,
                   lda=None, ldb=None, ldc=None, sA=None, sB=None, sC=None, mode="strided", seed=0,
-                  compute=cb.CUBLAS_COMPUTE_32F, a_sigma=0.02, sample=256, c_offset=0, broadcast_a=1, a_ptr_shift=0):
+                  compute=cb.CUBLAS_COMPUTE_32F, a_sigma=0.02, sample=256, c_offset=0, broadcast_a=1, a_ptr_shift=0,
+                  edges=False):
     """Build seeded operands, run one GEMM through the library's C ABI, check it against the oracle.
     mode: 'ex' (cublasGemmEx, batch 1), 'strided' (cublasGemmStridedBatchedEx), 'ptr' (cublasGemmBatchedEx,
-    A pointers repeated `broadcast_a` times, as for GQA). Returns the check dict (plus the status)."""
+    A pointers repeated `broadcast_a` times, as for GQA). Large shapes are checked on seeded row/column samples
+    (`sample` of each); edges=True adds the rows and columns around the last boundary of every tile width.
+    Returns the check dict (plus the status)."""
     import torch
     rng = np.random.default_rng(seed)
     a_rows, a_cols = (m, k) if opA == 0 else (k, m)
@@ -85,8 +103,8 @@ def run_and_check(lib, h, *, opA=1, opB=0, m, n, k, in_t=O.F16, out_t=O.F32, alp
     if st != 0:
         return {"ok": False, "status": st}
     got_all = host(dC, C0)[c_offset:]
-    rows = sample_idx(rng, m, sample)
-    cols = sample_idx(rng, n, sample)
+    rows = sample_idx(rng, m, sample, tile_edges(m) if edges else ())
+    cols = sample_idx(rng, n, sample, tile_edges(n) if edges else ())
     C0v = C0[c_offset:]
     if mode == "ptr":
         A_list = [A[o:o + lda * a_cols] for o in a_off]

@@ -1,14 +1,19 @@
 """tb200_gemm_batched_ex_noalloc: cublasGemmBatchedEx for callers that must not have the library allocate
-device memory (a global-mode stream capture, where cudaMalloc is not allowed; a server whose allocator
-owns all device memory; a loop that cannot take cudaMalloc's implicit synchronisation). It keeps its
-scratch in a fixed array inside the library instead of a per-(handle, stream) cudaMalloc buffer.
+device memory (a server whose allocator owns all device memory; a loop that cannot take cudaMalloc's
+implicit synchronisation). It keeps its scratch in a fixed array inside the library instead of a
+per-(handle, stream) cudaMalloc buffer.
 
-Checked through the C ABI against the existing entry point, cublasGemmBatchedEx, on two calls in a row
-(different inputs and batch sizes, so the second call runs over the first call's leftovers in the shared
-array), with the tolerance of the other parity tests (oracle.check). This file is named to be collected
-last, so a run that stops at the first failure has run every other test before it; it also passes alone
-in a fresh process (its first call performs the library's per-device set-up).
+Checked through the C ABI on two calls in a row (different inputs and batch sizes, so the second call runs
+over the first call's leftovers in the shared array): against the fp64 oracle with the gate of the other
+parity tests (oracle.check), and against the existing entry point, cublasGemmBatchedEx, within the same
+tolerance. A call whose pointers the tensor cores cannot load (A 2 bytes off a 16-byte boundary, so the
+general kernel computes it) is followed by an aligned call, which must be back on the tensor cores. This
+file is named to be collected last, so a run that stops at the first failure has run every other test
+before it; it also passes alone in a fresh process (its first call performs the library's per-device
+set-up).
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -19,20 +24,27 @@ from tests.helpers import dev, ptr_table, storage
 pytestmark = pytest.mark.gpu
 
 
-def _problem(rng, m, n, k, batch, broadcast_a=1):
+def _sms():
+    import torch
+    return torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+
+
+def _problem(rng, m, n, k, batch, broadcast_a=1, a_shift=0):
+    """Seeded operands of a pointer-array batch; element b's A starts a_shift elements late when b is odd."""
     nA = (batch + broadcast_a - 1) // broadcast_a
-    A = storage(rng, nA * m * k, O.F16, 0.02)  # element b: op(A) = A_b^T, A_b stored k x m (lda = k)
+    A = storage(rng, nA * m * k + a_shift, O.F16, 0.02)  # element b: op(A) = A_b^T, A_b stored k x m (lda = k)
     B = storage(rng, batch * k * n, O.F16)  # element b: k x n (ldb = k)
     dA, dB = dev(A), dev(B)
-    a_ptrs = ptr_table([dA.data_ptr() + (b // broadcast_a) * m * k * 2 for b in range(batch)])
+    a_off = [(b // broadcast_a) * m * k + (a_shift if b % 2 else 0) for b in range(batch)]
+    a_ptrs = ptr_table([dA.data_ptr() + o * 2 for o in a_off])
     b_ptrs = ptr_table([dB.data_ptr() + b * k * n * 2 for b in range(batch)])
-    return A, B, dA, dB, a_ptrs, b_ptrs
+    A_list = [A[o:o + m * k] for o in a_off]
+    B_list = [B[b * k * n:(b + 1) * k * n] for b in range(batch)]
+    return (dA, dB, a_ptrs, b_ptrs), A_list, B_list
 
 
 def _run(lib, h, fn_name, m, n, k, batch, a_ptrs, b_ptrs):
     """One call through the C ABI into a NaN-poisoned output; returns the host copy of C."""
-    import ctypes
-
     import torch
     C = torch.full((batch * m * n,), float("nan"), device="cuda")
     c_ptrs = ptr_table([C.data_ptr() + b * m * n * 4 for b in range(batch)])
@@ -49,7 +61,26 @@ def _run(lib, h, fn_name, m, n, k, batch, a_ptrs, b_ptrs):
     return C.cpu().numpy()
 
 
-def test_noalloc_matches_gemm_batched_ex_on_two_calls(lib):
+def _check_against_oracle_and_entry_point(lib, h, m, n, k, batch, bufs, A_list, B_list):
+    _, _, a_ptrs, b_ptrs = bufs
+    allocs_before = lib.lib.tb200_scratch_allocs(h.h)
+    got = _run(lib, h, "tb200_gemm_batched_ex_noalloc", m, n, k, batch, a_ptrs, b_ptrs)
+    assert lib.lib.tb200_scratch_allocs(h.h) == allocs_before, "the no-alloc entry point allocated scratch"
+    fell_back = lib.lib.tb200_noalloc_last_fallback()
+    assert np.isfinite(got).all(), "some element of C was never written"
+    rows = np.unique(np.concatenate([np.arange(0, m, 7), [m - 1]])).astype(np.int32)
+    R, S = O.gemm(1, 0, m, n, k, 1.0, None, O.F16, k, None, O.F16, k, batch=batch, rows=rows, A_list=A_list,
+                  B_list=B_list)
+    got_s = O.extract(got, O.F32, m, n, m, sC=m * n, batch=batch, rows=rows)
+    res = O.check(got_s, R, S, O.F32)
+    assert res["ok"], ("against the oracle", res)
+    want = _run(lib, h, "cublasGemmBatchedEx", m, n, k, batch, a_ptrs, b_ptrs)
+    res = O.check(got_s, O.extract(want, O.F32, m, n, m, sC=m * n, batch=batch, rows=rows), S, O.F32)
+    assert res["ok"], ("against cublasGemmBatchedEx", res)
+    return fell_back
+
+
+def test_noalloc_matches_oracle_and_gemm_batched_ex_on_two_calls(lib):
     import torch
     assert torch.cuda.is_available()
     rng = np.random.default_rng(2024)
@@ -57,27 +88,26 @@ def test_noalloc_matches_gemm_batched_ex_on_two_calls(lib):
     # two calls in a row on the shared scratch: MoE-expert shape, then a GQA pointer batch with fewer
     # elements (the second call must not see the first one's leftover tensor maps)
     for (m, n, k, batch, bcast) in [(768, 32, 2048, 24, 1), (512, 256, 128, 6, 3)]:
-        assert lib.plan(1, 0, m, n, k, batch, 1, 0, 0, 1, 1, 148)[0] == cb.TB200_KERNEL_TC
-        A, B, dA, dB, a_ptrs, b_ptrs = _problem(rng, m, n, k, batch, bcast)
-        allocs_before = lib.lib.tb200_scratch_allocs(h.h)
-        got = _run(lib, h, "tb200_gemm_batched_ex_noalloc", m, n, k, batch, a_ptrs, b_ptrs)
-        assert lib.lib.tb200_scratch_allocs(h.h) == allocs_before, "the no-alloc entry point allocated scratch"
-        want = _run(lib, h, "cublasGemmBatchedEx", m, n, k, batch, a_ptrs, b_ptrs)
-        # the existing entry point's output as the reference, the oracle's scale for the normalisation
-        rows = np.arange(0, m, 7, dtype=np.int32)
-        A_list = [A[(b // bcast) * m * k:(b // bcast + 1) * m * k] for b in range(batch)]
-        B_list = [B[b * k * n:(b + 1) * k * n] for b in range(batch)]
-        _, S = O.gemm(1, 0, m, n, k, 1.0, None, O.F16, k, None, O.F16, k, batch=batch, rows=rows, A_list=A_list,
-                      B_list=B_list)
-        R = O.extract(want, O.F32, m, n, m, sC=m * n, batch=batch, rows=rows)
-        res = O.check(O.extract(got, O.F32, m, n, m, sC=m * n, batch=batch, rows=rows), R, S, O.F32)
-        assert res["ok"], res
-        assert np.isfinite(got).all(), "some element of C was never written"
+        assert lib.plan(1, 0, m, n, k, batch, 1, 0, 0, 1, 1, _sms())[0] == cb.TB200_KERNEL_TC
+        bufs, A_list, B_list = _problem(rng, m, n, k, batch, bcast)
+        assert _check_against_oracle_and_entry_point(lib, h, m, n, k, batch, bufs, A_list, B_list) == 0
+    h.close()
+
+
+def test_noalloc_misaligned_call_then_aligned_call(lib):
+    """The per-call flag in the shared array: a batch with A pointers 2 bytes off a 16-byte boundary is
+    computed by the general kernel, and the aligned call after it goes back to the tensor cores."""
+    rng = np.random.default_rng(77)
+    h = lib.handle()
+    m, n, k, batch = 256, 64, 512, 4
+    bufs, A_list, B_list = _problem(rng, m, n, k, batch, a_shift=1)
+    assert _check_against_oracle_and_entry_point(lib, h, m, n, k, batch, bufs, A_list, B_list) == 1
+    bufs, A_list, B_list = _problem(rng, m, n, k, batch)
+    assert _check_against_oracle_and_entry_point(lib, h, m, n, k, batch, bufs, A_list, B_list) == 0
     h.close()
 
 
 def test_noalloc_rejects_batches_beyond_its_scratch(lib):
-    import ctypes
     h = lib.handle()
     one = ctypes.c_float(1.0)
     big = lib.lib.tb200_noalloc_max_batch() + 1
