@@ -10,19 +10,27 @@ K 4096->1024, V 4096->1024, O 4096->4096, gate and up 4096->14336, down 14336->4
 4096->128256 (761.2 GFLOP). Synthetic seeded data of those shapes; weights are random, not a checkpoint.
 Inputs are larger than L2 (1.9 GB touched per step), so no flush is needed between steps.
 
-At N > 1 (torchrun, one process per GPU, NCCL): every projection is N-sharded along m (the weight's
-output features); each rank computes its m/N rows and its GEMM epilogue stores them into every rank's
-C over NVLink P2P (CUDA IPC mappings, macuda_b200.dist.FusedShardedGemm), with one 4-byte NCCL
-all-reduce per step as the completion barrier. --exchange multicast stores each element once to an
-NVLink multicast address instead (symmetric memory; slower for this all-gather, see macuda_b200/dist.py);
---exchange allgather uses an NCCL all-gather + layout kernel. Total work is fixed, so scaling is
-"strong".
+At N > 1 (torchrun, one process per GPU, NCCL) each projection is either N-sharded along m (the weight's
+output features: each rank computes its m/N rows) or run whole on every rank, and every rank ends the step
+holding every projection's full C. Default exchange (--exchange ce): a sharded projection's GEMM writes its
+rows into the rank's own C and the copy engines push them into every peer's C (CUDA IPC mappings,
+macuda_b200.dist.CopyEngineShardedGemm); the sharded projections run first, so their copies cross NVLink
+while the SMs run the projections that are whole on every rank; one 4-byte NCCL all-reduce per step is the
+completion barrier. Which projections are sharded is chosen at set-up by timing candidate plans as whole
+steps on every rank (max over ranks). --exchange fused stores the rows into the peers' C from the GEMM
+epilogue instead (P2P), --exchange multicast through an NVLink multicast address, --exchange allgather with
+an NCCL all-gather + layout kernel. Total work is fixed, so scaling is "strong". After the timed region every
+rank checks sampled rows of every projection's C - rows of every peer's shard included - against fp64 on the
+device ("parity", max over ranks), and `sharded_shapes` gives per-shape figures split across the N ranks
+(lm_head, FFN, squares N-sharded; config 3 attention by KV-head groups and config 5 MoE by experts), each
+with its one-GPU time, compute-only and end-to-end scaling and the link bound R.
 
-Keys beyond the base contract: roofline (dominant kernel = the lm_head GEMM), cpu_baseline (the
-oracle's multithreaded fp16 GEMM on the host, a stand-in for ggml-cpu), e2e (the same step through the
-public API with host buffers: H2D of the step's activations and D2H of the last token's logits), per
-projection figures, decode (n <= 8) HBM bandwidth figures (config 4), and configs 3 and 5 figures
-(attention batched GEMMs, MoE pointer-array GEMMs, squares).
+Keys beyond the base contract: roofline (dominant kernel = the lm_head GEMM, against the burst tensor peak:
+the timed region lasts milliseconds), cpu_baseline (the oracle's multithreaded fp16 GEMM on the host, a
+stand-in for ggml-cpu), e2e (the same step through the public API with host buffers: H2D of the step's
+activations and D2H of the last token's logits), parity, per projection figures, decode (n <= 8) HBM
+bandwidth figures (config 4), the HBM probes, and configs 3 and 5 figures (attention batched GEMMs, MoE
+pointer-array and grouped GEMMs, squares).
 
 --impl reference runs the same step through the reference's own libtinycublas (its cublas.c and gemm.cu,
 compiled from source for sm_100a by oracle/build_ref.sh): the reference's implementation of this path
@@ -145,8 +153,41 @@ def make_inputs(torch, rank, world, dtype, seed=1234):
         w_full = (torch.randn(m, k, device="cuda", generator=gw) * 0.02).to(dtype)  # row r = output feature r
         w = w_full if world == 1 else w_full[first:first + max(rows, 1)].clone()
         c = torch.empty(m * TOKENS, device="cuda", dtype=torch.float32) if world == 1 else None
-        layers.append({"name": name, "m": m, "mp": rows, "k": k, "src": src, "w": w, "w_full": w_full, "c_local": c})
+        check = parity_rows(m, max(world, 8), seed + len(layers))
+        layers.append({"name": name, "m": m, "mp": rows, "first": first, "k": k, "src": src, "w": w, "w_full": w_full,
+                       "c_local": c, "check_rows": torch.tensor(check, device="cuda"),
+                       "w_check": w_full[check].clone()})
     return acts, layers
+
+
+def parity_rows(m, world, seed):
+    """Rows of C the parity check reads: the first, middle and last row of every rank's shard (of `world`
+    shards, so every peer's rows are covered at any N up to it) and 24 seeded others."""
+    import numpy as np
+    from macuda_b200.dist import shard_rows
+    rows = set()
+    for r in range(world):
+        first, cnt, _ = shard_rows(m, world, r)
+        if cnt:
+            rows |= {first, first + cnt // 2, first + cnt - 1}
+    rows |= set(np.random.default_rng(seed).choice(m, 24, replace=False).tolist())
+    return sorted(rows)
+
+
+def check_rows(torch, C, m, n, rows, W_rows, X):
+    """The parity gate on sampled rows of a T,N GEMM's column-major f32 C (ldc = m), against fp64 on the device:
+    R = W_rows X^T; max |C - R| / (|W_i| |X_j|) <= 2^-10 (north star) and the reference's own metric
+    max |C - R| / max |R| <= 2e-3 (cuda-shim/libtinycublas/bf16-20260921/bench_gemm_contract.cu:8-10), non-finite
+    values refused first. The checker only: it never feeds the measured path."""
+    got = C[: m * n].view(n, m)[:, rows].t().double()
+    W, Xd = W_rows.double(), X.double()
+    R = W @ Xd.t()
+    S = W.norm(dim=1)[:, None] * Xd.norm(dim=1)[None, :]
+    finite = bool(torch.isfinite(got).all().item())
+    d = (got - R).abs()
+    norm = float((d / S.clamp_min(1e-300)).max().item()) if finite else float("inf")
+    refm = float((d.max() / R.abs().max().clamp_min(1e-300)).item()) if finite else float("inf")
+    return {"ok": finite and norm <= 2.0 ** -10 and refm <= 2e-3, "norm_err": norm, "ref_metric": refm}
 
 
 def gemm_call(h, cb, layer, act, ctype, out_ptr, ldc):
@@ -401,6 +442,314 @@ def config_figures(torch, lib, cb, dtype_code, dtype, only=None, reps_override=N
     return out
 
 
+# measured peer-to-peer copy bandwidth per direction between two B200s of this pool over NVLink 5 (GB/s): the
+# link figure of the scaling bound R
+PEER_GBS = 770.0
+
+
+def probe_figures(torch, lib):
+    """The HBM probes (tb200_bw_write / tb200_bw_read, the counterparts of the reference's bandwidth probes,
+    cuda-shim/libtinycublas/gemm.cu:421-431 driven by cuda-shim/test/bw_bench.c): 1 GiB streamed one way,
+    20 launches each, GB/s from CUDA events."""
+    import ctypes
+    n4 = (1 << 30) // 16
+    buf = torch.empty(n4 * 4, device="cuda")
+    sink = torch.zeros(1, device="cuda")
+    s = torch.cuda.current_stream()
+    out = {}
+    for name in ("write", "read"):
+        def call():
+            if name == "write":
+                return lib.lib.tb200_bw_write(buf.data_ptr(), n4, ctypes.c_float(1.0), ctypes.c_void_p(s.cuda_stream))
+            return lib.lib.tb200_bw_read(buf.data_ptr(), n4, sink.data_ptr(), ctypes.c_void_p(s.cuda_stream))
+        for _ in range(3):
+            call()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(20):
+            call()
+        e1.record(s)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / 20
+        out[name] = {"GB/s": round(n4 * 16 / us / 1e3, 1), "us": round(us, 1), "bytes": n4 * 16}
+    del buf
+    return out
+
+
+def sharded_figures(torch, lib, cb, h, stream, rank, world, copies):
+    """Per-shape figures at N > 1 (3 and 5): each case once on one GPU (the whole GEMM,
+    every rank timing it on its own GPU), then split across the N ranks:
+      * N-sharded along m (the weight's output features): lm_head, FFN gate/up and down, squares
+        4096/8192/16384 in f16 and bf16. Each rank computes its rows into its own full C (ldc = m) and the copy
+        engines push them into every peer's C (tb200_push_block), the columns in `chunks` GEMMs so the copies of
+        one chunk overlap the next chunk's math;
+      * batch-sharded (whole batch elements per rank): config 3 attention by KV-head groups (strided with the 4
+        query heads of each KV head folded into n; pointer arrays with each KV head's pointer repeated for its
+        query heads), config 5 MoE by experts (pointer arrays, and the grouped GEMM). Each rank's C slab is
+        contiguous and is pushed whole.
+    Times are device times on the compute stream (CUDA events, max over ranks): `n1_us` the whole GEMM on one
+    GPU, `compute_us` this rank's part alone, `e2e_us` its part plus the exchange until every rank holds all of
+    C (the copies joined and one NCCL barrier). compute_scaling = n1 / (N compute), e2e_scaling = n1 / (N e2e).
+    R = n1 * B / ((N - 1) * C bytes), B = PEER_GBS: the efficiency bound of a perfectly overlapped exchange (each
+    rank receives (N-1)/N of C over its link while computing 1/N of the work). parity: sampled rows of C as rank
+    0..N-1 hold it after the exchange (every rank's part included), against fp64 on the device, max over ranks."""
+    import torch.distributed as dist
+    from macuda_b200.dist import IpcReplicas, shard_rows, step_barrier
+    f32 = cb.CUDA_R_32F
+    out = {}
+
+    def timed(fn, reps):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+        return float(t.item())
+
+    def gen(shape, seed, scale, dt):
+        g = torch.Generator(device="cuda")
+        g.manual_seed(seed)  # the same on every rank: every rank holds the same operands
+        return (torch.randn(*shape, device="cuda", generator=g) * scale).to(dt)
+
+    def reduce_parity(r):
+        t = torch.tensor([r["norm_err"], r["ref_metric"], 0.0 if r["ok"] else 1.0], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return {"ok": float(t[2].item()) == 0.0, "norm_err": float("%.3e" % t[0].item()),
+                "ref_metric": float("%.3e" % t[1].item())}
+
+    def merge(a, b):
+        return {"ok": a["ok"] and b["ok"], "norm_err": max(a["norm_err"], b["norm_err"]),
+                "ref_metric": max(a["ref_metric"], b["ref_metric"])}
+
+    def record(name, flop, c_bytes, bound, t1, tc, te, par, extra=None):
+        rec = {"n1_us": round(t1 * 1e3, 1), "compute_us": round(tc * 1e3, 1), "e2e_us": round(te * 1e3, 1),
+               "compute_scaling": round(t1 / (world * tc), 3), "e2e_scaling": round(t1 / (world * te), 3),
+               "R": round(t1 * 1e-3 * PEER_GBS * 1e9 / ((world - 1) * c_bytes), 3), "bound": bound,
+               "TFLOP/s_e2e": round(flop / (te * 1e-3) / 1e12, 1), "TFLOP/s_n1": round(flop / (t1 * 1e-3) / 1e12, 1),
+               "C_bytes": int(c_bytes), "parity": reduce_parity(par)}
+        if extra:
+            rec.update(extra)
+        out[name] = rec
+
+    def reps_for(t_ms):
+        return int(max(3, min(40, 25.0 / max(t_ms, 1e-3))))
+
+    # ---- N-sharded along m: lm_head, FFN, squares ----
+    cases = [("lm_head", 128256, 512, 4096, "f16", (1,)), ("ffn_gate_up", 14336, 512, 4096, "f16", (1,)),
+             ("ffn_down", 4096, 512, 14336, "f16", (1,))]
+    for S in (4096, 8192, 16384):
+        for tn in ("f16", "bf16"):
+            cases.append((f"square_{S}_{tn}", S, S, S, tn, (1, 4, 8) if S > 4096 else (1, 4)))
+    for ci, (name, m, n, k, tn, chunk_opts) in enumerate(cases):
+        dt = torch.float16 if tn == "f16" else torch.bfloat16
+        code = cb.CUDA_R_16F if tn == "f16" else cb.CUDA_R_16BF
+        A = gen((m, k), 7000 + ci, 0.02, dt)   # stored k x m (op T, lda = k): row i = output feature i
+        B = gen((n, k), 7100 + ci, 1.0, dt)    # stored k x n (op N, ldb = k)
+        first, rows, _ = shard_rows(m, world, rank)
+        C1 = torch.empty(m * n, device="cuda")
+        buf = IpcReplicas(lib, m * n * 4, rank, world)
+        esz = 2
+
+        def whole():
+            return h.gemm_ex(1, 0, m, n, k, 1.0, A.data_ptr(), code, k, B.data_ptr(), code, k, 0.0, C1.data_ptr(), f32,
+                             m, cb.CUBLAS_COMPUTE_32F)
+
+        def part(col0=0, nc=n):
+            if rows == 0:
+                return 0
+            return h.gemm_ex(1, 0, rows, nc, k, 1.0, A.data_ptr() + first * k * esz, code, k,
+                             B.data_ptr() + col0 * k * esz, code, k, 0.0, buf.own + (first + col0 * m) * 4, f32, m,
+                             cb.CUBLAS_COMPUTE_32F)
+
+        def sharded(chunks):
+            step = -(-n // chunks)
+            for col0 in range(0, n, step):
+                nc = min(step, n - col0)
+                if part(col0, nc) != 0:
+                    raise RuntimeError(f"{name}: GEMM failed")
+                copies.after(stream)
+                if rows and lib.lib.tb200_push_block(buf.array, world, rank, first, rows, col0, nc, m, 4, copies.array,
+                                                     world) != 0:
+                    raise RuntimeError(f"{name}: push failed")
+            copies.join(stream)
+            step_barrier(stream)
+
+        t1 = timed(whole, reps_for(2.0 * m * n * k / 1.2e15 * 1e3))
+        reps = reps_for(t1)
+        tc = timed(part, reps)
+        best = None
+        for ch in chunk_opts:
+            te = timed(lambda: sharded(ch), reps)
+            if best is None or te < best[0]:
+                best = (te, ch)
+        sharded(best[1])
+        torch.cuda.synchronize()
+        dist.barrier()
+        rws = torch.tensor(parity_rows(m, world, 11 + ci), device="cuda")
+        Cfull = torch.as_tensor(_Dev(buf.own, m * n), device="cuda")
+        par = check_rows(torch, Cfull, m, n, rws, A[rws], B)
+        record(name, 2.0 * m * n * k, m * n * 4, "tensor", t1, tc, best[0], par,
+               {"m": m, "n": n, "k": k, "dtype": tn, "sharded": "m (weight rows)", "chunks": best[1]})
+        del Cfull
+        buf.close()
+        del A, B, C1
+        torch.cuda.empty_cache()
+
+    # ---- batch-sharded: config 3 attention (KV-head groups), config 5 MoE (experts) ----
+    dt, code = torch.float16, cb.CUDA_R_16F
+    Hq, Hkv, D, Tq, Tk = 32, 8, 128, 512, 4096
+    g = Hq // Hkv
+    K = gen((Hkv, Tk, D), 7201, 1.0, dt)
+    Q = gen((Hq, Tq, D), 7202, 1.0, dt)
+    V = gen((Hkv, D, Tk), 7203, 1.0, dt)
+    u = torch.rand(Hq, Tq, Tk, device="cuda", generator=torch.Generator(device="cuda").manual_seed(7204))
+    P_ = (u / u.sum(dim=2, keepdim=True)).to(dt)  # softmax-shaped weights
+    del u
+
+    def table(ptrs):
+        return torch.tensor(ptrs, dtype=torch.int64, device="cuda")
+
+    def batch_case(name, nbatch, slab, flop, c_bytes, bound, whole_fn, part_fn, check_fn, extra):
+        """whole_fn(C base): the whole batch; part_fn(C base, b0, nb): batch elements [b0, b0 + nb) into their
+        slabs of the full C; check_fn(C tensor, b) -> parity dict of element b."""
+        b0, nb, _ = shard_rows(nbatch, world, rank)
+        total = nbatch * slab
+        C1 = torch.empty(total, device="cuda")
+        buf = IpcReplicas(lib, total * 4, rank, world)
+
+        def sharded():
+            if nb and part_fn(buf.own, b0, nb) != 0:
+                raise RuntimeError(f"{name}: GEMM failed")
+            copies.after(stream)
+            if nb and lib.lib.tb200_push_block(buf.array, world, rank, b0 * slab, nb * slab, 0, 1, total, 4,
+                                               copies.array, world) != 0:
+                raise RuntimeError(f"{name}: push failed")
+            copies.join(stream)
+            step_barrier(stream)
+
+        t1 = timed(lambda: whole_fn(C1.data_ptr()), 10)
+        reps = reps_for(t1)
+        tc = timed(lambda: part_fn(buf.own, b0, nb) if nb else 0, reps)
+        te = timed(sharded, reps)
+        sharded()
+        torch.cuda.synchronize()
+        dist.barrier()
+        Cfull = torch.as_tensor(_Dev(buf.own, total), device="cuda")
+        par = {"ok": True, "norm_err": 0.0, "ref_metric": 0.0}
+        for r in range(world):  # the first and last element of every rank's share
+            rb0, rnb, _ = shard_rows(nbatch, world, r)
+            for b in {rb0, rb0 + rnb - 1} if rnb else ():
+                par = merge(par, check_fn(Cfull, b))
+        record(name, flop, c_bytes, bound, t1, tc, te, par, dict(extra, batch=nbatch, sharded="batch"))
+        del Cfull
+        buf.close()
+        del C1
+
+    def gemm_cols(C, b, m, n, slab, W_t, X_t, nrows=48):
+        """parity of element b (m x n, column-major at b * slab) on seeded rows: W_t (m x k rows), X_t (n x k)"""
+        rws = torch.tensor(sorted(set([0, m - 1] + torch.randperm(m, generator=torch.Generator().manual_seed(b))[
+            :nrows].tolist())), device="cuda")
+        return check_rows(torch, C[b * slab:(b + 1) * slab], m, n, rws, W_t[rws], X_t)
+
+    flop3 = 2.0 * Tk * Tq * D * Hq
+    # KQ, strided, the 4 query heads of a KV head folded into n: element = KV head (8)
+    batch_case("c3_kq_strided_folded", Hkv, Tk * g * Tq, flop3, Hq * Tk * Tq * 4, "hbm",
+               lambda C: h.gemm_strided_batched_ex(1, 0, Tk, g * Tq, D, 1.0, K.data_ptr(), code, D, Tk * D, Q.data_ptr(),
+                                                   code, D, g * Tq * D, 0.0, C, f32, Tk, Tk * g * Tq, Hkv),
+               lambda C, b0, nb: h.gemm_strided_batched_ex(
+                   1, 0, Tk, g * Tq, D, 1.0, K.data_ptr() + b0 * Tk * D * 2, code, D, Tk * D,
+                   Q.data_ptr() + b0 * g * Tq * D * 2, code, D, g * Tq * D, 0.0, C + b0 * Tk * g * Tq * 4, f32, Tk,
+                   Tk * g * Tq, nb),
+               lambda C, b: gemm_cols(C, b, Tk, g * Tq, Tk * g * Tq, K[b], Q[b * g:(b + 1) * g].reshape(g * Tq, D)),
+               {"m": Tk, "n": g * Tq, "k": D, "split": "KV heads"})
+    batch_case("c3_kqv_strided_folded", Hkv, D * g * Tq, flop3, Hq * D * Tq * 4, "hbm",
+               lambda C: h.gemm_strided_batched_ex(1, 0, D, g * Tq, Tk, 1.0, V.data_ptr(), code, Tk, D * Tk,
+                                                   P_.data_ptr(), code, Tk, g * Tq * Tk, 0.0, C, f32, D, D * g * Tq, Hkv),
+               lambda C, b0, nb: h.gemm_strided_batched_ex(
+                   1, 0, D, g * Tq, Tk, 1.0, V.data_ptr() + b0 * D * Tk * 2, code, Tk, D * Tk,
+                   P_.data_ptr() + b0 * g * Tq * Tk * 2, code, Tk, g * Tq * Tk, 0.0, C + b0 * D * g * Tq * 4, f32, D,
+                   D * g * Tq, nb),
+               lambda C, b: gemm_cols(C, b, D, g * Tq, D * g * Tq, V[b], P_[b * g:(b + 1) * g].reshape(g * Tq, Tk)),
+               {"m": D, "n": g * Tq, "k": Tk, "split": "KV heads"})
+    # pointer arrays, element = query head (32), whole KV-head groups per rank (world divides 8)
+    kq_a = table([K.data_ptr() + (q // g) * Tk * D * 2 for q in range(Hq)])
+    kq_b = table([Q.data_ptr() + q * Tq * D * 2 for q in range(Hq)])
+    kqv_a = table([V.data_ptr() + (q // g) * D * Tk * 2 for q in range(Hq)])
+    kqv_b = table([P_.data_ptr() + q * Tq * Tk * 2 for q in range(Hq)])
+
+    def ctab(C, slab, b0, nb):
+        return table([C + (b0 + i) * slab * 4 for i in range(nb)])
+
+    tabs = {}
+
+    def ptr_call(key, a, b, m, n, k, lda, slab, C, b0, nb):
+        if (key, C, b0) not in tabs:
+            tabs[(key, C, b0)] = ctab(C, slab, b0, nb)
+        return h.gemm_batched_ex(1, 0, m, n, k, 1.0, a.data_ptr() + b0 * 8, code, lda, b.data_ptr() + b0 * 8, code, lda,
+                                 0.0, tabs[(key, C, b0)].data_ptr(), f32, m, nb)
+
+    batch_case("c3_kq_pointer_gqa", Hq, Tk * Tq, flop3, Hq * Tk * Tq * 4, "hbm",
+               lambda C: ptr_call("kq", kq_a, kq_b, Tk, Tq, D, D, Tk * Tq, C, 0, Hq),
+               lambda C, b0, nb: ptr_call("kq", kq_a, kq_b, Tk, Tq, D, D, Tk * Tq, C, b0, nb),
+               lambda C, b: gemm_cols(C, b, Tk, Tq, Tk * Tq, K[b // g], Q[b]),
+               {"m": Tk, "n": Tq, "k": D, "split": "query heads, whole KV-head groups per rank"})
+    batch_case("c3_kqv_pointer_gqa", Hq, D * Tq, flop3, Hq * D * Tq * 4, "hbm",
+               lambda C: ptr_call("kqv", kqv_a, kqv_b, D, Tq, Tk, Tk, D * Tq, C, 0, Hq),
+               lambda C, b0, nb: ptr_call("kqv", kqv_a, kqv_b, D, Tq, Tk, Tk, D * Tq, C, b0, nb),
+               lambda C, b: gemm_cols(C, b, D, Tq, D * Tq, V[b // g], P_[b]),
+               {"m": D, "n": Tq, "k": Tk, "split": "query heads, whole KV-head groups per rank"})
+    del K, Q, V, P_, kq_a, kq_b, kqv_a, kqv_b
+    tabs.clear()
+
+    # config 5 MoE: 128 experts, hidden 2048, expert FFN 768, 32 tokens each (balanced top-8 routing)
+    E, Hd, Fe, Te = 128, 2048, 768, 32
+    Wgu = gen((E, Fe, Hd), 7301, 0.02, dt)
+    Wd = gen((E, Hd, Fe), 7302, 0.02, dt)
+    Xe = gen((E, Te, Hd), 7303, 1.0, dt)
+    He = gen((E, Te, Fe), 7304, 1.0, dt)
+    flop5 = 2.0 * Fe * Te * Hd * E
+    for nm, W, X, m, k in (("c5_moe_gate_up_pointer", Wgu, Xe, Fe, Hd), ("c5_moe_down_pointer", Wd, He, Hd, Fe)):
+        pa = table([W.data_ptr() + e * m * k * 2 for e in range(E)])
+        pb = table([X.data_ptr() + e * Te * k * 2 for e in range(E)])
+        batch_case(nm, E, m * Te, flop5, E * m * Te * 4, "hbm",
+                   lambda C, pa=pa, pb=pb, m=m, k=k, nm=nm: ptr_call(nm, pa, pb, m, Te, k, k, m * Te, C, 0, E),
+                   lambda C, b0, nb, pa=pa, pb=pb, m=m, k=k, nm=nm: ptr_call(nm, pa, pb, m, Te, k, k, m * Te, C, b0, nb),
+                   lambda C, b, W=W, X=X, m=m: gemm_cols(C, b, m, Te, m * Te, W[b], X[b]),
+                   {"m": m, "n": Te, "k": k, "split": "experts"})
+    offs_full = torch.arange(0, (E + 1) * Te, Te, dtype=torch.int32, device="cuda")
+    batch_case("c5_moe_gate_up_grouped_balanced", E, Fe * Te, flop5, E * Fe * Te * 4, "hbm",
+               lambda C: h.gemm_grouped_ex(1, 0, Fe, E * Te, Hd, E, offs_full.data_ptr(), 1.0, Wgu.data_ptr(), code, Hd,
+                                           Fe * Hd, Xe.data_ptr(), code, Hd, 0.0, C, f32, Fe),
+               lambda C, b0, nb: h.gemm_grouped_ex(1, 0, Fe, nb * Te, Hd, nb, offs_full.data_ptr(), 1.0,
+                                                   Wgu.data_ptr() + b0 * Fe * Hd * 2, code, Hd, Fe * Hd,
+                                                   Xe.data_ptr() + b0 * Te * Hd * 2, code, Hd, 0.0,
+                                                   C + b0 * Te * Fe * 4, f32, Fe),
+               lambda C, b: gemm_cols(C, b, Fe, Te, Fe * Te, Wgu[b], Xe[b]),
+               {"m": Fe, "n": Te, "k": Hd, "split": "experts (grouped GEMM, offsets on the device)"})
+    del Wgu, Wd, Xe, He
+    tabs.clear()
+    torch.cuda.empty_cache()
+    return out
+
+
+class _Dev:
+    """A raw device range seen by torch through __cuda_array_interface__ (no copy)."""
+
+    def __init__(self, ptr, count):
+        self.__cuda_array_interface__ = {"shape": (count,), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                         "strides": None, "stream": None}
+
+
+
 def run_case(args):
     """--case NAME: one config 3/5 figure alone (its inputs, 2 warm-up calls, 3 x --steps timed calls)."""
     import torch
@@ -466,6 +815,12 @@ def run_single(args):
     return 0
 
 
+# candidate sets of projections to N-shard under the copy-engine exchange (the others run whole on every
+# rank); each is timed as a whole step at set-up and the fastest kept
+CE_PLANS = [("lm_head",), ("lm_head", "gate", "up"), ("lm_head", "gate", "up", "down"),
+            ("lm_head", "gate", "up", "down", "q", "o"), ("lm_head", "gate", "up", "down", "q", "o", "k", "v"), ()]
+
+
 def run(args):
     import torch
     import torch.distributed as dist
@@ -477,7 +832,11 @@ def run(args):
     torch.cuda.set_device(local)
     if world > 1:
         from datetime import timedelta
-        os.environ["NCCL_DEBUG"] = "WARN"  # keep NCCL's version banner off stdout: one JSON line only
+        # NCCL's initialisation lines (communicator size, ranks, transports) go to stderr, so that the rank count
+        # can be read from the log; stdout carries only the JSON line
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     if args.impl == "reference":
         from oracle import oracle as O
@@ -499,64 +858,131 @@ def run(args):
     dtype = torch.float16 if args.dtype == "f16" else torch.bfloat16
     ctype = cb.CUDA_R_16F if args.dtype == "f16" else cb.CUDA_R_16BF
     acts, layers = make_inputs(torch, rank, world, dtype)
+    names = [L["name"] for L in layers]
     stream = torch.cuda.Stream()
-    comm = torch.cuda.Stream() if world > 1 else None
     h = lib.handle()
     h.set_stream(stream.cuda_stream)
-    sharded = []
-    fused = world > 1 and args.exchange != "allgather"
-    any_shard = True
+    exchange = args.exchange if world > 1 else "none"
+    if exchange in ("fused", "p2p"):
+        exchange = "p2p"
+    runners = [None] * len(layers)
+    order = list(range(len(layers)))
+    copies, comm = None, None
+    finish = lambda: None  # noqa: E731  completes the step's exchange on the compute stream
     if world > 1:
-        from macuda_b200.dist import FusedShardedGemm, ReplicatedGemm, ShardedGemm, pick_fastest, step_barrier
-        for L in layers:
-            if fused:
+        from macuda_b200.dist import (CopyEngineShardedGemm, CopyStreams, FusedShardedGemm, ReplicatedGemm,
+                                      ShardedGemm, pick_fastest, step_barrier)
+        if exchange == "ce":
+            copies = CopyStreams(world)
+            ce = [CopyEngineShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype, copies)
+                  for L in layers]
+            whole = [ReplicatedGemm(lib, h, L["m"], TOKENS, L["k"], L["w_full"], ctype) for L in layers]
+
+            def plan_step(sharded):
+                for i in [i for i in range(len(layers)) if names[i] in sharded] + \
+                         [i for i in range(len(layers)) if names[i] not in sharded]:
+                    g = ce[i] if names[i] in sharded else whole[i]
+                    if g.run(acts[layers[i]["src"]], stream) != 0:
+                        raise RuntimeError(f"{names[i]}: GEMM failed")
+                if sharded:
+                    copies.join(stream)
+                    step_barrier(stream)
+
+            if args.shard == "auto":
+                # every candidate plan timed as a whole step on every rank (max over ranks), the fastest kept: the
+                # same choice everywhere
+                times = torch.zeros(len(CE_PLANS), dtype=torch.float64, device="cuda")
+                for pi, plan in enumerate(CE_PLANS):
+                    for _ in range(3):
+                        plan_step(plan)
+                    torch.cuda.synchronize()
+                    dist.barrier()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    for _ in range(10):
+                        plan_step(plan)
+                    e1.record(stream)
+                    torch.cuda.synchronize()
+                    times[pi] = e0.elapsed_time(e1) / 10
+                    dist.barrier()
+                dist.all_reduce(times, op=dist.ReduceOp.MAX)
+                sharded_set = CE_PLANS[int(torch.argmin(times).item())]
+                plan_times = {"+".join(p) or "none": round(float(t), 4) for p, t in zip(CE_PLANS, times.tolist())}
+            else:
+                sharded_set = tuple(names) if args.shard == "sharded" else ()
+                plan_times = None
+            for i in range(len(layers)):
+                keep, drop = (ce[i], whole[i]) if names[i] in sharded_set else (whole[i], ce[i])
+                drop.close()
+                runners[i] = keep
+            order = [i for i in range(len(layers)) if names[i] in sharded_set] + \
+                    [i for i in range(len(layers)) if names[i] not in sharded_set]
+            if sharded_set:
+                def finish():
+                    copies.join(stream)
+                    step_barrier(stream)
+        elif exchange in ("p2p", "multicast"):
+            plan_times = None
+            for i, L in enumerate(layers):
                 # N-sharded (rows exchanged by the epilogue) or whole on every rank (nothing exchanged): the
                 # faster of the two, timed on every rank (max over ranks) during set-up
                 cands = {"sharded": FusedShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype,
-                                                     exchange={"fused": "p2p"}.get(args.exchange, args.exchange)),
+                                                     exchange=exchange),
                          "whole": ReplicatedGemm(lib, h, L["m"], TOKENS, L["k"], L["w_full"], ctype)}
                 choice = pick_fastest(cands, acts[L["src"]], stream) if args.shard == "auto" else args.shard
                 for key, c in cands.items():
                     if key != choice:
                         c.close()
-                sharded.append(cands[choice])
-            else:
-                sharded.append(ShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype))
-        any_shard = any(getattr(g, "exchange", "allgather") != "replicated" for g in sharded)
+                runners[i] = cands[choice]
+            sharded_set = tuple(n for n, g in zip(names, runners) if g.exchange != "replicated")
+            if sharded_set:
+                def finish():
+                    step_barrier(stream)  # every peer's stores into this rank's C have landed
+        else:  # NCCL all-gather + layout kernel, every projection sharded
+            plan_times = None
+            comm = torch.cuda.Stream()
+            runners = [ShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype) for L in layers]
+            sharded_set = tuple(names)
+
+            def finish():
+                stream.wait_stream(comm)
+    else:
+        sharded_set, plan_times = (), None
     for L in layers:
         L.pop("w_full", None)  # whole weights stay only where a projection runs whole on every rank
+
+    def launch(i, act):
+        L = layers[i]
+        if world == 1:
+            return gemm_call(h, cb, L, act, ctype, L["c_local"].data_ptr(), L["m"])
+        if exchange == "allgather":  # this rank's rows, then the all-gather + layout on the comm stream
+            return runners[i].run(act, stream, comm)
+        return runners[i].run(act, stream)
+
+    def step(src, marks=None):
+        """One step: every projection once, in `order` (the N-sharded ones first, so that their exchange
+        overlaps the rest), then the exchange's completion. marks: {i: (event, event)} recorded around GEMM i."""
+        for i in order:
+            if marks is not None and i in marks:
+                marks[i][0].record(stream)
+            st = launch(i, src[layers[i]["src"]])
+            if marks is not None and i in marks:
+                marks[i][1].record(stream)
+            if st != 0:
+                raise RuntimeError(f"{names[i]}: status {st}")
+        finish()
+
     # Inside the timed region the only events are the two around the dominant GEMM (lm_head, the roofline
     # kernel): an event between two kernels would also stop the next one from being scheduled while the
     # previous one finishes (programmatic dependent launch). The per-projection breakdown comes from a
-    # separate pass after the timed region, with an event before every GEMM.
-    dom = layers.index(next(L for L in layers if L["name"] == "lm_head"))
-    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(len(layers) + 1)] for _ in range(args.steps)]
-    per_gemm_ms = [0.0] * len(layers)
-    launches_per_step = len(layers) * (2 if world > 1 and not fused else 1)
+    # separate pass after the timed region, with events around every GEMM.
+    dom = names.index("lm_head")
+    ev = lambda: torch.cuda.Event(enable_timing=True)  # noqa: E731
+    marks = [{dom: (ev(), ev())} for _ in range(args.steps)]
+    launches_per_step = len(layers) * (2 if exchange == "allgather" else 1)
 
-    def step(ev=None, only=None):
-        for i, L in enumerate(layers):
-            act = acts[L["src"]]
-            if ev is not None and (only is None or i == only):
-                ev[i].record(stream)
-            if world == 1:
-                st = gemm_call(h, cb, L, act, ctype, L["c_local"].data_ptr(), L["m"])
-            elif fused:  # this rank's rows, stored by the epilogue into every rank's C
-                st = sharded[i].run(act, stream)
-            else:  # this rank's rows, then the all-gather + layout on the comm stream (overlaps the next GEMM)
-                st = sharded[i].run(act, stream, comm)
-            if ev is not None and (i == len(layers) - 1 if only is None else i == only):
-                ev[i + 1].record(stream)
-            if st != 0:
-                raise RuntimeError(f"{L['name']}: status {st}")
-        if fused and any_shard:
-            step_barrier(stream)  # every peer's stores into this rank's C have landed
-        elif world > 1 and not fused:
-            stream.wait_stream(comm)
-
-    # warm-up
     for _ in range(args.warmup):
-        step()
+        step(acts)
     torch.cuda.synchronize()
     clocks = ClockSampler(local) if not args.no_clocks else None
     if clocks:
@@ -565,12 +991,12 @@ def run(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0, e1 = ev(), ev()
     if clocks:
         clocks.mark(True)
     e0.record(stream)
     for j in range(args.steps):
-        step(marks[j], only=dom)
+        step(acts, marks[j])
     e1.record(stream)
     torch.cuda.synchronize()
     if clocks:
@@ -583,26 +1009,31 @@ def run(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     clock_info = clocks.stop() if clocks else None
+    dom_ms = sum(marks[j][dom][0].elapsed_time(marks[j][dom][1]) for j in range(args.steps)) / args.steps
 
-    dom_ms = sum(marks[j][dom].elapsed_time(marks[j][dom + 1]) for j in range(args.steps)) / args.steps
-    # the per-projection breakdown, after the timed region: an event before every GEMM
+    # the per-projection breakdown, after the timed region: events around every GEMM
     n_bd = min(args.steps, 20)
+    per_gemm_ms = [0.0] * len(layers)
+    bd = [{i: (ev(), ev()) for i in range(len(layers))} for _ in range(n_bd)]
     for j in range(n_bd):
-        step(marks[j])
+        step(acts, bd[j])
     torch.cuda.synchronize()
     for j in range(n_bd):
         for i in range(len(layers)):
-            per_gemm_ms[i] += marks[j][i].elapsed_time(marks[j][i + 1]) / n_bd
+            per_gemm_ms[i] += bd[j][i][0].elapsed_time(bd[j][i][1]) / n_bd
     value = STEP_FLOP / (ms * 1e-3) / 1e12
-    gemm_only_ms = sum(per_gemm_ms)  # this rank's GEMMs alone (the all-gathers overlap on the comm stream)
+    gemm_only_ms = sum(per_gemm_ms)  # this rank's GEMMs alone (the exchange's copies run on other streams)
     if world > 1:
         t = torch.tensor([gemm_only_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         gemm_only_ms = float(t.item())
 
+    def m_run(i):  # rows the GEMM of projection i computes on this rank
+        return layers[i]["mp"] if names[i] in sharded_set else layers[i]["m"]
+
     pk = peaks()
     L = layers[dom]
-    dom_flop = 2.0 * L["mp"] * TOKENS * L["k"]
+    dom_flop = 2.0 * m_run(dom) * TOKENS * L["k"]
     dom_tflops = dom_flop / (dom_ms * 1e-3) / 1e12
     traffic = None
     prof = os.path.join(ROOT, "profiles", "roofline_traffic.json")
@@ -612,56 +1043,48 @@ def run(args):
                 traffic = json.load(f).get("lm_head_dram_bytes")
         except Exception:
             traffic = None
-    roofline = {"bound": "tensor", "achieved": round(dom_tflops, 2), "peak": pk["bf16_tflops_sustained"],
-                "unit": "TFLOP/s", "frac": round(dom_tflops / pk["bf16_tflops_sustained"], 4), "traffic": traffic,
-                "kernel": "lm_head GEMM (%d x %d x %d)" % (L["mp"], TOKENS, L["k"]),
-                "peak_source": pk["source"] + " bf16 sustained (cuBLAS 8192^3, MEASURED_PEAKS.json)",
-                "frac_of_burst": round(dom_tflops / pk["bf16_tflops"], 4),
-                "algorithmic_bytes": L["mp"] * L["k"] * 2 + TOKENS * L["k"] * 2 + L["mp"] * TOKENS * 4}
+    # the timed region lasts milliseconds (args.steps steps of well under 1 ms): the burst peak is the denominator
+    roofline = {"bound": "tensor", "achieved": round(dom_tflops, 2), "peak": pk["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": round(dom_tflops / pk["bf16_tflops"], 4), "traffic": traffic,
+                "kernel": "lm_head GEMM (%d x %d x %d)" % (m_run(dom), TOKENS, L["k"]),
+                "peak_source": pk["source"] + " bf16 burst (cuBLAS 8192^3, MEASURED_PEAKS.json): the timed region is "
+                               "%.1f ms long, far from the seconds-long loop of the sustained figure" % (ms * args.steps),
+                "frac_of_sustained": round(dom_tflops / pk["bf16_tflops_sustained"], 4),
+                "algorithmic_bytes": m_run(dom) * L["k"] * 2 + TOKENS * L["k"] * 2 + m_run(dom) * TOKENS * 4}
 
-    shapes = {Lx["name"]: {"m": Lx["mp"], "n": TOKENS, "k": Lx["k"], "us": round(per_gemm_ms[i] * 1e3, 2),
-                           "TFLOP/s": round(2.0 * Lx["mp"] * TOKENS * Lx["k"] / (per_gemm_ms[i] * 1e-3) / 1e12, 1)}
-              for i, Lx in enumerate(layers)}
+    shapes = {names[i]: {"m": m_run(i), "n": TOKENS, "k": layers[i]["k"],
+                         "ran": ("N-sharded" if names[i] in sharded_set else "whole on every rank") if world > 1
+                         else "single GPU",
+                         "us": round(per_gemm_ms[i] * 1e3, 2),
+                         "TFLOP/s": round(2.0 * m_run(i) * TOKENS * layers[i]["k"] / (per_gemm_ms[i] * 1e-3) / 1e12, 1)}
+              for i in range(len(layers))}
 
     # e2e through the public API with host buffers: each step copies its activations from pinned host
     # memory (double-buffered on a copy stream, overlapping the previous step) and reads back the last
     # token's logits
-    e2e = None
-    hx = [acts["x"].cpu().pin_memory(), acts["h"].cpu().pin_memory()]
-    dev_bufs = [[torch.empty_like(acts["x"]), torch.empty_like(acts["h"])] for _ in range(2)]
+    hx = {"x": acts["x"].cpu().pin_memory(), "h": acts["h"].cpu().pin_memory()}
+    dev_bufs = [{"x": torch.empty_like(acts["x"]), "h": torch.empty_like(acts["h"])} for _ in range(2)]
     logits = torch.empty(VOCAB, dtype=torch.float32).pin_memory()
-    copy = torch.cuda.Stream()
+    h2d = torch.cuda.Stream()
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
-    lm = layers[dom]
     n_e2e = max(3, min(args.steps, 100))
+
+    def c_of(i):
+        return layers[i]["c_local"] if world == 1 else runners[i].c
 
     def e2e_step(i):
         b = i % 2
-        with torch.cuda.stream(copy):
-            copy.wait_event(free[b])
-            dev_bufs[b][0].copy_(hx[0], non_blocking=True)
-            dev_bufs[b][1].copy_(hx[1], non_blocking=True)
-            ready[b].record(copy)
+        with torch.cuda.stream(h2d):
+            h2d.wait_event(free[b])
+            dev_bufs[b]["x"].copy_(hx["x"], non_blocking=True)
+            dev_bufs[b]["h"].copy_(hx["h"], non_blocking=True)
+            ready[b].record(h2d)
         stream.wait_event(ready[b])
-        for j, L2 in enumerate(layers):
-            act = dev_bufs[b][0] if L2["src"] == "x" else dev_bufs[b][1]
-            if world == 1:
-                st = gemm_call(h, cb, L2, act, ctype, L2["c_local"].data_ptr(), L2["m"])
-            elif fused:
-                st = sharded[j].run(act, stream)
-            else:
-                st = sharded[j].run(act, stream, comm)
-            if st != 0:
-                raise RuntimeError("e2e gemm failed")
-        if fused and any_shard:
-            step_barrier(stream)
-        elif world > 1 and not fused:
-            stream.wait_stream(comm)
+        step(dev_bufs[b])
         free[b].record(stream)
-        c_lm = lm["c_local"] if world == 1 else sharded[dom].c
         with torch.cuda.stream(stream):
-            logits.copy_(c_lm[(TOKENS - 1) * lm["m"]:TOKENS * lm["m"]], non_blocking=True)
+            logits.copy_(c_of(dom)[(TOKENS - 1) * VOCAB:TOKENS * VOCAB], non_blocking=True)
 
     for i in range(3):
         e2e_step(i)
@@ -669,7 +1092,7 @@ def run(args):
     if world > 1:
         dist.barrier()
         torch.cuda.synchronize()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0, f1 = ev(), ev()
     f0.record(stream)
     t_wall = time.perf_counter()
     for i in range(n_e2e):
@@ -683,8 +1106,33 @@ def run(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e = {"value": round(STEP_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-           "h2d_bytes_per_step": int(hx[0].numel() * 2 + hx[1].numel() * 2), "d2h_bytes_per_step": VOCAB * 4,
+           "h2d_bytes_per_step": int(hx["x"].numel() * 2 + hx["h"].numel() * 2), "d2h_bytes_per_step": VOCAB * 4,
            "ms_per_step": round(e2e_ms, 4), "wall_ms_per_step": round(t_wall * 1e3 / n_e2e, 4), "steps": n_e2e}
+
+    # parity of every projection's C as every rank holds it after the last step (each peer's rows included),
+    # against fp64 on sampled rows
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    par = {"ok": True, "norm_err": 0.0, "ref_metric": 0.0, "rows_per_projection": 0}
+    for i in range(len(layers)):
+        Li = layers[i]
+        r = check_rows(torch, c_of(i), Li["m"], TOKENS, Li["check_rows"], Li["w_check"], acts[Li["src"]])
+        par["ok"] = par["ok"] and r["ok"]
+        par["norm_err"] = max(par["norm_err"], r["norm_err"])
+        par["ref_metric"] = max(par["ref_metric"], r["ref_metric"])
+        par["rows_per_projection"] = max(par["rows_per_projection"], int(Li["check_rows"].numel()))
+    if world > 1:
+        t = torch.tensor([par["norm_err"], par["ref_metric"], 0.0 if par["ok"] else 1.0], device="cuda",
+                         dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        par.update(norm_err=float(t[0].item()), ref_metric=float(t[1].item()), ok=float(t[2].item()) == 0.0)
+    par.update(ranks_checked=world, tol=2.0 ** -10, columns="all %d" % TOKENS,
+               how="every rank: the first, middle and last row of each of 8 row shards (every peer's rows at any "
+                   "N <= 8) plus 24 seeded rows of each projection's C, against fp64 W_rows X^T on the device; "
+                   "max over ranks")
+    par["norm_err"] = float("%.3e" % par["norm_err"])
+    par["ref_metric"] = float("%.3e" % par["ref_metric"])
 
     cpu = None
     if rank == 0 and world == 1 and args.impl == "ours" and not args.no_cpu_baseline:
@@ -696,43 +1144,60 @@ def run(args):
     decode = None
     if rank == 0 and world == 1 and not args.no_decode:
         decode = decode_figures(torch, lib, cb, ctype, dtype)
+    probes = None
+    if rank == 0 and world == 1 and args.impl == "ours":
+        probes = probe_figures(torch, lib)
     configs = None
     if rank == 0 and world == 1 and not args.no_configs:
         configs = config_figures(torch, lib, cb, ctype, dtype)
+    sharded = None
+    if world > 1 and args.impl == "ours" and not args.no_sharded_shapes:
+        sharded = sharded_figures(torch, lib, cb, h, stream, rank, world, copies or CopyStreams(world))
 
-    if fused:
-        for g in sharded:
+    for g in runners:
+        if g is not None and hasattr(g, "close"):
             g.close()
     h.close()
     if rank == 0:
+        if world == 1:
+            par_note = "single GPU"
+        elif exchange == "ce":
+            par_note = f"x{world}: " + ", ".join(
+                f"{n} " + ("N-sharded, rows pushed to every peer by the copy engines" if n in sharded_set
+                           else "whole on every rank") for n in (names[i] for i in order)) + \
+                ("; sharded projections run first so their copies overlap the rest; one NCCL barrier per step"
+                 if sharded_set else "")
+        elif exchange in ("p2p", "multicast"):
+            par_note = f"x{world}: " + ", ".join(
+                f"{n} " + (("N-sharded, rows exchanged by " + ("NVLink multicast" if exchange == "multicast" else "P2P")
+                            + " stores from the GEMM epilogue") if n in sharded_set else "whole on every rank")
+                for n in names) + ("; one NCCL barrier per step" if sharded_set else "")
+        else:
+            par_note = f"N-shard x{world}, C exchanged by NCCL all-gather + layout kernel"
         line = {
-            "metric": "GEMM TFLOP/s (Llama-3.1-8B prefill projection set, 512 tokens, fp16 -> f32, ggml's T,N call)",
+            "metric": "GEMM TFLOP/s (Llama-3.1-8B prefill projection set, 512 tokens, %s -> f32, ggml's T,N call)"
+                      % args.dtype,
             "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": args.dtype, "data": "synthetic (seeded N(0,0.02^2) weights, N(0,1) activations; no checkpoint)",
             "config": {"workload": "llama3.1-8b prefill projections q,k,v,o,gate,up,down,lm_head @ 512 tokens "
                                    "(BASELINE configs[1])", "tokens": TOKENS, "step_gflop": round(STEP_FLOP / 1e9, 1),
-                       "parallelism": ((f"x{world}: " + ", ".join(
-                                           f"{L['name']} " + ("whole on every rank" if g.exchange == "replicated"
-                                                              else "N-sharded, rows exchanged by " +
-                                                              ("NVLink multicast" if g.exchange == "multicast" else
-                                                               "P2P") + " stores from the GEMM epilogue")
-                                           for L, g in zip(layers, sharded)) +
-                                        ("; one NCCL barrier per step" if any_shard else "")) if fused else
-                                       f"N-shard x{world}, C exchanged by NCCL all-gather + layout kernel")
-                                      if world > 1 else "single GPU",
+                       "parallelism": par_note, "exchange": exchange if world > 1 else None,
                        "l2": "inputs larger than L2 (1.9 GB per step); no flush"},
-            "frac_of_peak": round(value / pk["bf16_tflops_sustained"], 4),
+            "frac_of_peak": round(value / pk["bf16_tflops"], 4),
+            "parity": par,
             "roofline": roofline, "shapes": shapes,
-            "shapes_note": "per-projection device time from %d further steps after the timed region, an event before "
+            "shapes_note": "per-projection device time from %d further steps after the timed region, events around "
                            "every GEMM (events between kernels stop the next one being scheduled early, so these "
-                           "sum to more than ms_per_step)" % n_bd,
+                           "sum to more than ms_per_step); m is the rows the GEMM computed on each rank" % n_bd,
             "gpu_launches": launches_per_step * args.steps,
             "gemm_only": {"ms_per_step": round(gemm_only_ms, 4),
                           "TFLOP/s": round(STEP_FLOP / (gemm_only_ms * 1e-3) / 1e12, 2),
-                          "note": "sum of the per-projection times (max over ranks); at N > 1 the all-gathers run "
-                                  "on a second stream and the step time includes them"},
+                          "note": "sum of the per-projection GEMM times (max over ranks); at N > 1 the exchange runs "
+                                  "on other streams or engines and the step time includes it"},
         }
+        if plan_times:
+            line["plan_search_ms"] = plan_times
         if args.impl == "reference":
             line["impl"] = "reference"
             line["n_gpus"] = launched
@@ -750,8 +1215,12 @@ def run(args):
             line["clocks"] = clock_info
         if decode:
             line["decode"] = decode
+        if probes:
+            line["hbm_probes"] = probes
         if configs:
             line["configs_3_5"] = configs
+        if sharded:
+            line["sharded_shapes"] = sharded
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
@@ -776,10 +1245,13 @@ def main():
     ap.add_argument("--case", default=None, help="run one config 3/5 figure alone, by its name in configs_3_5 "
                                                  "(profiling); --steps sets its back-to-back calls")
     ap.add_argument("--shard", choices=["auto", "sharded", "whole"], default="auto",
-                    help="N > 1, fused exchange: per projection N-sharded or whole on every rank (auto: the faster, "
-                         "timed on every rank at set-up)")
-    ap.add_argument("--exchange", choices=["fused", "multicast", "p2p", "allgather"], default="fused",
-                    help="N > 1: how the sharded C is replicated (fused = p2p stores from the epilogue)")
+                    help="N > 1: which projections are N-sharded (the rest run whole on every rank); auto: the fastest "
+                         "plan, timed on every rank at set-up")
+    ap.add_argument("--exchange", choices=["ce", "fused", "multicast", "p2p", "allgather"], default="ce",
+                    help="N > 1: how the sharded C is replicated (ce = copy engines pushing each rank's rows to its "
+                         "peers; fused = p2p = stores from the GEMM epilogue)")
+    ap.add_argument("--no-sharded-shapes", action="store_true",
+                    help="N > 1: skip the per-shape sharded figures (squares, lm_head, FFN, configs 3 and 5)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -167,6 +167,30 @@ extern "C" int tb200_launch_moe_combine(const float *Cp, int m, long long ldc, i
   return (int)cudaGetLastError();
 }
 
+// ---- the sharded GEMM's exchange on the copy engines: this rank's block of C into every peer's replica ----
+extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_push_block(
+    void *const *replicas, int P, int self, long long row0, long long rows, long long col0, long long ncols,
+    long long ldc, int elem_bytes, const cudaStream_t *streams, int nstreams) {
+  if (!replicas || P < 1 || self < 0 || self >= P || row0 < 0 || rows < 0 || col0 < 0 || ncols < 0 ||
+      ldc < row0 + rows || ldc < 1 || (elem_bytes != 2 && elem_bytes != 4) || !streams || nstreams < 1)
+    return CUBLAS_STATUS_INVALID_VALUE;
+  if (rows == 0 || ncols == 0 || P == 1) return CUBLAS_STATUS_SUCCESS;
+  const size_t pitch = (size_t)ldc * elem_bytes;
+  const size_t off = (size_t)(row0 + col0 * ldc) * elem_bytes;
+  const char *src = (const char *)replicas[self] + off;
+  for (int q = 0; q < P; ++q) {
+    if (q == self) continue;
+    if (!replicas[q]) return CUBLAS_STATUS_INVALID_VALUE;
+    cudaError_t e = cudaMemcpy2DAsync((char *)replicas[q] + off, pitch, src, pitch, (size_t)rows * elem_bytes,
+                                      (size_t)ncols, cudaMemcpyDefault, streams[q % nstreams]);
+    if (e != cudaSuccess) {
+      fprintf(stderr, "[tinycublas_b200] tb200_push_block to rank %d: %s\n", q, cudaGetErrorString(e));
+      return CUBLAS_STATUS_EXECUTION_FAILED;
+    }
+  }
+  return CUBLAS_STATUS_SUCCESS;
+}
+
 extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_bw_write(void *p, long long n4, float v, cudaStream_t stream) {
   if (n4 <= 0) return CUBLAS_STATUS_SUCCESS;
   tb200_bw_write_kernel<<<grid_for(n4, 256), 256, 0, stream>>>((float4 *)p, n4, v);

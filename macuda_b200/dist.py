@@ -15,6 +15,14 @@ Two ways to replicate C:
     (P-1)/P of it, and inbound is the bound of an all-gather, so P2P is the default (measured at P = 2:
     0.586 vs 0.778 ms per step). Either way one 4-byte NCCL all-reduce per step tells each rank that its
     peers' stores have landed.
+  CopyEngineShardedGemm: the GEMM writes this rank's rows straight into its own full C (ldc = m), and the
+    copy engines push that row block into every peer's C (tb200_push_block: one cudaMemcpy2DAsync per peer,
+    each on its own stream). No SM time goes to the exchange, so it overlaps whatever the SMs run next -
+    in the benchmark's step, the projections that run whole on every rank. `wait` joins the copies into the
+    caller's stream; then the same 4-byte NCCL all-reduce tells each rank that its peers' copies have landed.
+    BatchShardedGemm does the same for a strided batch split across ranks (whole batch elements per rank:
+    KV-head groups of an attention GEMM, experts of an MoE layer): each rank's C slab is contiguous and is
+    pushed whole.
   ShardedGemm: the GEMM writes a local mp x n block, an NCCL all-gather on a communication stream
     concatenates the P blocks, and tb200_gather_row_blocks lays them out as the column-major C.
 
@@ -101,6 +109,176 @@ class _DeviceArray:
     def __init__(self, ptr: int, count: int, typestr: str = "<f4"):
         self.__cuda_array_interface__ = {"shape": (count,), "typestr": typestr, "data": (ptr, False), "version": 3,
                                          "strides": None, "stream": None}
+
+
+class IpcReplicas:
+    """A device buffer of `nbytes` on every rank, each mapped into every other rank of the group (CUDA IPC):
+    `reps[q]` is rank q's buffer as a pointer valid in this process (`own` = reps[rank]). Collective: every
+    rank constructs it with the same size, and closes it."""
+
+    def __init__(self, lib, nbytes: int, rank: int, world: int, group=None):
+        import ctypes
+
+        import torch.distributed as dist
+        self.lib, self.rank, self.world, self.group = lib, rank, world, group
+        own = ctypes.c_void_p()
+        hbuf = ctypes.create_string_buffer(64)
+        st = lib.lib.tb200_ipc_alloc(nbytes, ctypes.byref(own), hbuf)
+        if st != 0:
+            raise RuntimeError(f"tb200_ipc_alloc: status {st}")
+        self.own = own.value
+        handles = [None] * world
+        dist.all_gather_object(handles, hbuf.raw, group=group)
+        self.reps, self.opened = [], []
+        for r in range(world):
+            if r == rank:
+                self.reps.append(self.own)
+                continue
+            p = ctypes.c_void_p()
+            st = lib.lib.tb200_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(p))
+            if st != 0:
+                raise RuntimeError(f"tb200_ipc_open (rank {r}): status {st}")
+            self.reps.append(p.value)
+            self.opened.append(p.value)
+        self.array = (ctypes.c_void_p * world)(*self.reps)
+
+    def close(self):
+        import torch
+        import torch.distributed as dist
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            self.lib.lib.tb200_ipc_close(p)
+        self.opened = []
+        dist.barrier(group=self.group)  # every peer has unmapped this rank's buffer before it is freed
+        if self.own:
+            self.lib.lib.tb200_ipc_free(self.own)
+            self.own = 0
+
+
+class CopyStreams:
+    """One stream per rank of the group for the copy-engine exchange (peer q's copies go on stream q), and an
+    event per stream that `join` records and makes another stream wait on."""
+
+    def __init__(self, world: int):
+        import ctypes
+
+        import torch
+        self.streams = [torch.cuda.Stream() for _ in range(world)]
+        self.array = (ctypes.c_void_p * world)(*[s.cuda_stream for s in self.streams])
+        self.events = [torch.cuda.Event() for _ in range(world)]
+        self.ready = torch.cuda.Event()
+
+    def after(self, stream):
+        """Order the copies enqueued next after everything enqueued on `stream` so far."""
+        self.ready.record(stream)
+        for s in self.streams:
+            s.wait_event(self.ready)
+
+    def join(self, stream):
+        """Make `stream` wait for every copy enqueued so far."""
+        for s, e in zip(self.streams, self.events):
+            e.record(s)
+            stream.wait_event(e)
+
+
+class CopyEngineShardedGemm:
+    """N-sharded GEMM with the exchange on the copy engines.
+
+    Rank r's GEMM writes its rows [first, first + rows) of C straight into its own full C (leading dimension
+    m) and tb200_push_block copies that row block into every peer's C. `run` splits the columns into `chunks`
+    GEMMs so that the copies of one chunk overlap the next chunk's math (1 = one GEMM, then the copies). The
+    copies go on `copies` (a CopyStreams shared by the step); `copies.join(stream)` and `step_barrier` then
+    complete the exchange."""
+
+    exchange = "ce"
+
+    def __init__(self, lib, handle, m: int, n: int, k: int, rank: int, world: int, w_local, dtype_code: int,
+                 copies: "CopyStreams", group=None, chunks: int = 1):
+        import torch
+        self.lib, self.h = lib, handle
+        self.m, self.n, self.k = m, n, k
+        self.rank, self.world, self.group = rank, world, group
+        self.first, self.rows, self.mp = shard_rows(m, world, rank)
+        self.w = w_local
+        self.dtype_code = dtype_code
+        self.copies = copies
+        self.chunks = max(1, chunks)
+        self.esize = torch.empty((), dtype=torch.float16).element_size()
+        self.buf = IpcReplicas(lib, m * n * 4, rank, world, group)
+        self.c = torch.as_tensor(_DeviceArray(self.buf.own, m * n), device="cuda")
+
+    def run(self, x, stream=None, chunks: int = None) -> int:
+        from . import cublas as cb
+        chunks = self.chunks if chunks is None else max(1, chunks)
+        if self.rows == 0:
+            return 0
+        step = -(-self.n // chunks)
+        for col0 in range(0, self.n, step):
+            nc = min(step, self.n - col0)
+            st = self.h.gemm_ex(cb.CUBLAS_OP_T, cb.CUBLAS_OP_N, self.rows, nc, self.k, 1.0, self.w.data_ptr(),
+                                self.dtype_code, self.k, x.data_ptr() + col0 * self.k * self.esize, self.dtype_code,
+                                self.k, 0.0, self.buf.own + (self.first + col0 * self.m) * 4, cb.CUDA_R_32F, self.m,
+                                cb.CUBLAS_COMPUTE_32F)
+            if st != 0:
+                return st
+            self.copies.after(stream)
+            st = self.lib.lib.tb200_push_block(self.buf.array, self.world, self.rank, self.first, self.rows, col0, nc,
+                                               self.m, 4, self.copies.array, self.world)
+            if st != 0:
+                return st
+        return 0
+
+    def close(self):
+        self.c = None
+        self.buf.close()
+
+
+class BatchShardedGemm:
+    """A strided-batched GEMM (T, N, f32 C) split across ranks by whole batch elements: rank r computes
+    elements [b0, b0 + nb) (bshard of them per rank, the last rank possibly fewer) into its slab of its own
+    full C and the copy engines push the slab into every peer's C. The slabs are contiguous because C's batch
+    stride is m * n: they all-gather straight into C. A, B: this rank's elements only (strides sA, sB)."""
+
+    exchange = "ce"
+
+    def __init__(self, lib, handle, m: int, n: int, k: int, batch: int, rank: int, world: int, A_local, sA: int,
+                 B_local, sB: int, dtype_code: int, copies: "CopyStreams", group=None):
+        import torch
+        self.lib, self.h = lib, handle
+        self.m, self.n, self.k, self.batch = m, n, k, batch
+        self.rank, self.world = rank, world
+        self.b0, self.nb, self.bshard = shard_rows(batch, world, rank)
+        self.A, self.sA, self.B, self.sB = A_local, sA, B_local, sB
+        self.dtype_code = dtype_code
+        self.copies = copies
+        self.buf = IpcReplicas(lib, batch * m * n * 4, rank, world, group)
+        self.c = torch.as_tensor(_DeviceArray(self.buf.own, batch * m * n), device="cuda")
+
+    def compute(self, stream=None) -> int:
+        from . import cublas as cb
+        if self.nb == 0:
+            return 0
+        return self.h.gemm_strided_batched_ex(cb.CUBLAS_OP_T, cb.CUBLAS_OP_N, self.m, self.n, self.k, 1.0,
+                                              self.A.data_ptr(), self.dtype_code, self.k, self.sA, self.B.data_ptr(),
+                                              self.dtype_code, self.k, self.sB, 0.0,
+                                              self.buf.own + self.b0 * self.m * self.n * 4, cb.CUDA_R_32F, self.m,
+                                              self.m * self.n, self.nb, cb.CUBLAS_COMPUTE_32F)
+
+    def push(self, stream=None) -> int:
+        if self.nb == 0:
+            return 0
+        self.copies.after(stream)
+        slab = self.m * self.n
+        return self.lib.lib.tb200_push_block(self.buf.array, self.world, self.rank, self.b0 * slab, self.nb * slab, 0, 1,
+                                             self.batch * slab, 4, self.copies.array, self.world)
+
+    def run(self, x=None, stream=None) -> int:
+        return self.compute(stream) or self.push(stream)
+
+    def close(self):
+        self.c = None
+        self.buf.close()
 
 
 class FusedShardedGemm:

@@ -1,7 +1,8 @@
-"""The N-sharded GEMM on every visible GPU, up to 8 (skipped with fewer than 2): both exchanges, every
-rank's full C - including the rows its peers computed and delivered (over NCCL, or by P2P stores from the
-peers' epilogues) - checked against the fp64 oracle on seeded row samples. m is not a multiple of the
-rank count, so the last rank owns fewer rows."""
+"""The sharded GEMMs on every visible GPU, up to 8 (skipped with fewer than 2): every exchange, every
+rank's full C - including the rows its peers computed and delivered (over NCCL, by P2P stores from the
+peers' epilogues, or by the peers' copy engines) - checked against the fp64 oracle on seeded row samples.
+m is not a multiple of the rank count, so the last rank owns fewer rows. The batch-sharded form splits a
+strided batch of 5 elements (a ragged share) and checks every element of every rank's C."""
 import os
 import socket
 
@@ -30,7 +31,8 @@ def _worker(rank, world, port, mode, m, n, k, q):
     ok, info, used = False, "", mode
     try:
         from macuda_b200 import cublas as cb
-        from macuda_b200.dist import FusedShardedGemm, ShardedGemm, shard_rows, step_barrier
+        from macuda_b200.dist import (BatchShardedGemm, CopyEngineShardedGemm, CopyStreams, FusedShardedGemm,
+                                      ShardedGemm, shard_rows, step_barrier)
         from oracle import oracle as O
         lib = cb.library()
         h = lib.handle()
@@ -42,7 +44,53 @@ def _worker(rank, world, port, mode, m, n, k, q):
         first, rows, _ = shard_rows(m, world, rank)
         w_local = torch.from_numpy(W[first * k:(first + rows) * k].view(np.int16).copy()).cuda()
         x = torch.from_numpy(X.view(np.int16)).cuda()
-        if mode in ("multicast", "p2p"):
+        if mode == "batch":
+            nb_total = 5
+            Wb = O.to_bits(rng.normal(0, 0.02, nb_total * m * k).astype(np.float32), O.F16)
+            Xb = O.to_bits(rng.normal(0, 1, nb_total * k * n).astype(np.float32), O.F16)
+            b0, nb, _ = shard_rows(nb_total, world, rank)
+            copies = CopyStreams(world)
+            wl = torch.from_numpy(Wb[b0 * m * k:(b0 + max(nb, 1)) * m * k].view(np.int16).copy()).cuda()
+            xl = torch.from_numpy(Xb[b0 * k * n:(b0 + max(nb, 1)) * k * n].view(np.int16).copy()).cuda()
+            g = BatchShardedGemm(lib, h, m, n, k, nb_total, rank, world, wl, m * k, xl, k * n, cb.CUDA_R_16F, copies)
+            g.c.fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier()
+            st = 0
+            for _ in range(2):
+                st = st or g.run(None, stream)
+                copies.join(stream)
+                step_barrier(stream)
+            torch.cuda.synchronize()
+            C = g.c.cpu().numpy()
+            rows_s = np.unique(np.concatenate([np.arange(0, m, 41), [m - 1]])).astype(np.int32)
+            res = {"ok": True}
+            for b in range(nb_total):
+                R, S = O.gemm(1, 0, m, n, k, 1.0, Wb[b * m * k:(b + 1) * m * k], O.F16, k, Xb[b * k * n:(b + 1) * k * n],
+                              O.F16, k, rows=rows_s)
+                r = O.check(O.extract(C[b * m * n:(b + 1) * m * n], O.F32, m, n, m, rows=rows_s), R, S, O.F32)
+                if not r["ok"]:
+                    res = dict(r, element=b)
+            ok, info = (st == 0 and res["ok"]), f"st={st} {res}"
+            g.close()
+            h.close()
+            q.put((rank, ok, info, used))
+            dist.destroy_process_group()
+            return
+        if mode == "ce":
+            copies = CopyStreams(world)
+            g = CopyEngineShardedGemm(lib, h, m, n, k, rank, world, w_local, cb.CUDA_R_16F, copies)
+            g.c.fill_(float("nan"))
+            torch.cuda.synchronize()
+            dist.barrier()
+            st = 0
+            for chunks in (1, 3):  # the second pass, in three column chunks, overwrites the first in place
+                st = st or g.run(x, stream, chunks=chunks)
+                copies.join(stream)
+                step_barrier(stream)
+            torch.cuda.synchronize()
+            C = g.c.cpu().numpy()
+        elif mode in ("multicast", "p2p"):
             g = FusedShardedGemm(lib, h, m, n, k, rank, world, w_local, cb.CUDA_R_16F,
                                  exchange="auto" if mode == "multicast" else "p2p")  # auto: multicast if present
             used = g.exchange
@@ -64,7 +112,7 @@ def _worker(rank, world, port, mode, m, n, k, q):
         R, S = O.gemm(1, 0, m, n, k, 1.0, W, O.F16, k, X, O.F16, k, rows=rows_s)
         res = O.check(O.extract(C, O.F32, m, n, m, rows=rows_s), R, S, O.F32)
         ok, info = (st == 0 and res["ok"]), f"st={st} {res}"
-        if mode in ("multicast", "p2p"):
+        if mode in ("multicast", "p2p", "ce"):
             g.close()
         h.close()
     except Exception as ex:
@@ -73,7 +121,7 @@ def _worker(rank, world, port, mode, m, n, k, q):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["multicast", "p2p", "allgather"])
+@pytest.mark.parametrize("mode", ["ce", "batch", "multicast", "p2p", "allgather"])
 def test_sharded_gemm_on_all_gpus(mode):
     import torch
     world = min(torch.cuda.device_count(), 8)
