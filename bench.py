@@ -77,8 +77,9 @@ class ClockSampler:
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, period_ms: int = 100):
         self.dev = device_index
+        self.period_ms = period_ms
         self.samples = []
         self.proc = None
         self.t0 = self.t1 = None
@@ -87,7 +88,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.dev}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", str(self.period_ms)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
             return
@@ -104,6 +105,10 @@ class ClockSampler:
         else:
             self.t1 = time.time()
 
+    def window(self, t0, t1):
+        """median SM clock and the throttle reasons of the samples taken between wall times t0 and t1"""
+        return self._summary([s for t, s in list(self.samples) if t0 <= t <= t1])
+
     def stop(self):
         if self.proc is None:
             return None
@@ -116,6 +121,10 @@ class ClockSampler:
         rows = [s for t, s in self.samples if self.t0 is None or (self.t0 - 0.15 <= t <= (self.t1 or t) + 0.15)]
         if not rows:
             rows = [s for _, s in self.samples]
+        return self._summary(rows)
+
+    @staticmethod
+    def _summary(rows):
         sm, smax, reasons = [], 0.0, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for r in rows:
@@ -254,13 +263,16 @@ def decode_figures(torch, lib, cb, dtype_code, dtype):
     return out
 
 
-def config_figures(torch, lib, cb, dtype_code, dtype, only=None, reps_override=None):
+def config_figures(torch, lib, cb, dtype_code, dtype, only=None, reps_override=None, clocks=None):
     """Configs 3 and 5: attention batched GEMMs (strided with the GQA heads folded into n, and pointer arrays
     with each KV head's pointer repeated for its 4 query heads), MoE expert GEMMs (pointer arrays over 128
     experts, 32 tokens each) and square GEMMs, all T,N with f32 C as ggml issues them. Per case: device
     time (CUDA events around back-to-back calls, median of 3 repeats), TFLOP/s, compulsory bytes / time, and
     the fraction of the measured peak of its bound (HBM copy bandwidth, or burst bf16 tensor throughput).
-    only: run just the case of that name (bench.py --case, for profiling one kernel)."""
+    only: run just the case of that name (bench.py --case, for profiling one kernel). clocks: a running
+    ClockSampler; the square cases, timed for about half a second each, then carry the median SM clock of their
+    own window and their time scaled to the maximum clock (us x MHz / max MHz), which compares the two input
+    types at equal clocks."""
     pk = peaks()
     out = {}
     h = lib.handle()
@@ -286,6 +298,7 @@ def config_figures(torch, lib, cb, dtype_code, dtype, only=None, reps_override=N
                 return
         torch.cuda.synchronize()
         ts = []
+        w0 = time.time()
         for _ in range(3):
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(s)
@@ -294,11 +307,18 @@ def config_figures(torch, lib, cb, dtype_code, dtype, only=None, reps_override=N
             e1.record(s)
             torch.cuda.synchronize()
             ts.append(e0.elapsed_time(e1) * 1e3 / reps)
+        w1 = time.time()
         us = statistics.median(ts)
         tf, gbs = flop / us / 1e6, byts / us / 1e3
         frac = gbs / pk["hbm_gbs"] if bound == "hbm" else tf / pk["bf16_tflops"]
         out[name] = {"us": round(us, 2), "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "bound": bound,
                      "frac_of_measured_peak": round(frac, 3)}
+        if clocks is not None and name.startswith("c5_square"):
+            time.sleep(0.12)  # the sampler's last reading of the window
+            c = clocks.window(w0, w1)
+            if c:
+                out[name]["clocks"] = c
+                out[name]["us_at_max_clock"] = round(us * c["sm_mhz"] / max(c["sm_max_mhz"], 1.0), 2)
 
     # config 3: 32 query heads / 8 KV heads, head_dim 128, 512 queries, 4096 keys
     Hq, Hkv, D, Tq, Tk = 32, 8, 128, 512, 4096
@@ -433,9 +453,11 @@ def config_figures(torch, lib, cb, dtype_code, dtype, only=None, reps_override=N
             A = (torch.randn(S, S, device="cuda") * 0.02).to(tdt)
             B = torch.randn(S, S, device="cuda").to(tdt)
             C = torch.empty(S * S, device="cuda")
+            # about 0.15 s per repeat: enough clock samples per case
             measure(f"c5_square_{S}_{tname}", lambda: h.gemm_ex(
                 1, 0, S, S, S, 1.0, A.data_ptr(), tcode, S, B.data_ptr(), tcode, S, 0.0, C.data_ptr(), f32, S,
-                cb.CUBLAS_COMPUTE_32F), 3 if S == 16384 else 10, 2.0 * S ** 3, 2 * S * S * 2 + S * S * 4, "tensor")
+                cb.CUBLAS_COMPUTE_32F), {4096: 1500, 8192: 200, 16384: 25}[S], 2.0 * S ** 3, 2 * S * S * 2 + S * S * 4,
+                "tensor")
             del A, B, C
     torch.cuda.empty_cache()
     h.close()
@@ -544,8 +566,8 @@ def sharded_figures(torch, lib, cb, h, stream, rank, world, copies):
         return int(max(3, min(40, 25.0 / max(t_ms, 1e-3))))
 
     # ---- N-sharded along m: lm_head, FFN, squares ----
-    cases = [("lm_head", 128256, 512, 4096, "f16", (1,)), ("ffn_gate_up", 14336, 512, 4096, "f16", (1,)),
-             ("ffn_down", 4096, 512, 14336, "f16", (1,))]
+    cases = [("lm_head", 128256, 512, 4096, "f16", (1, 2, 4)), ("ffn_gate_up", 14336, 512, 4096, "f16", (1, 2)),
+             ("ffn_down", 4096, 512, 14336, "f16", (1, 2))]
     for S in (4096, 8192, 16384):
         for tn in ("f16", "bf16"):
             cases.append((f"square_{S}_{tn}", S, S, S, tn, (1, 4, 8) if S > 4096 else (1, 4)))
@@ -1149,7 +1171,15 @@ def run(args):
         probes = probe_figures(torch, lib)
     configs = None
     if rank == 0 and world == 1 and not args.no_configs:
-        configs = config_figures(torch, lib, cb, ctype, dtype)
+        cs = ClockSampler(local, period_ms=20) if not args.no_clocks else None
+        if cs:
+            cs.start()
+            time.sleep(0.3)
+        try:
+            configs = config_figures(torch, lib, cb, ctype, dtype, clocks=cs)
+        finally:
+            if cs:
+                cs.stop()
     sharded = None
     if world > 1 and args.impl == "ours" and not args.no_sharded_shapes:
         sharded = sharded_figures(torch, lib, cb, h, stream, rank, world, copies or CopyStreams(world))

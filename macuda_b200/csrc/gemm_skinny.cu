@@ -179,6 +179,119 @@ __global__ void __launch_bounds__(SK_WARPS * 32) tb200_gemm_skinny_kernel(const 
   }
 }
 
+// Balanced form, built for weights with fewer than two 16-row blocks per SM (4096-row weights on 148 SMs: one CTA
+// per block leaves some SMs with two blocks and some with one); opt-in, see tb200_skinny_bal_plan. The grid has G
+// CTAs, two per SM, and CTA i takes
+// the i-th of G equal contiguous ranges of the m / 16 x k / 32 units (16-row block, 32-wide chunk), so that every
+// SM streams the same bytes. A range is cut at block boundaries into segments; its warps sum a segment as the
+// per-block kernel does. A block inside one range is stored directly. A block shared by several CTAs (at most
+// nslots) is finished by the last to arrive: each contributor parks its 16 x 8 partial tile in ws at its slot (its
+// index among the block's CTAs), fences, and counts itself on cnt[block]; the last one adds the parked tiles in
+// slot order (so the sum is the same whichever CTA arrives last), stores C and resets the counter to zero for the
+// next launch. No CTA waits for another.
+__device__ __forceinline__ long long bal_cta_of(long long x, long long U, long long G) {
+  long long i = x * G / U;
+  while (i + 1 < G && (i + 1) * U / G <= x) ++i;
+  while (i > 0 && i * U / G > x) --i;
+  return i;
+}
+
+template <typename T, int SK_WARPS, int SK_UNROLL>
+__global__ void __launch_bounds__(SK_WARPS * 32, 2)
+    tb200_gemm_skinny_bal_kernel(const tb200_gemm_t g, float *ws, unsigned *cnt, int nslots) {
+  __shared__ float red[SK_WARPS][SK_ROWS][8];
+  __shared__ int s_last;
+  griddep_wait();
+  griddep_launch_dependents();
+  const T *A = (const T *)g.A;
+  const T *B = (const T *)g.B;
+  char *C = (char *)g.C;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int gi = lane >> 2, ci = lane & 3;
+  const long long nch = g.k >> 5;  // the host guarantees k % 32 == 0
+  const long long blocks = (g.m + SK_ROWS - 1) / SK_ROWS;
+  const long long U = blocks * nch, G = gridDim.x, i = blockIdx.x;
+  const long long u1 = (i + 1) * U / G;
+  const bool ok_col = gi < g.n;
+  const T *pB = B + (long long)(ok_col ? gi : 0) * g.ldb + 8 * ci;
+  const int r = threadIdx.x & 15, col = threadIdx.x >> 4;
+  for (long long u = i * U / G; u < u1;) {
+    const long long blk = u / nch;
+    const int c0 = (int)(u - blk * nch);
+    const int c1 = (int)(nch < c0 + (u1 - u) ? nch : c0 + (u1 - u));
+    u += c1 - c0;
+    const int row0 = (int)blk * SK_ROWS;
+    const int ra = row0 + gi, rb = row0 + gi + 8;
+    const bool ok_a = ra < g.m, ok_b = rb < g.m;
+    const T *pa = A + (long long)(ok_a ? ra : 0) * g.lda + 8 * ci;
+    const T *pb = A + (long long)(ok_b ? rb : 0) * g.lda + 8 * ci;
+    float d[4] = {0.f, 0.f, 0.f, 0.f};
+    int j = c0 + warp;
+    for (; j + (SK_UNROLL - 1) * SK_WARPS < c1; j += SK_UNROLL * SK_WARPS) {
+      uint4 va[SK_UNROLL], vb[SK_UNROLL], vB[SK_UNROLL];
+#pragma unroll
+      for (int q = 0; q < SK_UNROLL; ++q) {
+        const long long off = (long long)(j + q * SK_WARPS) * 32;
+        va[q] = ld_stream_v4(pa + off);
+        vb[q] = ld_stream_v4(pb + off);
+        vB[q] = ld_cached_v4(pB + off);
+      }
+#pragma unroll
+      for (int q = 0; q < SK_UNROLL; ++q) {
+        if (!ok_col) vB[q] = make_uint4(0, 0, 0, 0);
+        mma16816<T>(d, va[q].x, vb[q].x, va[q].y, vb[q].y, vB[q].x, vB[q].y);
+        mma16816<T>(d, va[q].z, vb[q].z, va[q].w, vb[q].w, vB[q].z, vB[q].w);
+      }
+    }
+    for (; j < c1; j += SK_WARPS) {
+      const long long off = (long long)j * 32;
+      uint4 va = ld_stream_v4(pa + off), vb = ld_stream_v4(pb + off), vB = ld_cached_v4(pB + off);
+      if (!ok_col) vB = make_uint4(0, 0, 0, 0);
+      mma16816<T>(d, va.x, vb.x, va.y, vb.y, vB.x, vB.y);
+      mma16816<T>(d, va.z, vb.z, va.w, vb.w, vB.z, vB.w);
+    }
+    red[warp][gi][2 * ci] = d[0];
+    red[warp][gi][2 * ci + 1] = d[1];
+    red[warp][gi + 8][2 * ci] = d[2];
+    red[warp][gi + 8][2 * ci + 1] = d[3];
+    __syncthreads();
+    float sum = 0.f;
+    if (threadIdx.x < SK_ROWS * 8) {
+#pragma unroll
+      for (int w = 0; w < SK_WARPS; ++w) sum += red[w][r][col];
+    }
+    bool store = c0 == 0 && c1 == nch;
+    if (!store) {
+      const long long first = bal_cta_of(blk * nch, U, G), last = bal_cta_of(blk * nch + nch - 1, U, G);
+      const int slot = (int)(i - first), ncontrib = (int)(last - first + 1);
+      if (threadIdx.x < SK_ROWS * 8) ws[((long long)blk * nslots + slot) * (SK_ROWS * 8) + threadIdx.x] = sum;
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) s_last = atomicAdd(&cnt[blk], 1u) == (unsigned)(ncontrib - 1);
+      __syncthreads();
+      store = s_last != 0;
+      if (store) {
+        __threadfence();
+        if (threadIdx.x < SK_ROWS * 8) {
+          sum = 0.f;
+          for (int q = 0; q < ncontrib; ++q) sum += __ldcg(&ws[((long long)blk * nslots + q) * (SK_ROWS * 8) + threadIdx.x]);
+        }
+        if (threadIdx.x == 0) atomicExch(&cnt[blk], 0u);  // ready for the next launch
+      }
+    }
+    if (store && threadIdx.x < SK_ROWS * 8) {
+      const int row = row0 + r;
+      if (row < g.m && col < g.n) {
+        const long long idx = row + (long long)col * g.ldc;
+        float v = g.alpha * sum;
+        if (g.beta != 0.f) v += g.beta * load_out(C, idx, g.out_type);
+        store_out(C, idx, v, g.out_type);
+      }
+    }
+    __syncthreads();  // red is reused by the next segment
+  }
+}
+
 }  // namespace
 
 extern "C" int tb200_skinny_ok(const tb200_gemm_t *g) {
@@ -247,6 +360,65 @@ extern "C" __attribute__((visibility("default"))) int tb200_skinny_shape(long lo
   if (unroll) *unroll = cfg == SK_CFG_4x8 ? 8 : cfg == SK_CFG_8x4 ? 4 : 2;
   if (slices) *slices = S;
   return 0;
+}
+
+// The balanced decode's workspace keeps the same layout for every launch, so that no launch's parked tiles land
+// where another launch keeps its counters: BAL_MAX_BLOCKS counters (zero between launches) first, then the parked
+// tiles. At most BAL_MAX_BLOCKS 16-row blocks (65536 rows) take this kernel.
+#define BAL_MAX_BLOCKS 4096
+#define BAL_CNT_BYTES (BAL_MAX_BLOCKS * 4)
+
+// The balanced decode's grid, slots per block and workspace bytes, or 0 when the GEMM is not one for it: batch 1,
+// plain pointers, k % 32 == 0, at most BAL_MAX_BLOCKS blocks. Opt-in (TB200_SKINNY_BAL=1, read per call): on the
+// B200 it ran slower than the per-block kernel on the 4096-row weights it was built for (4096 x 4096: 14.5 against
+// 9.5-11 us; 4096 x 14336: 25 against 21 us). Each range ends in one or two segment tails (reduction, fence,
+// counter) during which the CTA has no loads in flight, which costs more than the balance gains.
+extern "C" size_t tb200_skinny_bal_plan(const tb200_gemm_t *g, int num_sms, int *grid, int *nslots) {
+  if (!tb200_skinny_ok(g) || g->batch != 1 || g->Aarr || g->k % 32 != 0 || g->k <= 0) return 0;
+  const char *e = getenv("TB200_SKINNY_BAL");
+  if (e && *e == '0') return 0;
+  const char *fc = getenv("TB200_SKINNY_CFG"), *fs = getenv("TB200_SKINNY_SPLIT");
+  if (((fc && *fc) || (fs && *fs)) && !(e && *e == '1')) return 0;  // a forced per-block configuration
+  if (num_sms <= 0) num_sms = 148;
+  const long long blocks = (g->m + SK_ROWS - 1) / SK_ROWS, nch = g->k / 32;
+  if (blocks > BAL_MAX_BLOCKS || (blocks >= 2LL * num_sms && !(e && *e == '1'))) return 0;
+  const long long U = blocks * nch;
+  long long G = 2LL * num_sms;
+  if (G > U / 32) G = U / 32;  // at least 32 chunks (two per warp) a CTA
+  if (G < 2) return 0;
+  const long long per = U / G;  // every range holds at least `per` units: a block meets at most this many CTAs
+  const long long ns = (nch + per - 1) / per + 1;
+  *grid = (int)G;
+  *nslots = (int)ns;
+  return (size_t)BAL_CNT_BYTES + (size_t)(blocks * ns) * SK_ROWS * 8 * sizeof(float);
+}
+
+extern "C" int tb200_launch_skinny_bal(const tb200_gemm_t *g, void *ws, size_t ws_bytes, cudaStream_t s) {
+  int G = 0, ns = 0;
+  const size_t need = tb200_skinny_bal_plan(g, tb200_num_sms(), &G, &ns);
+  if (!need || !ws || ws_bytes < need || ((uintptr_t)ws & 255)) return (int)cudaErrorNotSupported;
+  unsigned *cnt = (unsigned *)ws;
+  float *parked = (float *)((char *)ws + BAL_CNT_BYTES);
+  if (tb200_trace())
+    fprintf(stderr, "[trace] launch tb200_gemm_skinny_bal<W=16,U=2> grid=(%d,1,1) block=(512,1,1) slots=%d m=%d n=%d k=%d\n",
+            G, ns, g->m, g->n, g->k);
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  int na = 0;
+  if (tb200_pdl()) {
+    at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  cfg.gridDim = dim3((unsigned)G, 1, 1);
+  cfg.blockDim = dim3(512, 1, 1);
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = na;
+  cudaError_t e = g->in_type == TB200_F16
+                      ? cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_bal_kernel<__half, 16, 2>, *g, parked, cnt, ns)
+                      : cudaLaunchKernelEx(&cfg, tb200_gemm_skinny_bal_kernel<__nv_bfloat16, 16, 2>, *g, parked, cnt, ns);
+  return (int)e;
 }
 
 extern "C" int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s) {

@@ -96,6 +96,14 @@ struct TcParams {
   // outside [0, n_src) is read as column 0 and its column of the product is zero
   const int *gidx;
   int n_src;
+  // epilogue through TMA stores (a third tensor map, of C): each epilogue warp stages its 32 rows x 32 columns in
+  // shared memory and one lane stores them as one tiled copy into this GPU's own C (plain GEMMs and strided
+  // batches with beta == 0; the map covers m x n (x batch), so rows and columns past the ends are clipped)
+  int c_tma, c_batched;
+  // bounded waits: budget of every pipeline wait in SM cycles (WAIT_BUDGET_CYC unless a test shortens it), and
+  // the test-only stall: the MMA thread first waits on a barrier nothing arrives at, so that its wait runs out
+  uint64_t wait_budget;
+  int test_stall;
 };
 
 constexpr int TC_MAX_GROUPS = TB200_MAX_GROUPS;
@@ -112,9 +120,10 @@ struct TcCfg {
   static constexpr int STAGES_RAW = 196608 / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
+  static constexpr int STG_BYTES = 4 * 4096;  // epilogue staging: 32 x 32 f32 per epilogue warp
   static constexpr int BAR_BYTES = 256;
   static constexpr int GRP_BYTES = 2 * 4 * (TC_MAX_GROUPS + 1);  // grouped GEMM: column offsets + tile prefix
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + BAR_BYTES + GRP_BYTES;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + GRP_BYTES;
 };
 
 
@@ -198,7 +207,7 @@ __device__ __forceinline__ void load_operand(uint8_t *dst, const CUtensorMap *tm
 template <int KIND, int BN, int KC, int CG, int KS>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tb200_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                         const TcParams p) {
+                         const __grid_constant__ CUtensorMap tmC, const TcParams p) {
   using Cfg = TcCfg<BN, KC, CG>;
   constexpr int STAGES = Cfg::STAGES;
   static_assert(KS == 1 || (BN >= 64 && STAGES * Cfg::STAGE_BYTES >= TC_BM * (BN / 2) * 4),
@@ -209,7 +218,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t *smA = smem;
   uint8_t *smB = smem + STAGES * Cfg::A_BYTES;
-  uint64_t *bars = (uint64_t *)(smem + STAGES * Cfg::STAGE_BYTES);
+  uint8_t *stg_all = smem + STAGES * Cfg::STAGE_BYTES;  // epilogue staging, 4 KB per epilogue warp
+  uint64_t *bars = (uint64_t *)(stg_all + Cfg::STG_BYTES);
   uint64_t *full = bars;
   uint64_t *empty = bars + STAGES;
   uint64_t *tfull = bars + 2 * STAGES;
@@ -258,6 +268,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     fence_mbar_init();
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (p.c_tma) prefetch_tmap(&tmC);
   }
   if (warp == 1) {
     if (CG == 1) {
@@ -334,7 +345,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int kb = kb_lo; kb < kb_hi; ++kb) {
         int got = 1;
         if (lane == 0) {
-          got = mbar_wait(&empty[s], ph ^ 1u, abort_flag, WAIT_BUDGET_CYC) ? 1 : 0;
+          got = mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.wait_budget) ? 1 : 0;
           if (got) mbar_arrive_expect_tx(&full[s], (uint32_t)Cfg::B_BYTES);
         }
         got = __shfl_sync(0xffffffffu, got, 0);  // also orders the expect_tx before every lane's copy
@@ -382,7 +393,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           fence_tensormap_acquire(tm);
         }
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
-          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, WAIT_BUDGET_CYC)) break;
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort_flag, p.wait_budget)) break;
           // the even CTA announces the bytes of both CTAs; the odd CTA's copies only complete them
           if (leader) mbar_arrive_expect_tx(&full[s], (uint32_t)(stage_bytes * CG));
           load_operand<KC, CG>(base + s * stage_bytes, tm, &full[s], lead_full0 + (uint32_t)(s * 8), mn_major,
@@ -422,13 +433,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const uint32_t empty0_l = smem_u32(empty), tfull0_l = smem_u32(tfull), drain_l = smem_u32(drain);
       const uint32_t empty0_p = CG == 2 ? mapa_shared(empty0_l, pair_odd) : 0u;
       const uint32_t tfull0_p = CG == 2 ? mapa_shared(tfull0_l, pair_odd) : 0u;
+      // test-only (TB200_TEST_STALL=1): a wait that nothing completes - no CTA of a single-CTA, unsplit tile
+      // arrives on xfull - runs out of its budget and takes the abort path below
+      if (p.test_stall && KS == 1 && CG == 1) (void)mbar_wait(xfull, 0, abort_flag, p.wait_budget);
       for (long long t = t_first; t < total_tiles && !*abort_flag; t += t_step) {
-        if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, WAIT_BUDGET_CYC)) break;
+        if (!mbar_wait(&tempty[acc], aph ^ 1u, abort_flag, p.wait_budget)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
         bool ok = true;
         for (int kb = kb_lo; kb < kb_hi; ++kb) {
-          if (!mbar_wait(&full[s], ph, abort_flag, WAIT_BUDGET_CYC)) {
+          if (!mbar_wait(&full[s], ph, abort_flag, p.wait_budget)) {
             ok = false;
             break;
           }
@@ -489,27 +503,38 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int b = tc.b, mt = tc.mt;
       // one lane waits, the warp follows its verdict: tcgen05.ld below needs the whole warp converged
       int got = 0;
-      if (lane == 0) got = mbar_wait(&tfull[acc], aph, abort_flag, WAIT_BUDGET_CYC) ? 1 : 0;
+      if (lane == 0) got = mbar_wait(&tfull[acc], aph, abort_flag, p.wait_budget) ? 1 : 0;
       got = __shfl_sync(0xffffffffu, got, 0);
       if (!got) break;
       tc_fence_after();
+      // TMEM address of 32-column chunk c of this warp's lane quadrant in the current accumulator
+      const uint32_t t_chunk0 = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      // Chunks go through two register sets: the load of chunk c + 1 is issued before chunk c is stored, so
+      // its latency hides behind the stores (tcgen05.wait::ld then waits only for what is left of it).
+      uint32_t ra[32], rb[32];
       if (KS == 2) {
         // park the partial sums of the peer's columns, announce them, wait for the peer's of this CTA's own
         float4 *park = (float4 *)smem;  // [chunk][4 columns][quadrant][lane]: a warp's stores are contiguous
+        tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)(o_lo * 32), ra);
+        tmem_ld_wait_regs(ra);
 #pragma unroll 1
         for (int c = 0; c < HCH; ++c) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + (o_lo + c) * 32), r);
-          tmem_ld_wait();
+          const bool more = c + 1 < HCH;
+          if (more) tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)((o_lo + c + 1) * 32), rb);
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             park[((c * 8 + q) * 4 + quad) * 32 + lane] =
-                make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
-                            __uint_as_float(r[4 * q + 3]));
+                make_float4(__uint_as_float(ra[4 * q]), __uint_as_float(ra[4 * q + 1]), __uint_as_float(ra[4 * q + 2]),
+                            __uint_as_float(ra[4 * q + 3]));
+          if (more) {
+            tmem_ld_wait_regs(rb);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ra[j] = rb[j];
+          }
         }
         mbar_arrive_cluster(mapa_shared(smem_u32(xfull), xpeer));  // every thread releases its own stores
         int parked = 0;
-        if (lane == 0) parked = mbar_wait_cluster(xfull, xph, abort_flag, WAIT_BUDGET_CYC) ? 1 : 0;
+        if (lane == 0) parked = mbar_wait_cluster(xfull, xph, abort_flag, p.wait_budget) ? 1 : 0;
         parked = __shfl_sync(0xffffffffu, parked, 0);
         __syncwarp();  // lane 0's acquire orders the peer's parked sums before every lane's reads
         xph ^= 1u;
@@ -519,11 +544,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int n0 = tc.n0;
       char *Cb = p.Carr ? (char *)p.Carr[b] : (char *)p.C + (p.groups > 0 ? 0ll : (long long)b * p.sC * osz);
       const bool row_ok = row < p.m;
-#pragma unroll 1
-      for (int c = c_lo; c < c_lo + HCH; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        tmem_ld_wait();
+      // one chunk's epilogue: the peer's partial sums added (k split), alpha / beta, conversion, stores
+      auto store_chunk = [&](uint32_t(&r)[32], int c) {
         if (KS == 2) {  // own sum + the peer's (two terms: the same value whichever CTA adds them)
           const uint32_t pk = mapa_shared(smem_u32(smem), xpeer);
 #pragma unroll
@@ -537,6 +559,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
         const int col0 = n0 + c * 32;
+        if (p.c_tma) {
+          // stage the warp's 32 rows x 32 columns (column-major, as C) and store them with one TMA copy; rows and
+          // columns outside C are clipped by the map. The previous chunk's store must have read the buffer.
+          const int wrow = mt * (TC_BM * CG) + (int)rank * TC_BM + quad * 32;
+          if (wrow < p.m && col0 < tc.n_end) {
+            uint8_t *stg = stg_all + quad * 4096;
+            if (lane == 0) bulk_wait_read_all();
+            __syncwarp();
+            if (p.out_type == 0) {
+              float *st = (float *)stg;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) st[j * 32 + lane] = p.alpha * __uint_as_float(r[j]);
+            } else if (p.out_type == 1) {
+              __half *st = (__half *)stg;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) st[j * 32 + lane] = __float2half_rn(p.alpha * __uint_as_float(r[j]));
+            } else {
+              __nv_bfloat16 *st = (__nv_bfloat16 *)stg;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) st[j * 32 + lane] = __float2bfloat16_rn(p.alpha * __uint_as_float(r[j]));
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              if (p.c_batched) tma_store_3d(&tmC, stg, wrow, col0, b);
+              else tma_store_2d(&tmC, stg, wrow, col0);
+              bulk_commit();
+            }
+          }
+          return;
+        }
         if (p.gidx && col0 < tc.n_end) {  // fused gather: a column whose token id is out of range is zero
           const int cj = col0 + lane;
           const int id = cj < tc.n_end ? __ldg(p.gidx + cj) : 0;
@@ -586,6 +639,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                           p.out_type);
           }
         }
+      };
+      tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)(c_lo * 32), ra);
+      tmem_ld_wait_regs(ra);
+#pragma unroll 1
+      for (int c = c_lo; c < c_lo + HCH; ++c) {
+        const bool more = c + 1 < c_lo + HCH;
+        if (more) tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)((c + 1) * 32), rb);
+        store_chunk(ra, c);
+        if (more) {
+          tmem_ld_wait_regs(rb);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ra[j] = rb[j];
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -596,6 +662,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       acc ^= 1;
       if (acc == 0) aph ^= 1u;
     }
+    if (p.c_tma && lane == 0) bulk_wait_all();  // the staged stores have completed before the CTA leaves
   }
 
   if ((p.nrep > 0 || p.mc) && warp >= 2 && warp <= 5) __threadfence_system();  // peers' replicas: stores performed
@@ -666,8 +733,29 @@ bool make_map(CUtensorMap *tm, CUtensorMapDataType dt, int esz, const void *base
   return r == CUDA_SUCCESS;
 }
 
+// the C map of the TMA-store epilogue: m x n (x batch) elements of the output type, a 32 x 32 box, no swizzle
+bool make_c_map(CUtensorMap *tm, int out_type, void *C, long long m, long long n, long long ldc, int batch,
+                long long sC, int *batched) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc = encode_fn();
+  if (!enc) return false;
+  const int esz = out_type == TB200_F32 ? 4 : 2;
+  const CUtensorMapDataType dt = out_type == TB200_F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : out_type == TB200_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                         : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const bool b3 = batch > 1;
+  cuuint64_t dims[3] = {(cuuint64_t)m, (cuuint64_t)n, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ldc * esz), (cuuint64_t)(sC * esz)};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(tm, dt, b3 ? 3 : 2, C, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  *batched = b3 ? 1 : 0;
+  return r == CUDA_SUCCESS;
+}
+
 template <int KIND, int BN, int KC, int CG, int KS = 1>
-int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, int num_sms, cudaStream_t s) {
+int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &tcm, const TcParams &p, int num_sms,
+              cudaStream_t s) {
   using Cfg = TcCfg<BN, KC, CG>;
   constexpr int CSIZE = CG * KS;  // CTAs per tile: one cluster
   auto kern = tb200_gemm_tc_kernel<KIND, BN, KC, CG, KS>;
@@ -706,9 +794,9 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, i
   if (tb200_trace())
     fprintf(stderr,
             "[trace] launch tb200_gemm_tc<%s,BN=%d,KC=%d,CG=%d%s> grid=(%u,1,1) block=(%d,1,1) smem=%d stages=%d m=%d "
-            "n=%d k=%d batch=%d\n",
+            "n=%d k=%d batch=%d store=%s\n",
             KIND ? "tf32" : "f16", BN, KC, CG, KS == 2 ? ",KS=2" : "", grid, TC_THREADS, Cfg::SMEM_BYTES, Cfg::STAGES,
-            p.m, p.n, p.k, p.batch);
+            p.m, p.n, p.k, p.batch, p.c_tma ? "tma" : "lanes");
   // Programmatic stream serialization: this grid may be scheduled while the kernel before it in the stream
   // finishes (the kernel waits for it with griddep_wait before touching memory), which hides the launch and
   // the set-up of barriers and tensor memory behind that kernel's last tiles.
@@ -733,7 +821,7 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const TcParams &p, i
   cfg.stream = s;
   cfg.attrs = at;
   cfg.numAttrs = na;
-  return (int)cudaLaunchKernelEx(&cfg, kern, ta, tb, p);
+  return (int)cudaLaunchKernelEx(&cfg, kern, ta, tb, tcm, p);
 }
 
 // tile width BN -> k-chunks per stage: the widest single-CTA tile keeps one chunk (four stages of 48 KB);
@@ -839,6 +927,28 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
     e = cudaGetLastError();
     if (e != cudaSuccess) return (int)e;
   }
+  // the TMA-store epilogue, where C is this GPU's own plain or strided C with beta == 0 and its base, leading
+  // dimension and batch stride suit a tensor map (16-byte multiples); TB200_TMA_STORE=0 keeps the per-lane stores
+  // (bisecting; read per call)
+  CUtensorMap tcm;
+  memset(&tcm, 0, sizeof tcm);
+  {
+    const char *e = getenv("TB200_TMA_STORE");
+    const int esc = g->out_type == TB200_F32 ? 4 : 2;
+    if (!(e && *e == '0') && !ptr_ws && !g->nrep && !g->mc && !g->groups && !g->gidx && g->beta == 0.f && g->C &&
+        ((uintptr_t)g->C & 15) == 0 && ((long long)g->ldc * esc) % 16 == 0 &&
+        (g->batch == 1 || (g->sC > 0 && (g->sC * esc) % 16 == 0)))
+      p.c_tma = make_c_map(&tcm, g->out_type, g->C, g->m, g->n, g->ldc, g->batch, g->sC, &p.c_batched) ? 1 : 0;
+  }
+  // TB200_WAIT_BUDGET_CYC shortens the pipeline waits' budget (tests; read per call); the drain waits after an
+  // abort keep theirs. TB200_TEST_STALL=1 plants the MMA thread's wait that nothing completes (tests only).
+  {
+    const char *e = getenv("TB200_WAIT_BUDGET_CYC");
+    const long long v = e && *e ? atoll(e) : 0;
+    p.wait_budget = v > 0 && (uint64_t)v < WAIT_BUDGET_CYC ? (uint64_t)v : WAIT_BUDGET_CYC;
+    const char *st = getenv("TB200_TEST_STALL");
+    p.test_stall = st && *st == '1';
+  }
   p.a_mn = a_mn; p.b_mn = b_mn;
   // K-major: 8-row core groups 1024 bytes apart (SBO), chunk c of a stage rows*128 bytes in, UMMA_K step
   // = 32 bytes inside the swizzle atom. MN-major: 128-byte rows along m/n, 8 k-rows per 1024-byte atom
@@ -869,12 +979,12 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
                          (cg == 2 ? bn == 256 : bn == 64 || bn == 128 || bn == 256) &&
                          p.total_tiles * 2 * cg <= num_sms && (pair >= 2 || want == 1);
     if (allowed && want != 0 && cg == 2) {
-      rc = launch_bn<0, 256, 1, 2, 2>(ta, tb, p, num_sms, s);
+      rc = launch_bn<0, 256, 1, 2, 2>(ta, tb, tcm, p, num_sms, s);
     } else if (allowed && want != 0) {
       switch (bn) {
-        case 64: rc = launch_bn<0, 64, kc_for(64), 1, 2>(ta, tb, p, num_sms, s); break;
-        case 128: rc = launch_bn<0, 128, kc_for(128), 1, 2>(ta, tb, p, num_sms, s); break;
-        default: rc = launch_bn<0, 256, kc_for(256), 1, 2>(ta, tb, p, num_sms, s); break;
+        case 64: rc = launch_bn<0, 64, kc_for(64), 1, 2>(ta, tb, tcm, p, num_sms, s); break;
+        case 128: rc = launch_bn<0, 128, kc_for(128), 1, 2>(ta, tb, tcm, p, num_sms, s); break;
+        default: rc = launch_bn<0, 256, kc_for(256), 1, 2>(ta, tb, tcm, p, num_sms, s); break;
       }
     }
   }
@@ -882,22 +992,22 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
     // launched (or failed) with the k split
   } else if (cg == 2) {
     if (bn == 128)
-      rc = f32in ? launch_bn<1, 128, 2, 2>(ta, tb, p, num_sms, s) : launch_bn<0, 128, 2, 2>(ta, tb, p, num_sms, s);
+      rc = f32in ? launch_bn<1, 128, 2, 2>(ta, tb, tcm, p, num_sms, s) : launch_bn<0, 128, 2, 2>(ta, tb, tcm, p, num_sms, s);
     else
-      rc = f32in ? launch_bn<1, 256, 1, 2>(ta, tb, p, num_sms, s) : launch_bn<0, 256, 1, 2>(ta, tb, p, num_sms, s);
+      rc = f32in ? launch_bn<1, 256, 1, 2>(ta, tb, tcm, p, num_sms, s) : launch_bn<0, 256, 1, 2>(ta, tb, tcm, p, num_sms, s);
   } else if (f32in) {
     switch (bn) {
-      case 32: rc = launch_bn<1, 32, kc_for(32), 1>(ta, tb, p, num_sms, s); break;
-      case 64: rc = launch_bn<1, 64, kc_for(64), 1>(ta, tb, p, num_sms, s); break;
-      case 128: rc = launch_bn<1, 128, kc_for(128), 1>(ta, tb, p, num_sms, s); break;
-      default: rc = launch_bn<1, 256, kc_for(256), 1>(ta, tb, p, num_sms, s); break;
+      case 32: rc = launch_bn<1, 32, kc_for(32), 1>(ta, tb, tcm, p, num_sms, s); break;
+      case 64: rc = launch_bn<1, 64, kc_for(64), 1>(ta, tb, tcm, p, num_sms, s); break;
+      case 128: rc = launch_bn<1, 128, kc_for(128), 1>(ta, tb, tcm, p, num_sms, s); break;
+      default: rc = launch_bn<1, 256, kc_for(256), 1>(ta, tb, tcm, p, num_sms, s); break;
     }
   } else {
     switch (bn) {
-      case 32: rc = launch_bn<0, 32, kc_for(32), 1>(ta, tb, p, num_sms, s); break;
-      case 64: rc = launch_bn<0, 64, kc_for(64), 1>(ta, tb, p, num_sms, s); break;
-      case 128: rc = launch_bn<0, 128, kc_for(128), 1>(ta, tb, p, num_sms, s); break;
-      default: rc = launch_bn<0, 256, kc_for(256), 1>(ta, tb, p, num_sms, s); break;
+      case 32: rc = launch_bn<0, 32, kc_for(32), 1>(ta, tb, tcm, p, num_sms, s); break;
+      case 64: rc = launch_bn<0, 64, kc_for(64), 1>(ta, tb, tcm, p, num_sms, s); break;
+      case 128: rc = launch_bn<0, 128, kc_for(128), 1>(ta, tb, tcm, p, num_sms, s); break;
+      default: rc = launch_bn<0, 256, kc_for(256), 1>(ta, tb, tcm, p, num_sms, s); break;
     }
   }
   if (rc != 0 || !ptr_ws) return rc;

@@ -52,6 +52,10 @@ typedef struct {
 
 int tb200_launch_simt(const tb200_gemm_t *g, cudaStream_t s);
 int tb200_launch_skinny(const tb200_gemm_t *g, cudaStream_t s);
+/* the balanced decode kernel (few 16-row blocks per SM): grid, slots and workspace bytes, 0 when not for this
+ * GEMM; the launch takes a zero-initialised workspace of at least that size, owned by the caller per stream */
+size_t tb200_skinny_bal_plan(const tb200_gemm_t *g, int num_sms, int *grid, int *nslots);
+int tb200_launch_skinny_bal(const tb200_gemm_t *g, void *ws, size_t ws_bytes, cudaStream_t s);
 int tb200_launch_tc(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, cudaStream_t s);
 /* pointer-array batches on the tensor cores: `ws` is device scratch of tb200_tc_ptr_ws_bytes(batch)
  * bytes owned by the caller for the duration of the launch */

@@ -46,46 +46,64 @@ struct tb200_handle {
   void *user_ws;
   size_t user_ws_bytes;
   struct tb200_ws ws[TB200_WS_SLOTS];
+  struct tb200_ws dws[TB200_WS_SLOTS]; /* the balanced decode kernel's workspace, per stream */
   unsigned ws_allocs; /* allocations made, for the tests */
 };
 
-/* scratch of at least `bytes` for the handle's current stream, or NULL (capturing, or out of memory:
- * the caller then takes a path that needs none) */
-static void *handle_scratch(struct tb200_handle *h, size_t bytes) {
+/* scratch of at least `bytes` from one of the handle's per-stream slot arrays (`arr`) for its current stream, or
+ * NULL (capturing, or out of memory: the caller then takes a path that needs none). zero: a new buffer is cleared
+ * on the stream before its first use. */
+static void *stream_slot(struct tb200_handle *h, struct tb200_ws *arr, size_t bytes, size_t min_bytes, int zero) {
   enum cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   int slot = -1;
   for (int i = 0; i < TB200_WS_SLOTS; i++)
-    if (h->ws[i].ptr && h->ws[i].stream == h->stream) {
+    if (arr[i].ptr && arr[i].stream == h->stream) {
       slot = i;
       break;
     }
-  if (slot >= 0 && h->ws[slot].bytes >= bytes) return h->ws[slot].ptr;
+  if (slot >= 0 && arr[slot].bytes >= bytes) return arr[slot].ptr;
   if (cudaStreamIsCapturing(h->stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return NULL;
   if (slot < 0) {
     for (int i = 0; i < TB200_WS_SLOTS && slot < 0; i++)
-      if (!h->ws[i].ptr) slot = i;
+      if (!arr[i].ptr) slot = i;
     if (slot < 0) { /* all slots taken by other streams: retire the first after its stream drains */
       slot = 0;
-      cudaStreamSynchronize(h->ws[0].stream);
+      cudaStreamSynchronize(arr[0].stream);
     }
   }
-  if (h->ws[slot].ptr) {
-    cudaStreamSynchronize(h->ws[slot].stream); /* growth: earlier launches on this stream may still read it */
-    cudaFree(h->ws[slot].ptr);
-    h->ws[slot].ptr = NULL;
-    h->ws[slot].bytes = 0;
+  if (arr[slot].ptr) {
+    cudaStreamSynchronize(arr[slot].stream); /* growth: earlier launches on this stream may still read it */
+    cudaFree(arr[slot].ptr);
+    arr[slot].ptr = NULL;
+    arr[slot].bytes = 0;
   }
-  size_t want = bytes < (64u << 10) ? (64u << 10) : bytes;
+  size_t want = bytes < min_bytes ? min_bytes : bytes;
   void *p = NULL;
   if (cudaMalloc(&p, want) != cudaSuccess) {
     (void)cudaGetLastError();
     return NULL;
   }
-  h->ws[slot].stream = h->stream;
-  h->ws[slot].ptr = p;
-  h->ws[slot].bytes = want;
+  if (zero && cudaMemsetAsync(p, 0, want, h->stream) != cudaSuccess) {
+    (void)cudaGetLastError();
+    cudaFree(p);
+    return NULL;
+  }
+  arr[slot].stream = h->stream;
+  arr[slot].ptr = p;
+  arr[slot].bytes = want;
   h->ws_allocs++;
   return p;
+}
+
+/* the pointer-array tensor maps' scratch: at least 64 KB, grown when a larger batch comes */
+static void *handle_scratch(struct tb200_handle *h, size_t bytes) { return stream_slot(h, h->ws, bytes, 64u << 10, 0); }
+
+/* the balanced decode kernel's workspace: one fixed 1 MB buffer per stream, zeroed once (its counters return to
+ * zero at the end of every launch) */
+#define TB200_DECODE_WS_BYTES (1u << 20)
+static void *decode_scratch(struct tb200_handle *h, size_t bytes) {
+  if (bytes > TB200_DECODE_WS_BYTES) return NULL;
+  return stream_slot(h, h->dws, TB200_DECODE_WS_BYTES, TB200_DECODE_WS_BYTES, 1);
 }
 
 /* ---- environment knobs, read once (the reference's TINYCUBLAS_TC / TINYCUBLAS_GEMM bisect knobs,
@@ -329,7 +347,16 @@ static cublasStatus_t run_gemm_with(struct tb200_handle *h, tb200_gemm_t *g, int
   int rc = 0;
   switch (kind) {
     case TB200_KERNEL_NONE: return CUBLAS_STATUS_SUCCESS;
-    case TB200_KERNEL_SKINNY: rc = tb200_launch_skinny(g, h->stream); break; /* no scratch */
+    case TB200_KERNEL_SKINNY: {
+      /* few 16-row blocks per SM: the balanced kernel, with its workspace (not on the allocation-free entry point,
+       * and not during a capture that would have to allocate it) */
+      int bal_grid = 0, bal_slots = 0;
+      const size_t need = noalloc ? 0 : tb200_skinny_bal_plan(g, sms, &bal_grid, &bal_slots);
+      void *dws = need ? decode_scratch(h, need) : NULL;
+      rc = dws ? tb200_launch_skinny_bal(g, dws, TB200_DECODE_WS_BYTES, h->stream) : (int)cudaErrorNotSupported;
+      if (rc == (int)cudaErrorNotSupported) rc = tb200_launch_skinny(g, h->stream);
+      break;
+    }
     case TB200_KERNEL_TC:
       if (ptr_array && noalloc) {
         rc = tb200_launch_tc_ptr_noalloc(g, tile_n, pair, sms, h->stream);
@@ -416,11 +443,16 @@ cublasStatus_t cublasCreate_v2(cublasHandle_t *handle) {
 cublasStatus_t cublasDestroy_v2(cublasHandle_t handle) {
   struct tb200_handle *h = (struct tb200_handle *)handle;
   if (h) {
-    for (int i = 0; i < TB200_WS_SLOTS; i++)
+    for (int i = 0; i < TB200_WS_SLOTS; i++) {
       if (h->ws[i].ptr) {
         cudaStreamSynchronize(h->ws[i].stream);
         cudaFree(h->ws[i].ptr);
       }
+      if (h->dws[i].ptr) {
+        cudaStreamSynchronize(h->dws[i].stream);
+        cudaFree(h->dws[i].ptr);
+      }
+    }
   }
   free(handle);
   return CUBLAS_STATUS_SUCCESS;

@@ -198,6 +198,63 @@ def test_decode_gemm_ex(lib, h, case):
         assert_ok(run_and_check(lib, h, mode="ex", seed=case["m"] + case["k"] + rep, **case), f"rep {rep}")
 
 
+# the balanced decode kernel (equal ranges of 16-row blocks x 32-wide chunks, two CTAs per SM; blocks shared by
+# several CTAs finished by the last to arrive), opt-in through TB200_SKINNY_BAL=1, on few- and many-block
+# weights. Tails in m, every n, alpha/beta with 16-bit C, bf16, a single block, a tiny k, and each shape twice on
+# the same stream (the per-block counters return to zero)
+BAL_CASES = [
+    dict(m=4096, n=1, k=4096),
+    dict(m=4096, n=8, k=14336),
+    dict(m=1000, n=7, k=1024, out_t=O.F16, alpha=0.5, beta=2.0),
+    dict(m=520, n=2, k=4096, in_t=O.BF16, out_t=O.BF16, alpha=-1.0, beta=1.0),
+    dict(m=14336, n=4, k=4096, sample=160),
+    dict(m=16, n=3, k=4096),
+    dict(m=33, n=5, k=2048, in_t=O.BF16),
+    dict(m=1024, n=8, k=1024),
+]
+
+
+@pytest.mark.parametrize("case", BAL_CASES, ids=[f"{c['m']}x{c['n']}x{c['k']}-{i}" for i, c in enumerate(BAL_CASES)])
+def test_decode_balanced(lib, h, monkeypatch, case):
+    monkeypatch.setenv("TB200_SKINNY_BAL", "1")
+    for rep in range(2):
+        assert_ok(run_and_check(lib, h, mode="ex", seed=case["m"] + case["n"] + case["k"] + rep, **case), f"rep {rep}")
+
+
+def test_decode_balanced_workspace_across_sizes(lib, monkeypatch):
+    """one stream's balanced-decode workspace serves launches of every size in turn: few blocks, then many (whose
+    counters must not be where a smaller launch parked its partial tiles), then few again"""
+    monkeypatch.setenv("TB200_SKINNY_BAL", "1")
+    with lib.handle() as hh:
+        for i, m in enumerate([64, 4096, 16, 14336, 1024, 4096, 48]):
+            assert_ok(run_and_check(lib, hh, m=m, n=1 + i % 8, k=4096, mode="ex", sample=192, seed=600 + i), f"m={m}")
+
+
+def test_decode_balanced_two_streams(lib, monkeypatch):
+    """the balanced kernel's workspace is per (handle, stream): two streams of one handle interleave decode GEMMs"""
+    import torch
+    monkeypatch.setenv("TB200_SKINNY_BAL", "1")
+    from tests.helpers import dev, host
+    rng = np.random.default_rng(71)
+    m, n, k = 4096, 4, 4096
+    A = storage(rng, m * k, O.F16, 0.02)
+    Bs = [storage(rng, k * n, O.F16) for _ in range(2)]
+    dA, dBs = dev(A), [dev(b) for b in Bs]
+    Cs = [torch.full((m * n,), float("nan"), device="cuda") for _ in range(2)]
+    streams = [torch.cuda.Stream() for _ in range(2)]
+    with lib.handle() as hh:
+        for it in range(6):
+            j = it % 2
+            hh.set_stream(streams[j].cuda_stream)
+            assert hh.gemm_ex(1, 0, m, n, k, 1.0, dA.data_ptr(), cb.CUDA_R_16F, k, dBs[j].data_ptr(), cb.CUDA_R_16F, k,
+                              0.0, Cs[j].data_ptr(), cb.CUDA_R_32F, m) == 0
+        torch.cuda.synchronize()
+    rows = np.arange(0, m, 13, dtype=np.int32)
+    for j in range(2):
+        R, S = O.gemm(1, 0, m, n, k, 1.0, A, O.F16, k, Bs[j], O.F16, k, rows=rows)
+        assert_ok(O.check(O.extract(Cs[j].cpu().numpy(), O.F32, m, n, m, rows=rows), R, S, O.F32), f"stream {j}")
+
+
 def test_skinny_pointer_arrays_gqa(lib, h):
     assert_ok(run_and_check(lib, h, m=768, n=8, k=2048, batch=8, mode="ptr", broadcast_a=4, seed=60), "ptr n=8")
 
