@@ -376,12 +376,10 @@ extern "C" __attribute__((visibility("default"))) int tb200_skinny_shape(long lo
 extern "C" size_t tb200_skinny_bal_plan(const tb200_gemm_t *g, int num_sms, int *grid, int *nslots) {
   if (!tb200_skinny_ok(g) || g->batch != 1 || g->Aarr || g->k % 32 != 0 || g->k <= 0) return 0;
   const char *e = getenv("TB200_SKINNY_BAL");
-  if (e && *e == '0') return 0;
-  const char *fc = getenv("TB200_SKINNY_CFG"), *fs = getenv("TB200_SKINNY_SPLIT");
-  if (((fc && *fc) || (fs && *fs)) && !(e && *e == '1')) return 0;  // a forced per-block configuration
+  if (!(e && *e == '1')) return 0;  // opt-in: measured slower than the per-block kernel (above)
   if (num_sms <= 0) num_sms = 148;
   const long long blocks = (g->m + SK_ROWS - 1) / SK_ROWS, nch = g->k / 32;
-  if (blocks > BAL_MAX_BLOCKS || (blocks >= 2LL * num_sms && !(e && *e == '1'))) return 0;
+  if (blocks > BAL_MAX_BLOCKS) return 0;
   const long long U = blocks * nch;
   long long G = 2LL * num_sms;
   if (G > U / 32) G = U / 32;  // at least 32 chunks (two per warp) a CTA
