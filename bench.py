@@ -12,14 +12,14 @@ Inputs are larger than L2 (1.9 GB touched per step), so no flush is needed betwe
 
 At N > 1 (torchrun, one process per GPU, NCCL) each projection is either N-sharded along m (the weight's
 output features: each rank computes its m/N rows) or run whole on every rank, and every rank ends the step
-holding every projection's full C. Default exchange (--exchange ce): a sharded projection's GEMM writes its
-rows into the rank's own C and the copy engines push them into every peer's C (CUDA IPC mappings,
-macuda_b200.dist.CopyEngineShardedGemm); the sharded projections run first, so their copies cross NVLink
-while the SMs run the projections that are whole on every rank; one 4-byte NCCL all-reduce per step is the
-completion barrier. Which projections are sharded is chosen at set-up by timing candidate plans as whole
-steps on every rank (max over ranks). --exchange fused stores the rows into the peers' C from the GEMM
-epilogue instead (P2P), --exchange multicast through an NVLink multicast address, --exchange allgather with
-an NCCL all-gather + layout kernel. Total work is fixed, so scaling is "strong". After the timed region every
+holding every projection's full C. A sharded projection's rows reach the peers one of two ways: the copy
+engines push them after the GEMM (CUDA IPC mappings, macuda_b200.dist.CopyEngineShardedGemm; these shards
+run first, so their copies cross NVLink while the SMs run what follows), or the GEMM epilogue stores them
+into every peer's C (FusedShardedGemm). One 4-byte NCCL all-reduce per step is the completion barrier. The
+plan - which projections are sharded, and how - is chosen at set-up by timing candidate plans as whole steps
+on every rank (max over ranks; --exchange auto, the default). --exchange ce keeps to copy-engine plans,
+--exchange fused decides per projection between epilogue stores and whole, --exchange multicast stores
+through an NVLink multicast address, --exchange allgather uses an NCCL all-gather + layout kernel. Total work is fixed, so scaling is "strong". After the timed region every
 rank checks sampled rows of every projection's C - rows of every peer's shard included - against fp64 on the
 device ("parity", max over ranks), and `sharded_shapes` gives per-shape figures split across the N ranks
 (lm_head, FFN, squares N-sharded; config 3 attention by KV-head groups and config 5 MoE by experts), each
@@ -499,13 +499,14 @@ def probe_figures(torch, lib):
     return out
 
 
-def sharded_figures(torch, lib, cb, h, stream, rank, world, copies):
+def sharded_figures(torch, lib, cb, h, stream, rank, world, copies, ring):
     """Per-shape figures at N > 1 (3 and 5): each case once on one GPU (the whole GEMM,
     every rank timing it on its own GPU), then split across the N ranks:
       * N-sharded along m (the weight's output features): lm_head, FFN gate/up and down, squares
-        4096/8192/16384 in f16 and bf16. Each rank computes its rows into its own full C (ldc = m) and the copy
-        engines push them into every peer's C (tb200_push_block), the columns in `chunks` GEMMs so the copies of
-        one chunk overlap the next chunk's math;
+        4096/8192/16384 in f16 and bf16. Each rank computes its rows into its own full C (ldc = m) and either the
+        copy engines push them into every peer's C (tb200_push_block), the columns in `chunks` GEMMs so the
+        copies of one chunk overlap the next chunk's math, or the GEMM epilogue stores them into every peer's C
+        (tb200_gemm_ex_allgather); both are timed and the faster is reported as e2e;
       * batch-sharded (whole batch elements per rank): config 3 attention by KV-head groups (strided with the 4
         query heads of each KV head folded into n; pointer arrays with each KV head's pointer repeated for its
         query heads), config 5 MoE by experts (pointer arrays, and the grouped GEMM). Each rank's C slab is
@@ -516,6 +517,8 @@ def sharded_figures(torch, lib, cb, h, stream, rank, world, copies):
     R = n1 * B / ((N - 1) * C bytes), B = PEER_GBS: the efficiency bound of a perfectly overlapped exchange (each
     rank receives (N-1)/N of C over its link while computing 1/N of the work). parity: sampled rows of C as rank
     0..N-1 hold it after the exchange (every rank's part included), against fp64 on the device, max over ranks."""
+    import ctypes
+
     import torch.distributed as dist
     from macuda_b200.dist import IpcReplicas, shard_rows, step_barrier
     f32 = cb.CUDA_R_32F
@@ -592,17 +595,26 @@ def sharded_figures(torch, lib, cb, h, stream, rank, world, copies):
                              B.data_ptr() + col0 * k * esz, code, k, 0.0, buf.own + (first + col0 * m) * 4, f32, m,
                              cb.CUBLAS_COMPUTE_32F)
 
-        def sharded(chunks):
+        def sharded(chunks, cs):
             step = -(-n // chunks)
             for col0 in range(0, n, step):
                 nc = min(step, n - col0)
                 if part(col0, nc) != 0:
                     raise RuntimeError(f"{name}: GEMM failed")
-                copies.after(stream)
-                if rows and lib.lib.tb200_push_block(buf.array, world, rank, first, rows, col0, nc, m, 4, copies.array,
-                                                     world) != 0:
+                cs.after(stream)
+                if rows and lib.lib.tb200_push_block(buf.array, world, rank, first, rows, col0, nc, m, 4, cs.array,
+                                                     cs.lanes) != 0:
                     raise RuntimeError(f"{name}: push failed")
-            copies.join(stream)
+            cs.join(stream)
+            step_barrier(stream)
+
+        one = ctypes.c_float(1.0)
+
+        def sharded_p2p():  # the GEMM epilogue stores the rows into every replica (peers' over NVLink)
+            if rows and lib.lib.tb200_gemm_ex_allgather(
+                    h.h, 1, 0, rows, n, k, ctypes.byref(one), A.data_ptr() + first * k * esz, code, k, B.data_ptr(),
+                    code, k, buf.array, world, f32, m, first, cb.CUBLAS_COMPUTE_32F) != 0:
+                raise RuntimeError(f"{name}: sharded GEMM failed")
             step_barrier(stream)
 
         t1 = timed(whole, reps_for(2.0 * m * n * k / 1.2e15 * 1e3))
@@ -610,17 +622,27 @@ def sharded_figures(torch, lib, cb, h, stream, rank, world, copies):
         tc = timed(part, reps)
         best = None
         for ch in chunk_opts:
-            te = timed(lambda: sharded(ch), reps)
-            if best is None or te < best[0]:
-                best = (te, ch)
-        sharded(best[1])
+            for cname, cs in (("every peer at once", copies), ("ring", ring)):
+                te = timed(lambda: sharded(ch, cs), reps)
+                if best is None or te < best[0]:
+                    best = (te, ch, cname, cs)
+        t_ce = best[0]
+        t_p2p = timed(sharded_p2p, reps)
+        if t_p2p < best[0]:
+            best = (t_p2p, "p2p", None, None)
+            sharded_p2p()
+        else:
+            sharded(best[1], best[3])
         torch.cuda.synchronize()
         dist.barrier()
         rws = torch.tensor(parity_rows(m, world, 11 + ci), device="cuda")
         Cfull = torch.as_tensor(_Dev(buf.own, m * n), device="cuda")
         par = check_rows(torch, Cfull, m, n, rws, A[rws], B)
         record(name, 2.0 * m * n * k, m * n * 4, "tensor", t1, tc, best[0], par,
-               {"m": m, "n": n, "k": k, "dtype": tn, "sharded": "m (weight rows)", "chunks": best[1]})
+               {"m": m, "n": n, "k": k, "dtype": tn, "sharded": "m (weight rows)",
+                "exchange": "p2p epilogue stores" if best[1] == "p2p" else
+                f"copy engines ({best[2]}), {best[1]} column chunk(s)",
+                "e2e_us_copy_engines": round(t_ce * 1e3, 1), "e2e_us_p2p_epilogue": round(t_p2p * 1e3, 1)})
         del Cfull
         buf.close()
         del A, B, C1
@@ -648,21 +670,24 @@ def sharded_figures(torch, lib, cb, h, stream, rank, world, copies):
         C1 = torch.empty(total, device="cuda")
         buf = IpcReplicas(lib, total * 4, rank, world)
 
-        def sharded():
+        def sharded(cs):
             if nb and part_fn(buf.own, b0, nb) != 0:
                 raise RuntimeError(f"{name}: GEMM failed")
-            copies.after(stream)
+            cs.after(stream)
             if nb and lib.lib.tb200_push_block(buf.array, world, rank, b0 * slab, nb * slab, 0, 1, total, 4,
-                                               copies.array, world) != 0:
+                                               cs.array, cs.lanes) != 0:
                 raise RuntimeError(f"{name}: push failed")
-            copies.join(stream)
+            cs.join(stream)
             step_barrier(stream)
 
         t1 = timed(lambda: whole_fn(C1.data_ptr()), 10)
         reps = reps_for(t1)
         tc = timed(lambda: part_fn(buf.own, b0, nb) if nb else 0, reps)
-        te = timed(sharded, reps)
-        sharded()
+        te_c = timed(lambda: sharded(copies), reps)
+        te_r = timed(lambda: sharded(ring), reps)
+        te, cs_best = (te_c, copies) if te_c <= te_r else (te_r, ring)
+        extra = dict(extra, exchange="copy engines (" + ("every peer at once" if cs_best is copies else "ring") + ")")
+        sharded(cs_best)
         torch.cuda.synchronize()
         dist.barrier()
         Cfull = torch.as_tensor(_Dev(buf.own, total), device="cuda")
@@ -837,10 +862,28 @@ def run_single(args):
     return 0
 
 
-# candidate sets of projections to N-shard under the copy-engine exchange (the others run whole on every
-# rank); each is timed as a whole step at set-up and the fastest kept
-CE_PLANS = [("lm_head",), ("lm_head", "gate", "up"), ("lm_head", "gate", "up", "down"),
-            ("lm_head", "gate", "up", "down", "q", "o"), ("lm_head", "gate", "up", "down", "q", "o", "k", "v"), ()]
+# candidate plans at N > 1: which projections are N-sharded and how their rows reach the peers ("ce": the copy
+# engines push them after the GEMM, to every peer at once, overlapping the projections that follow; "ring": the
+# same pushes one peer after another in ring order; "p2p": the GEMM epilogue stores them into the peers' C over
+# NVLink); the others run whole on every rank. A plan uses one copy-engine mode. Each is timed as a whole step on
+# every rank at set-up and the fastest kept. The copy engines win with one peer and lose with more (their
+# pushes to several peers at once ran at 300-400 GB/s in all against 585 GB/s to one), the epilogue stores
+# hold ~550-590 GB/s: so both are candidates, alone and mixed.
+_ALL = ("q", "k", "v", "o", "gate", "up", "down", "lm_head")
+PLANS = [
+    {},
+    {"lm_head": "ce"}, {"lm_head": "ring"}, {"lm_head": "p2p"},
+    {"lm_head": "ring", "gate": "ring", "up": "ring"},
+    {"lm_head": "ce", "gate": "ce", "up": "ce"}, {"lm_head": "p2p", "gate": "ce", "up": "ce"},
+    {"lm_head": "p2p", "gate": "p2p", "up": "p2p"},
+    {"lm_head": "ce", "gate": "ce", "up": "ce", "down": "ce"}, {"lm_head": "p2p", "down": "p2p"},
+    {"lm_head": "ce", "gate": "ce", "up": "ce", "down": "ce", "q": "ce", "o": "ce"},
+    {n: "ce" for n in _ALL}, {n: "p2p" for n in _ALL},
+]
+
+
+def plan_name(plan):
+    return "+".join(f"{n}:{m}" for n, m in plan.items()) or "none"
 
 
 def run(args):
@@ -894,27 +937,51 @@ def run(args):
     if world > 1:
         from macuda_b200.dist import (CopyEngineShardedGemm, CopyStreams, FusedShardedGemm, ReplicatedGemm,
                                       ShardedGemm, pick_fastest, step_barrier)
-        if exchange == "ce":
+        if exchange in ("auto", "ce"):
             copies = CopyStreams(world)
+            ring = CopyStreams(world, lanes=1)
+            plans = [pl for pl in PLANS if exchange == "auto" or all(v in ("ce", "ring") for v in pl.values())]
+            if args.shard == "sharded":
+                plans = [{n: ("ce" if exchange == "ce" else "p2p") for n in names}]
+            elif args.shard == "whole":
+                plans = [{}]
+            used = {m for pl in plans for m in pl.values()}
             ce = [CopyEngineShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype, copies)
-                  for L in layers]
+                  if used & {"ce", "ring"} else None for L in layers]
+            pp = [FusedShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype, exchange="p2p")
+                  if "p2p" in used else None for L in layers]
             whole = [ReplicatedGemm(lib, h, L["m"], TOKENS, L["k"], L["w_full"], ctype) for L in layers]
 
-            def plan_step(sharded):
-                for i in [i for i in range(len(layers)) if names[i] in sharded] + \
-                         [i for i in range(len(layers)) if names[i] not in sharded]:
-                    g = ce[i] if names[i] in sharded else whole[i]
+            def plan_order(plan):
+                """copy-engine shards first (their copies overlap what follows), then epilogue shards, then whole"""
+                rank_of = {"ce": 0, "ring": 0, "p2p": 1}
+                return sorted(range(len(layers)), key=lambda i: (rank_of.get(plan.get(names[i]), 2), i))
+
+            def runner_of(plan, i):
+                mode = plan.get(names[i])
+                return ce[i] if mode in ("ce", "ring") else pp[i] if mode == "p2p" else whole[i]
+
+            def copies_of(plan):
+                return ring if "ring" in plan.values() else copies
+
+            def plan_step(plan):
+                cs = copies_of(plan)
+                for i in plan_order(plan):
+                    g = runner_of(plan, i)
+                    if g is ce[i]:
+                        g.copies = cs
                     if g.run(acts[layers[i]["src"]], stream) != 0:
                         raise RuntimeError(f"{names[i]}: GEMM failed")
-                if sharded:
-                    copies.join(stream)
+                if set(plan.values()) & {"ce", "ring"}:
+                    cs.join(stream)
+                if plan:
                     step_barrier(stream)
 
-            if args.shard == "auto":
+            if len(plans) > 1:
                 # every candidate plan timed as a whole step on every rank (max over ranks), the fastest kept: the
                 # same choice everywhere
-                times = torch.zeros(len(CE_PLANS), dtype=torch.float64, device="cuda")
-                for pi, plan in enumerate(CE_PLANS):
+                times = torch.zeros(len(plans), dtype=torch.float64, device="cuda")
+                for pi, plan in enumerate(plans):
                     for _ in range(3):
                         plan_step(plan)
                     torch.cuda.synchronize()
@@ -928,20 +995,27 @@ def run(args):
                     times[pi] = e0.elapsed_time(e1) / 10
                     dist.barrier()
                 dist.all_reduce(times, op=dist.ReduceOp.MAX)
-                sharded_set = CE_PLANS[int(torch.argmin(times).item())]
-                plan_times = {"+".join(p) or "none": round(float(t), 4) for p, t in zip(CE_PLANS, times.tolist())}
+                plan = plans[int(torch.argmin(times).item())]
+                plan_times = {plan_name(pl): round(float(t), 4) for pl, t in zip(plans, times.tolist())}
             else:
-                sharded_set = tuple(names) if args.shard == "sharded" else ()
-                plan_times = None
+                plan, plan_times = plans[0], None
             for i in range(len(layers)):
-                keep, drop = (ce[i], whole[i]) if names[i] in sharded_set else (whole[i], ce[i])
-                drop.close()
+                keep = runner_of(plan, i)
+                for g in (ce[i], pp[i], whole[i]):
+                    if g is not None and g is not keep:
+                        g.close()
                 runners[i] = keep
-            order = [i for i in range(len(layers)) if names[i] in sharded_set] + \
-                    [i for i in range(len(layers)) if names[i] not in sharded_set]
-            if sharded_set:
+            order = plan_order(plan)
+            sharded_set = tuple(n for n in names if n in plan)
+            plan_modes = dict(plan)
+            copies = copies_of(plan)
+            for i in range(len(layers)):
+                if runners[i] is ce[i]:
+                    runners[i].copies = copies
+            if plan:
                 def finish():
-                    copies.join(stream)
+                    if set(plan.values()) & {"ce", "ring"}:
+                        copies.join(stream)
                     step_barrier(stream)
         elif exchange in ("p2p", "multicast"):
             plan_times = None
@@ -957,6 +1031,7 @@ def run(args):
                         c.close()
                 runners[i] = cands[choice]
             sharded_set = tuple(n for n, g in zip(names, runners) if g.exchange != "replicated")
+            plan_modes = {n: exchange for n in sharded_set}
             if sharded_set:
                 def finish():
                     step_barrier(stream)  # every peer's stores into this rank's C have landed
@@ -965,11 +1040,12 @@ def run(args):
             comm = torch.cuda.Stream()
             runners = [ShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype) for L in layers]
             sharded_set = tuple(names)
+            plan_modes = {n: "allgather" for n in names}
 
             def finish():
                 stream.wait_stream(comm)
     else:
-        sharded_set, plan_times = (), None
+        sharded_set, plan_times, plan_modes = (), None, {}
     for L in layers:
         L.pop("w_full", None)  # whole weights stay only where a projection runs whole on every rank
 
@@ -1182,28 +1258,26 @@ def run(args):
                 cs.stop()
     sharded = None
     if world > 1 and args.impl == "ours" and not args.no_sharded_shapes:
-        sharded = sharded_figures(torch, lib, cb, h, stream, rank, world, copies or CopyStreams(world))
+        sharded = sharded_figures(torch, lib, cb, h, stream, rank, world, CopyStreams(world),
+                                  CopyStreams(world, lanes=1))
 
     for g in runners:
         if g is not None and hasattr(g, "close"):
             g.close()
     h.close()
     if rank == 0:
+        how = {"ce": "N-sharded, rows pushed to every peer at once by the copy engines",
+               "ring": "N-sharded, rows pushed by the copy engines to one peer after another (ring order)",
+               "p2p": "N-sharded, rows stored into every peer's C by the GEMM epilogue (P2P)",
+               "multicast": "N-sharded, rows stored through an NVLink multicast address by the GEMM epilogue",
+               "allgather": "N-sharded, C exchanged by NCCL all-gather + layout kernel"}
         if world == 1:
             par_note = "single GPU"
-        elif exchange == "ce":
-            par_note = f"x{world}: " + ", ".join(
-                f"{n} " + ("N-sharded, rows pushed to every peer by the copy engines" if n in sharded_set
-                           else "whole on every rank") for n in (names[i] for i in order)) + \
-                ("; sharded projections run first so their copies overlap the rest; one NCCL barrier per step"
-                 if sharded_set else "")
-        elif exchange in ("p2p", "multicast"):
-            par_note = f"x{world}: " + ", ".join(
-                f"{n} " + (("N-sharded, rows exchanged by " + ("NVLink multicast" if exchange == "multicast" else "P2P")
-                            + " stores from the GEMM epilogue") if n in sharded_set else "whole on every rank")
-                for n in names) + ("; one NCCL barrier per step" if sharded_set else "")
         else:
-            par_note = f"N-shard x{world}, C exchanged by NCCL all-gather + layout kernel"
+            par_note = f"x{world}: " + ", ".join(f"{names[i]} " + how.get(plan_modes.get(names[i]), "whole on every rank")
+                                                 for i in order)
+            if plan_modes:
+                par_note += "; copy-engine shards run first so their copies overlap the rest; one NCCL barrier per step"
         line = {
             "metric": "GEMM TFLOP/s (Llama-3.1-8B prefill projection set, 512 tokens, %s -> f32, ggml's T,N call)"
                       % args.dtype,
@@ -1277,9 +1351,10 @@ def main():
     ap.add_argument("--shard", choices=["auto", "sharded", "whole"], default="auto",
                     help="N > 1: which projections are N-sharded (the rest run whole on every rank); auto: the fastest "
                          "plan, timed on every rank at set-up")
-    ap.add_argument("--exchange", choices=["ce", "fused", "multicast", "p2p", "allgather"], default="ce",
-                    help="N > 1: how the sharded C is replicated (ce = copy engines pushing each rank's rows to its "
-                         "peers; fused = p2p = stores from the GEMM epilogue)")
+    ap.add_argument("--exchange", choices=["auto", "ce", "fused", "multicast", "p2p", "allgather"], default="auto",
+                    help="N > 1: how the sharded C is replicated (auto = the fastest plan of copy-engine and epilogue "
+                         "shards, timed at set-up; ce = copy-engine plans only; fused = p2p = per projection, epilogue "
+                         "stores or whole)")
     ap.add_argument("--no-sharded-shapes", action="store_true",
                     help="N > 1: skip the per-shape sharded figures (squares, lm_head, FFN, configs 3 and 5)")
     args = ap.parse_args()

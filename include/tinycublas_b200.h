@@ -192,9 +192,10 @@ int tb200_skinny_shape(long long blocks, int k, int num_sms, int *warps, int *un
  * the library until the process exits), so batchCount is limited to tb200_noalloc_max_batch() (1024):
  * larger batches return CUBLAS_STATUS_INVALID_VALUE with a message on stderr.
  * The first call on a device looks up that array's device address (cudaGetSymbolAddress): make it before
- * any stream capture. All calls share the array and it keeps the last call's contents (each call clears the
- * flag that must start at zero and rewrites the tensor maps it uses): calls whose launches overlap on the GPU
- * - on different streams, or from different threads - race on it; serialise them. */
+ * any stream capture. All calls share the array and it keeps the last call's contents (each call rewrites the
+ * tensor maps it uses and compares the fallback flag with its own call number, so nothing needs clearing):
+ * calls whose launches overlap on the GPU - on different streams, or from different threads - race on it;
+ * serialise them. */
 cublasStatus_t tb200_gemm_batched_ex_noalloc(cublasHandle_t handle, cublasOperation_t transa,
                                              cublasOperation_t transb, int m, int n, int k, const void *alpha,
                                              const void *const Aarray[], cudaDataType Atype, int lda,
@@ -265,8 +266,9 @@ cublasStatus_t tb200_ipc_free(void *ptr);
 /* The exchange step of a sharded GEMM on the copy engines (no counterpart in the reference, which is
  * single-GPU): copies this rank's block of C - rows [row0, row0 + rows) of columns [col0, col0 + ncols) of
  * replicas[self] (elem_bytes per element, leading dimension ldc, column-major) - into the same place of every
- * other replica (peers' C mapped with tb200_ipc_open), one cudaMemcpy2DAsync per peer, peer q's on
- * streams[q % nstreams]. No kernel and no SM time: the copies overlap the GEMMs that run meanwhile on other
+ * other replica (peers' C mapped with tb200_ipc_open), one cudaMemcpy2DAsync per peer, issued in ring order
+ * from self + 1, peer q's on streams[q % nstreams] (nstreams = 1: one after another, every rank sending to a
+ * different peer at each moment). No kernel and no SM time: the copies overlap the GEMMs that run meanwhile on other
  * streams. The caller orders the copies after the GEMM that wrote the block (an event), and every rank's
  * reads of its C after all peers' copies (a collective after the copies' streams). A contiguous batch slab
  * is the case ldc = rows = the slab's length, ncols = 1. */

@@ -178,8 +178,10 @@ extern "C" __attribute__((visibility("default"))) cublasStatus_t tb200_push_bloc
   const size_t pitch = (size_t)ldc * elem_bytes;
   const size_t off = (size_t)(row0 + col0 * ldc) * elem_bytes;
   const char *src = (const char *)replicas[self] + off;
-  for (int q = 0; q < P; ++q) {
-    if (q == self) continue;
+  // peers in ring order from self + 1: with one stream every rank sends to a different peer at each moment
+  // (no peer receives from all the others at once)
+  for (int s = 1; s < P; ++s) {
+    const int q = (self + s) % P;
     if (!replicas[q]) return CUBLAS_STATUS_INVALID_VALUE;
     cudaError_t e = cudaMemcpy2DAsync((char *)replicas[q] + off, pitch, src, pitch, (size_t)rows * elem_bytes,
                                       (size_t)ncols, cudaMemcpyDefault, streams[q % nstreams]);

@@ -87,12 +87,17 @@ __device__ __forceinline__ void simt_tile(const tb200_gemm_t &g, int b, int m0, 
 }
 
 // Grid-stride over the 64 x 64 output tiles of every batch element (a grid of a few CTAs per SM), so that
-// a launch that has nothing to do (run_if clear) costs a few microseconds whatever the problem size.
+// a launch that has nothing to do (run_if not raised for this call) costs a few microseconds whatever the
+// problem size.
 template <typename TI>
 __global__ void __launch_bounds__(SB_T) tb200_gemm_simt_kernel(const tb200_gemm_t g, int gx, int gy) {
   __shared__ float As[SB_K][SB_M + 4];
   __shared__ float Bs[SB_K][SB_N + 4];
-  if (g.run_if && *(volatile const int *)g.run_if == 0) return;  // the tensor-core launch did the work
+  // launched with programmatic stream serialization behind the kernels of this library: wait for the kernel
+  // before this one to complete before touching memory, then let the next one be scheduled
+  griddep_wait();
+  griddep_launch_dependents();
+  if (g.run_if && *(volatile const int *)g.run_if != g.run_if_gen) return;  // the tensor-core launch did the work
   const long long tiles_xy = (long long)gx * gy, total = tiles_xy * g.batch;
   for (long long t = blockIdx.x; t < total; t += gridDim.x) {
     const int b = (int)(t / tiles_xy);
@@ -107,14 +112,25 @@ extern "C" int tb200_launch_simt(const tb200_gemm_t *g, cudaStream_t s) {
   const long long gx = (g->m + SB_M - 1) / SB_M, gy = (g->n + SB_N - 1) / SB_N;
   if (gx > 0x7fffffffLL || gy > 0x7fffffffLL) return (int)cudaErrorInvalidConfiguration;
   const long long total = gx * gy * g->batch;
-  const long long cap = 8LL * tb200_num_sms();  // 8 resident CTAs of 256 threads per SM
+  // 8 resident CTAs of 256 threads per SM; a stand-by launch (run_if) usually has nothing to do, so one per SM
+  const long long cap = (g->run_if ? 1LL : 8LL) * tb200_num_sms();
   const unsigned grid = (unsigned)(total < cap ? total : cap);
   if (grid == 0) return 0;
   if (tb200_trace())
     fprintf(stderr, "[trace] launch tb200_gemm_simt grid=(%u,1,1) block=(%d,1,1) tiles=%lld m=%d n=%d k=%d in=%d out=%d\n",
             grid, SB_T, total, g->m, g->n, g->k, g->in_type, g->out_type);
-  if (g->in_type == TB200_F32) tb200_gemm_simt_kernel<float><<<grid, SB_T, 0, s>>>(*g, (int)gx, (int)gy);
-  else if (g->in_type == TB200_F16) tb200_gemm_simt_kernel<__half><<<grid, SB_T, 0, s>>>(*g, (int)gx, (int)gy);
-  else tb200_gemm_simt_kernel<__nv_bfloat16><<<grid, SB_T, 0, s>>>(*g, (int)gx, (int)gy);
-  return (int)cudaGetLastError();
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(SB_T, 1, 1);
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = tb200_pdl() ? 1 : 0;
+  cudaError_t e;
+  if (g->in_type == TB200_F32) e = cudaLaunchKernelEx(&cfg, tb200_gemm_simt_kernel<float>, *g, (int)gx, (int)gy);
+  else if (g->in_type == TB200_F16) e = cudaLaunchKernelEx(&cfg, tb200_gemm_simt_kernel<__half>, *g, (int)gx, (int)gy);
+  else e = cudaLaunchKernelEx(&cfg, tb200_gemm_simt_kernel<__nv_bfloat16>, *g, (int)gx, (int)gy);
+  return (int)e;
 }

@@ -82,10 +82,12 @@ struct TcParams {
   void *rep[8];
   float *mc;       // or of the multicast address of all ranks' f32 C (one store reaches every replica)
   // pointer-array batches: per batch element b, maps[2b] (A) and maps[2b+1] (B) in global memory, C from
-  // Carr[b]; the launch does nothing if *skip != 0 (some pointer unfit for TMA: the general kernel runs)
+  // Carr[b]; the launch does nothing if *skip == skip_gen (the prep kernel found a pointer unfit for TMA in this
+  // call, whose generation number that is: the general kernel runs)
   const CUtensorMap *maps;
   void *const *Carr;
   const int *skip;
+  int skip_gen;
   // grouped GEMM (MoE experts): when groups > 0, group g owns columns [grp_off[g], grp_off[g + 1]) of B and
   // of C (device offsets, read by the kernel and clamped to [0, n]) and is batch element g of A; its tiles
   // are numbered after those of groups 0 .. g-1, m-tile fastest
@@ -231,12 +233,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   int *g_off = (int *)((uint8_t *)bars + Cfg::BAR_BYTES);  // grouped GEMM: clamped column offsets ...
   int *g_pre = g_off + TC_MAX_GROUPS + 1;                  // ... and tile-count prefix
 
-  // uniform early exit, before any barrier or TMEM allocation: every thread of every CTA reads the same flag
-  // (written by the kernel before this one, so read only once that kernel has completed)
-  if (p.skip) {
-    griddep_wait();
-    if (*(volatile const int *)p.skip != 0) return;
-  }
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   constexpr int CSIZE = CG * KS;   // CTAs per tile, launched as one cluster
@@ -290,6 +286,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   griddep_wait();
   griddep_launch_dependents();
   long long total_tiles = p.total_tiles;
+  // pointer-array batch with some pointer unfit for TMA (the flag written by the prep kernel before this one, read
+  // once that kernel has completed): no tiles, every role falls through to the teardown, the general kernel
+  // launched behind this one computes the batch
+  if (p.skip && *(volatile const int *)p.skip == p.skip_gen) total_tiles = 0;
   if (p.groups > 0) {
     // the groups' columns, clamped so that no tile reaches outside B or C whatever the offsets hold, and the
     // prefix of their tile counts (the same in every CTA)
@@ -684,16 +684,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
 namespace {
 
 // One thread per batch element of a pointer-array GEMM: copies the template maps (built on the host with a
-// placeholder address) to maps[2b] / maps[2b+1], points them at Aarr[b] / Barr[b], and raises *bad when a
-// pointer is not 16-byte aligned (a TMA source must be) so that the tensor-core launch stands down.
+// placeholder address) to maps[2b] / maps[2b+1], points them at Aarr[b] / Barr[b], and writes the call's
+// generation number `gen` to *bad when a pointer is not 16-byte aligned (a TMA source must be) so that the
+// tensor-core launch stands down. The flag is never cleared: a later call compares it with its own number.
 __global__ void tb200_ptr_maps_kernel(const __grid_constant__ CUtensorMap tA, const __grid_constant__ CUtensorMap tB,
                                       const void *const *Aarr, const void *const *Barr, CUtensorMap *maps, int batch,
-                                      int *bad) {
+                                      int *bad, int gen) {
+  // launched with programmatic stream serialization: the pointer arrays may come from the kernel before; the
+  // tensor-core kernel behind this one may set up meanwhile (it reads the maps only after this grid completes)
+  griddep_wait();
+  griddep_launch_dependents();
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b >= batch) return;
   const void *a = Aarr[b];
   const void *bb = Barr[b];
-  if ((((uintptr_t)a) | ((uintptr_t)bb)) & 15) atomicOr(bad, 1);
+  if ((((uintptr_t)a) | ((uintptr_t)bb)) & 15) atomicExch(bad, gen);
   maps[2 * b] = tA;
   maps[2 * b + 1] = tB;
   tensormap_set_address(&maps[2 * b], a);
@@ -843,7 +848,12 @@ extern "C" int tb200_tc_ok(const tb200_gemm_t *g) {
   return 1;
 }
 
-// The shared launcher. ptr_ws != NULL: pointer-array batch, scratch laid out as [flag (256 B)][maps].
+// generation number of the last pointer-array launch of this process (read by the allocation-free entry point's
+// test hook)
+static int g_last_ptr_gen;
+
+// The shared launcher. ptr_ws != NULL: pointer-array batch, scratch laid out as [flag (256 B)][maps]; the flag
+// starts at zero when the scratch is made and is never cleared (see tb200_ptr_maps_kernel).
 static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_sms, void *ptr_ws, cudaStream_t s) {
   const bool f32in = g->in_type == TB200_F32;
   const int es = f32in ? 4 : 2;
@@ -918,13 +928,27 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
     p.maps = maps;
     p.Carr = g->Carr;
     p.skip = flag;
-    cudaError_t e = cudaMemsetAsync(flag, 0, sizeof(int), s);
-    if (e != cudaSuccess) return (int)e;
+    // this call's number (never 0, the value of a fresh, zeroed flag): a flag raised by an earlier call on the same
+    // scratch does not match it
+    static unsigned next_gen;
+    unsigned gen = __atomic_add_fetch(&next_gen, 1u, __ATOMIC_RELAXED) & 0x7fffffffu;
+    if (gen == 0) gen = __atomic_add_fetch(&next_gen, 1u, __ATOMIC_RELAXED) & 0x7fffffffu;
+    p.skip_gen = (int)gen;
+    g_last_ptr_gen = (int)gen;
+    cudaError_t e;
     const unsigned blocks = (unsigned)((g->batch + 127) / 128);
     if (tb200_trace())
       fprintf(stderr, "[trace] launch tb200_ptr_maps_kernel grid=(%u,1,1) block=(128,1,1) batch=%d\n", blocks, g->batch);
-    tb200_ptr_maps_kernel<<<blocks, 128, 0, s>>>(ta, tb, g->Aarr, g->Barr, maps, g->batch, flag);
-    e = cudaGetLastError();
+    cudaLaunchConfig_t pcfg = {};
+    cudaLaunchAttribute pat[1];
+    pat[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pat[0].val.programmaticStreamSerializationAllowed = 1;
+    pcfg.gridDim = dim3(blocks, 1, 1);
+    pcfg.blockDim = dim3(128, 1, 1);
+    pcfg.stream = s;
+    pcfg.attrs = pat;
+    pcfg.numAttrs = tb200_pdl() ? 1 : 0;
+    e = cudaLaunchKernelEx(&pcfg, tb200_ptr_maps_kernel, ta, tb, g->Aarr, g->Barr, maps, g->batch, flag, p.skip_gen);
     if (e != cudaSuccess) return (int)e;
   }
   // the TMA-store epilogue, where C is this GPU's own plain or strided C with beta == 0 and its base, leading
@@ -1014,6 +1038,7 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   // the general kernel behind it: it computes the batch only if some pointer was unfit for TMA
   tb200_gemm_t gf = *g;
   gf.run_if = p.skip;
+  gf.run_if_gen = p.skip_gen;
   return tb200_launch_simt(&gf, s);
 }
 
@@ -1050,9 +1075,10 @@ extern "C" __attribute__((visibility("default"))) int tb200_device_error(void) {
 // tb200_gemm_batched_ex_noalloc serves callers that must not have the library call cudaMalloc: their
 // scratch is this fixed array, part of the library's device image, so every GPU that loads the library
 // holds its 256 KB + 256 B until the process exits. It bounds the batch at TB200_NOALLOC_MAX_BATCH.
-// All calls, on every stream, share it and it keeps the last call's contents: the flag that must start
-// at zero is cleared by each call (an asynchronous memset on the call's stream), the maps are rewritten
-// for every element, and calls whose launches overlap on the GPU race on it.
+// All calls, on every stream, share it and it keeps the last call's contents: the flag starts at zero (the
+// array is zero when the library is loaded) and is never cleared - each call compares it with its own
+// generation number - the maps are rewritten for every element, and calls whose launches overlap on the GPU
+// race on it.
 #define TB200_NOALLOC_MAX_BATCH 1024
 static __device__ __align__(256) unsigned char g_tb200_noalloc_scratch[256 + TB200_NOALLOC_MAX_BATCH * 256];
 
@@ -1082,11 +1108,13 @@ static void *noalloc_scratch(void) {
 // Test hook: 1 when the last allocation-free call on the current device found some batch pointer unfit for
 // TMA (the general kernel then ran the batch), 0 when its tensor-core launch ran, -1 on error. Waits for the
 // device.
+static int g_noalloc_last_gen;  // generation number of the last allocation-free pointer-array launch
+
 extern "C" __attribute__((visibility("default"))) int tb200_noalloc_last_fallback(void) {
   int v = 0;
   if (cudaDeviceSynchronize() != cudaSuccess) return -1;
   if (cudaMemcpyFromSymbol(&v, g_tb200_noalloc_scratch, sizeof v) != cudaSuccess) return -1;
-  return v != 0 ? 1 : 0;
+  return g_noalloc_last_gen != 0 && v == g_noalloc_last_gen ? 1 : 0;
 }
 
 extern "C" __attribute__((visibility("default"))) int tb200_noalloc_max_batch(void) { return TB200_NOALLOC_MAX_BATCH; }
@@ -1096,5 +1124,7 @@ extern "C" int tb200_launch_tc_ptr_noalloc(const tb200_gemm_t *g, int tile_n, in
     return (int)cudaErrorInvalidValue;
   void *ws = noalloc_scratch();
   if (!ws) return (int)cudaErrorInvalidSymbol;
-  return tb200_launch_tc_ptr(g, tile_n, pair, num_sms, ws, s);
+  const int rc = tb200_launch_tc_ptr(g, tile_n, pair, num_sms, ws, s);
+  g_noalloc_last_gen = g_last_ptr_gen;
+  return rc;
 }

@@ -34,9 +34,11 @@ typedef struct {
   /* the same with one multicast address instead of replicas: every f32 store of the epilogue goes to the
    * multicast object of all ranks' C (NVSwitch fans it out); row offset row0 */
   void *mc;
-  /* the general kernel runs only if *run_if != 0 (NULL: always): the fallback launch behind a
-   * pointer-array tensor-core launch, taken when some batch pointer is not 16-byte aligned */
+  /* the general kernel runs only if *run_if == run_if_gen (run_if NULL: always): the fallback launch behind a
+   * pointer-array tensor-core launch, taken when some batch pointer is not 16-byte aligned (the prep kernel
+   * then writes the call's generation number into the flag, which is never cleared) */
   const int *run_if;
+  int run_if_gen;
   /* grouped GEMM (tensor-core kernel only): when groups > 0, group g multiplies batch element g of A (stride
    * sA) with columns [grp_off[g], grp_off[g + 1]) of B into the same columns of C; grp_off is a device array
    * of groups + 1 offsets read by the kernel (batch == groups, sB == sC == 0, n = all columns) */

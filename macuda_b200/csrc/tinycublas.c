@@ -95,8 +95,9 @@ static void *stream_slot(struct tb200_handle *h, struct tb200_ws *arr, size_t by
   return p;
 }
 
-/* the pointer-array tensor maps' scratch: at least 64 KB, grown when a larger batch comes */
-static void *handle_scratch(struct tb200_handle *h, size_t bytes) { return stream_slot(h, h->ws, bytes, 64u << 10, 0); }
+/* the pointer-array tensor maps' scratch: at least 64 KB, grown when a larger batch comes, zeroed when made (its
+ * fallback flag starts at zero and is never cleared) */
+static void *handle_scratch(struct tb200_handle *h, size_t bytes) { return stream_slot(h, h->ws, bytes, 64u << 10, 1); }
 
 /* the balanced decode kernel's workspace: one fixed 1 MB buffer per stream, zeroed once (its counters return to
  * zero at the end of every launch) */

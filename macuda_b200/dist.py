@@ -157,15 +157,19 @@ class IpcReplicas:
 
 
 class CopyStreams:
-    """One stream per rank of the group for the copy-engine exchange (peer q's copies go on stream q), and an
-    event per stream that `join` records and makes another stream wait on."""
+    """Streams for the copy-engine exchange, and an event per stream that `join` records and makes another
+    stream wait on. lanes = world (default): one stream per peer, every peer's copy at once; lanes = 1: one
+    stream, the copies one after another in ring order from this rank (each rank sends to a different peer
+    at each moment)."""
 
-    def __init__(self, world: int):
+    def __init__(self, world: int, lanes: int = None):
         import ctypes
 
         import torch
-        self.streams = [torch.cuda.Stream() for _ in range(world)]
-        self.array = (ctypes.c_void_p * world)(*[s.cuda_stream for s in self.streams])
+        lanes = world if lanes is None else max(1, min(lanes, world))
+        self.lanes = lanes
+        self.streams = [torch.cuda.Stream() for _ in range(lanes)]
+        self.array = (ctypes.c_void_p * lanes)(*[s.cuda_stream for s in self.streams])
         self.events = [torch.cuda.Event() for _ in range(world)]
         self.ready = torch.cuda.Event()
 
@@ -188,8 +192,8 @@ class CopyEngineShardedGemm:
     Rank r's GEMM writes its rows [first, first + rows) of C straight into its own full C (leading dimension
     m) and tb200_push_block copies that row block into every peer's C. `run` splits the columns into `chunks`
     GEMMs so that the copies of one chunk overlap the next chunk's math (1 = one GEMM, then the copies). The
-    copies go on `copies` (a CopyStreams shared by the step); `copies.join(stream)` and `step_barrier` then
-    complete the exchange."""
+    copies go on `copies` (a CopyStreams shared by the step; it may be replaced between steps); then
+    `copies.join(stream)` and `step_barrier` complete the exchange."""
 
     exchange = "ce"
 
@@ -224,7 +228,7 @@ class CopyEngineShardedGemm:
                 return st
             self.copies.after(stream)
             st = self.lib.lib.tb200_push_block(self.buf.array, self.world, self.rank, self.first, self.rows, col0, nc,
-                                               self.m, 4, self.copies.array, self.world)
+                                               self.m, 4, self.copies.array, self.copies.lanes)
             if st != 0:
                 return st
         return 0
@@ -271,7 +275,7 @@ class BatchShardedGemm:
         self.copies.after(stream)
         slab = self.m * self.n
         return self.lib.lib.tb200_push_block(self.buf.array, self.world, self.rank, self.b0 * slab, self.nb * slab, 0, 1,
-                                             self.batch * slab, 4, self.copies.array, self.world)
+                                             self.batch * slab, 4, self.copies.array, self.copies.lanes)
 
     def run(self, x=None, stream=None) -> int:
         return self.compute(stream) or self.push(stream)

@@ -84,9 +84,12 @@ def _worker(rank, world, port, mode, m, n, k, q):
             torch.cuda.synchronize()
             dist.barrier()
             st = 0
-            for chunks in (1, 3):  # the second pass, in three column chunks, overwrites the first in place
+            # the second pass, in three column chunks pushed one peer after another (ring order), overwrites the
+            # first in place
+            for chunks, cs in ((1, copies), (3, CopyStreams(world, lanes=1))):
+                g.copies = cs
                 st = st or g.run(x, stream, chunks=chunks)
-                copies.join(stream)
+                cs.join(stream)
                 step_barrier(stream)
             torch.cuda.synchronize()
             C = g.c.cpu().numpy()
