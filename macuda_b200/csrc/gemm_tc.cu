@@ -6,17 +6,19 @@
 // (cuda-shim/libtinycublas/gemm.cu:241-415) and the first-cut tinyblas_gemm_f16_tc / f32_tc
 // (gemm.cu:61-221) for every aligned operand.
 //
-// Shape of one CTA (224 threads, one per SM, persistent over output tiles):
-//   warp 0      TMA producer of A, warp 6 TMA producer of B: one thread each streams its operand's k-blocks
+// Shape of one CTA (352 threads, one per SM, persistent over output tiles):
+//   warp 0      TMA producer of A, warp 2 TMA producer of B: one thread each streams its operand's k-blocks
 //               (128-byte rows, 128B swizzle) into a STAGES-deep shared-memory ring; the bytes complete
 //               full[s] by transaction count.
 //   warp 1      owns tensor memory (2 x BN columns: two accumulators); one thread issues tcgen05.mma for
 //               each k-block, then tcgen05.commit frees the smem stage (empty[s]); after a tile's last
 //               k-block a commit publishes the accumulator (tfull[a]).
-//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns at a time from the accumulator, apply alpha/beta,
-//               convert, store straight to column-major C (consecutive lanes hold consecutive rows, so every
-//               store instruction of a warp is contiguous), then release the accumulator (tempty[a]).
-// The two accumulators let the epilogue of tile i overlap the main loop of tile i+1.
+//   warps 3..10 epilogue, two groups of four (one warp per TMEM lane quadrant): tcgen05.ld 32 lanes x 32
+//               columns at a time from the accumulator, apply alpha/beta, convert, store to column-major C
+//               (staged TMA stores, or per lane: consecutive lanes hold consecutive rows), then release the
+//               accumulator (tempty[a]). Group g drains accumulator g, i.e. every other tile.
+// The two accumulators let the epilogue of tile i overlap the main loop of tile i+1, and the two epilogue groups
+// let the drains of consecutive tiles overlap each other (output-bound GEMMs).
 //
 // Tiles: 128 x BN on one CTA (BN 32..256), or 256 x BN (BN 128 or 256) on a cluster of two CTAs with
 // tcgen05.mma.cta_group::2 (each CTA loads its 128 rows of A and half of B's BN columns; the even CTA's
@@ -53,7 +55,11 @@ __device__ int g_tb200_err;  // error word: 1 = a pipeline wait gave up
 namespace {
 
 constexpr int TC_BM = 128;
-constexpr int TC_THREADS = 224;  // 7 warps: A loads, MMA, 4 x epilogue, B loads
+// 11 warps: the A producer (warp 0), the MMA issuer (1), the B producer (2), and two epilogue groups of four
+// warps (3-6 and 7-10), each warp on TMEM lane quadrant warp % 4. 352 threads leave 186 registers a thread.
+constexpr int TC_THREADS = 352;
+constexpr int TC_EPI_WARP0 = 3;  // first epilogue warp
+constexpr int TC_EPI_WARPS = 8;
 // wait budgets in SM cycles (about 2 s and 0.2 s at 2 GHz): far beyond any legitimate wait
 constexpr uint64_t WAIT_BUDGET_CYC = 4000000000ull;
 constexpr uint64_t DRAIN_BUDGET_CYC = 400000000ull;
@@ -122,10 +128,13 @@ struct TcCfg {
   static constexpr int STAGES_RAW = 196608 / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int TMEM_COLS = 2 * BN < 32 ? 32 : 2 * BN;
-  static constexpr int STG_BYTES = 4 * 4096;  // epilogue staging: 32 x 32 f32 per epilogue warp
+  // epilogue staging, 32 x 32 f32 per epilogue warp; a grouped GEMM (which never stages: no TMA stores) keeps its
+  // column offsets and tile-count prefix there instead
+  static constexpr int STG_BYTES = TC_EPI_WARPS * 4096;
+  static constexpr int GRP_BYTES = 2 * 4 * (TC_MAX_GROUPS + 1);
+  static_assert(GRP_BYTES <= STG_BYTES, "the grouped GEMM's tables live in the staging area");
   static constexpr int BAR_BYTES = 256;
-  static constexpr int GRP_BYTES = 2 * 4 * (TC_MAX_GROUPS + 1);  // grouped GEMM: column offsets + tile prefix
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES + GRP_BYTES;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * STAGE_BYTES + STG_BYTES + BAR_BYTES;
 };
 
 
@@ -230,8 +239,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   uint64_t *xfull = drain + 1;  // KS = 2: the k-split peer has parked its partial sums of this CTA's columns
   uint32_t *tmem_slot = (uint32_t *)(drain + 2);
   volatile int *abort_flag = (volatile int *)(tmem_slot + 1);
-  int *g_off = (int *)((uint8_t *)bars + Cfg::BAR_BYTES);  // grouped GEMM: clamped column offsets ...
-  int *g_pre = g_off + TC_MAX_GROUPS + 1;                  // ... and tile-count prefix
+  int *g_off = (int *)stg_all;             // grouped GEMM: clamped column offsets ...
+  int *g_pre = g_off + TC_MAX_GROUPS + 1;  // ... and tile-count prefix
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -259,7 +268,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       mbar_init(&tempty[a], 4 * CG);  // every epilogue warp of the tile
     }
     mbar_init(drain, 1);
-    mbar_init(xfull, 128);  // every epilogue thread of the k-split peer
+    mbar_init(xfull, 32 * TC_EPI_WARPS);  // every epilogue thread of the k-split peer
     *abort_flag = 0;
     fence_mbar_init();
     prefetch_tmap(&tmA);
@@ -319,7 +328,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   const uint32_t lead_tempty0 = CG == 2 ? mapa_shared(smem_u32(tempty), pair_even) : 0u;
 
   constexpr int NG = KC * BN / 4;  // tile::gather4 loads of B per stage (fused token gather)
-  if (warp == 6 && CG == 1 && NG <= 32 && p.gidx != nullptr) {
+  if (warp == 2 && CG == 1 && NG <= 32 && p.gidx != nullptr) {
     // ------------------------------------------------------------------ B producer, fused token gather
     // Lane l < NG issues one gather4 a stage: k-chunk l / (BN / 4), B rows 4 (l % (BN / 4)) .. + 3 of the
     // tile, i.e. the tile's columns of B, each read from the source column its token id names (an id
@@ -370,8 +379,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       for (int q = 0; q < STAGES; ++q)
         if (issued & (1u << q)) (void)mbar_wait(&full[q], (issued_par >> q) & 1u, &no_abort, DRAIN_BUDGET_CYC);
     }
-  } else if (warp == 0 || warp == 6) {
-    // ------------------------------------------------------------------ TMA producers (A: warp 0, B: warp 6)
+  } else if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------------ TMA producers (A: warp 0, B: warp 2)
     if (lane == 0) {
       const bool is_a = warp == 0;
       const CUtensorMap *tm0 = is_a ? &tmA : &tmB;
@@ -487,18 +496,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       volatile int no_abort = 0;
       (void)mbar_wait(drain, 0, &no_abort, DRAIN_BUDGET_CYC);
     }
-  } else {
-    // ------------------------------------------------------------------ epilogue (warps 2..5)
+  } else if (warp >= TC_EPI_WARP0) {
+    // ------------------------------------------------------------------ epilogue (warps 3..10)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
+    const int egrp = (warp - TC_EPI_WARP0) >> 2;  // epilogue group: warps 3-6 and 7-10
     // 32-column chunks this CTA stores: all, or (k split) its half [c_lo, c_lo + HCH); the peer stores
     // [o_lo, o_lo + HCH)
     constexpr int HCH = KS == 2 ? BN / 64 : BN / 32;
     const int c_lo = (int)kslice * HCH;
     const int o_lo = HCH - c_lo;
-    int acc = 0;
+    // Without the k split the two groups take alternate tiles, group g draining accumulator g, so that one
+    // group's stores overlap the other's. With it (one tile per cluster) both groups share the tile, each with
+    // half of the chunks (group 0 all of them when there is one).
+    const int g_lo = KS == 2 && HCH >= 2 ? egrp * (HCH / 2) : 0;
+    const int g_n = KS == 2 ? (HCH >= 2 ? HCH / 2 : (egrp == 0 ? HCH : 0)) : HCH;
+    const int acc = KS == 2 ? 0 : egrp;
     uint32_t aph = 0, xph = 0;
     const int osz = p.out_type == 0 ? 4 : 2;
-    for (long long t = t_first; t < total_tiles; t += t_step) {
+    const long long t_step_g = KS == 2 ? t_step : 2 * t_step;
+    for (long long t = t_first + (KS == 2 ? 0 : egrp * t_step); t < total_tiles; t += t_step_g) {
       const TileCoord tc = tile_coord<BN>(p, t, g_off, g_pre);
       const int b = tc.b, mt = tc.mt;
       // one lane waits, the warp follows its verdict: tcgen05.ld below needs the whole warp converged
@@ -509,36 +525,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       tc_fence_after();
       // TMEM address of 32-column chunk c of this warp's lane quadrant in the current accumulator
       const uint32_t t_chunk0 = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
-      // Chunks go through two register sets: the load of chunk c + 1 is issued before chunk c is stored, so
-      // its latency hides behind the stores (tcgen05.wait::ld then waits only for what is left of it).
-      uint32_t ra[32], rb[32];
+      uint32_t ra[32];
       if (KS == 2) {
-        // park the partial sums of the peer's columns, announce them, wait for the peer's of this CTA's own
+        // park the partial sums of the peer's columns (this group's share of them), announce them, wait for the
+        // peer's of this CTA's own
         float4 *park = (float4 *)smem;  // [chunk][4 columns][quadrant][lane]: a warp's stores are contiguous
-        tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)(o_lo * 32), ra);
-        tmem_ld_wait_regs(ra);
 #pragma unroll 1
-        for (int c = 0; c < HCH; ++c) {
-          const bool more = c + 1 < HCH;
-          if (more) tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)((o_lo + c + 1) * 32), rb);
+        for (int c = g_lo; c < g_lo + g_n; ++c) {
+          tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)((o_lo + c) * 32), ra);
+          tmem_ld_wait_regs(ra);
 #pragma unroll
           for (int q = 0; q < 8; ++q)
             park[((c * 8 + q) * 4 + quad) * 32 + lane] =
                 make_float4(__uint_as_float(ra[4 * q]), __uint_as_float(ra[4 * q + 1]), __uint_as_float(ra[4 * q + 2]),
                             __uint_as_float(ra[4 * q + 3]));
-          if (more) {
-            tmem_ld_wait_regs(rb);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) ra[j] = rb[j];
-          }
         }
         mbar_arrive_cluster(mapa_shared(smem_u32(xfull), xpeer));  // every thread releases its own stores
-        int parked = 0;
-        if (lane == 0) parked = mbar_wait_cluster(xfull, xph, abort_flag, p.wait_budget) ? 1 : 0;
-        parked = __shfl_sync(0xffffffffu, parked, 0);
-        __syncwarp();  // lane 0's acquire orders the peer's parked sums before every lane's reads
-        xph ^= 1u;
-        if (!parked) break;
+        if (g_n > 0) {
+          int parked = 0;
+          if (lane == 0) parked = mbar_wait_cluster(xfull, xph, abort_flag, p.wait_budget) ? 1 : 0;
+          parked = __shfl_sync(0xffffffffu, parked, 0);
+          __syncwarp();  // lane 0's acquire orders the peer's parked sums before every lane's reads
+          xph ^= 1u;
+          if (!parked) break;
+        }
       }
       const int row = mt * (TC_BM * CG) + (int)rank * TC_BM + quad * 32 + lane;
       const int n0 = tc.n0;
@@ -564,7 +574,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           // columns outside C are clipped by the map. The previous chunk's store must have read the buffer.
           const int wrow = mt * (TC_BM * CG) + (int)rank * TC_BM + quad * 32;
           if (wrow < p.m && col0 < tc.n_end) {
-            uint8_t *stg = stg_all + quad * 4096;
+            uint8_t *stg = stg_all + (warp - TC_EPI_WARP0) * 4096;
             if (lane == 0) bulk_wait_read_all();
             __syncwarp();
             if (p.out_type == 0) {
@@ -640,32 +650,26 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       };
-      tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)(c_lo * 32), ra);
-      tmem_ld_wait_regs(ra);
 #pragma unroll 1
-      for (int c = c_lo; c < c_lo + HCH; ++c) {
-        const bool more = c + 1 < c_lo + HCH;
-        if (more) tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)((c + 1) * 32), rb);
+      for (int c = c_lo + g_lo; c < c_lo + g_lo + g_n; ++c) {
+        tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)(c * 32), ra);
+        tmem_ld_wait_regs(ra);
         store_chunk(ra, c);
-        if (more) {
-          tmem_ld_wait_regs(rb);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) ra[j] = rb[j];
-        }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) {
+      // the accumulator is free again once its group's four warps have read it (with the k split, one tile per
+      // cluster and nothing more to compute, group 0 alone signals)
+      if (lane == 0 && (KS == 1 || egrp == 0)) {
         if (CG == 1) mbar_arrive(&tempty[acc]);
         else mbar_arrive_cluster(lead_tempty0 + (uint32_t)(acc * 8));
       }
-      acc ^= 1;
-      if (acc == 0) aph ^= 1u;
+      aph ^= 1u;
     }
     if (p.c_tma && lane == 0) bulk_wait_all();  // the staged stores have completed before the CTA leaves
   }
 
-  if ((p.nrep > 0 || p.mc) && warp >= 2 && warp <= 5) __threadfence_system();  // peers' replicas: stores performed
+  if ((p.nrep > 0 || p.mc) && warp >= TC_EPI_WARP0) __threadfence_system();  // peers' replicas: stores performed
   tc_fence_before();
   __syncwarp();
   if (CL) cluster_sync();  // no CTA leaves while a peer may still read its memory or signal its barriers
