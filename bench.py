@@ -864,16 +864,17 @@ def run_single(args):
 
 # candidate plans at N > 1: which projections are N-sharded and how their rows reach the peers ("ce": the copy
 # engines push them after the GEMM, to every peer at once, overlapping the projections that follow; "ring": the
-# same pushes one peer after another in ring order; "p2p": the GEMM epilogue stores them into the peers' C over
-# NVLink); the others run whole on every rank. A plan uses one copy-engine mode. Each is timed as a whole step on
+# same pushes one peer after another in ring order; "ring2": two such rings at once; "p2p": the GEMM epilogue
+# stores them into the peers' C over NVLink); the others run whole on every rank. A plan uses one copy-engine
+# mode. Each is timed as a whole step on
 # every rank at set-up and the fastest kept. The copy engines win with one peer and lose with more (their
 # pushes to several peers at once ran at 300-400 GB/s in all against 585 GB/s to one), the epilogue stores
 # hold ~550-590 GB/s: so both are candidates, alone and mixed.
 _ALL = ("q", "k", "v", "o", "gate", "up", "down", "lm_head")
 PLANS = [
     {},
-    {"lm_head": "ce"}, {"lm_head": "ring"}, {"lm_head": "p2p"},
-    {"lm_head": "ring", "gate": "ring", "up": "ring"},
+    {"lm_head": "ce"}, {"lm_head": "ring"}, {"lm_head": "ring2"}, {"lm_head": "p2p"},
+    {"lm_head": "ring", "gate": "ring", "up": "ring"}, {"lm_head": "ring2", "gate": "ring2", "up": "ring2"},
     {"lm_head": "ce", "gate": "ce", "up": "ce"}, {"lm_head": "p2p", "gate": "ce", "up": "ce"},
     {"lm_head": "p2p", "gate": "p2p", "up": "p2p"},
     {"lm_head": "ce", "gate": "ce", "up": "ce", "down": "ce"}, {"lm_head": "p2p", "down": "p2p"},
@@ -939,30 +940,31 @@ def run(args):
                                       ShardedGemm, pick_fastest, step_barrier)
         if exchange in ("auto", "ce"):
             copies = CopyStreams(world)
-            ring = CopyStreams(world, lanes=1)
-            plans = [pl for pl in PLANS if exchange == "auto" or all(v in ("ce", "ring") for v in pl.values())]
+            lanes = {"ce": copies, "ring": CopyStreams(world, lanes=1), "ring2": CopyStreams(world, lanes=2)}
+            plans = [pl for pl in PLANS if exchange == "auto" or all(v in lanes for v in pl.values())]
             if args.shard == "sharded":
                 plans = [{n: ("ce" if exchange == "ce" else "p2p") for n in names}]
             elif args.shard == "whole":
                 plans = [{}]
             used = {m for pl in plans for m in pl.values()}
             ce = [CopyEngineShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype, copies)
-                  if used & {"ce", "ring"} else None for L in layers]
+                  if used & set(lanes) else None for L in layers]
             pp = [FusedShardedGemm(lib, h, L["m"], TOKENS, L["k"], rank, world, L["w"], ctype, exchange="p2p")
                   if "p2p" in used else None for L in layers]
             whole = [ReplicatedGemm(lib, h, L["m"], TOKENS, L["k"], L["w_full"], ctype) for L in layers]
 
             def plan_order(plan):
                 """copy-engine shards first (their copies overlap what follows), then epilogue shards, then whole"""
-                rank_of = {"ce": 0, "ring": 0, "p2p": 1}
+                rank_of = {"ce": 0, "ring": 0, "ring2": 0, "p2p": 1}
                 return sorted(range(len(layers)), key=lambda i: (rank_of.get(plan.get(names[i]), 2), i))
 
             def runner_of(plan, i):
                 mode = plan.get(names[i])
-                return ce[i] if mode in ("ce", "ring") else pp[i] if mode == "p2p" else whole[i]
+                return ce[i] if mode in lanes else pp[i] if mode == "p2p" else whole[i]
 
             def copies_of(plan):
-                return ring if "ring" in plan.values() else copies
+                modes = [m for m in plan.values() if m in lanes]
+                return lanes[modes[0]] if modes else copies
 
             def plan_step(plan):
                 cs = copies_of(plan)
@@ -972,7 +974,7 @@ def run(args):
                         g.copies = cs
                     if g.run(acts[layers[i]["src"]], stream) != 0:
                         raise RuntimeError(f"{names[i]}: GEMM failed")
-                if set(plan.values()) & {"ce", "ring"}:
+                if set(plan.values()) & set(lanes):
                     cs.join(stream)
                 if plan:
                     step_barrier(stream)
@@ -1014,7 +1016,7 @@ def run(args):
                     runners[i].copies = copies
             if plan:
                 def finish():
-                    if set(plan.values()) & {"ce", "ring"}:
+                    if set(plan.values()) & set(lanes):
                         copies.join(stream)
                     step_barrier(stream)
         elif exchange in ("p2p", "multicast"):
@@ -1268,6 +1270,7 @@ def run(args):
     if rank == 0:
         how = {"ce": "N-sharded, rows pushed to every peer at once by the copy engines",
                "ring": "N-sharded, rows pushed by the copy engines to one peer after another (ring order)",
+               "ring2": "N-sharded, rows pushed by the copy engines along two rings of peers at once",
                "p2p": "N-sharded, rows stored into every peer's C by the GEMM epilogue (P2P)",
                "multicast": "N-sharded, rows stored through an NVLink multicast address by the GEMM epilogue",
                "allgather": "N-sharded, C exchanged by NCCL all-gather + layout kernel"}

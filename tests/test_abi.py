@@ -300,3 +300,27 @@ def test_grouped_gemm_argument_rules(lib):
         assert call(Btype=cb.CUDA_R_16BF) == cb.CUBLAS_STATUS_NOT_SUPPORTED  # A and B types differ
         assert call(Atype=cb.CUDA_R_32F, Btype=cb.CUDA_R_32F) == cb.CUBLAS_STATUS_NOT_SUPPORTED  # exact fp32
         assert call(groups=0) == cb.CUBLAS_STATUS_SUCCESS and call(n_total=0) == cb.CUBLAS_STATUS_SUCCESS
+
+
+def test_push_block_argument_rules(lib):
+    """tb200_push_block (the copy-engine exchange) refuses bad arguments before any copy is issued, and does
+    nothing for an empty block or a single rank."""
+    import ctypes
+    P = 4
+    reps = (ctypes.c_void_p * P)(256, 512, 768, 1024)
+    streams = (ctypes.c_void_p * P)(None, None, None, None)
+    push = lib.lib.tb200_push_block
+    inval = cb.CUBLAS_STATUS_INVALID_VALUE
+    assert push(None, P, 0, 0, 16, 0, 8, 64, 4, streams, P) == inval          # no replica list
+    assert push(reps, 0, 0, 0, 16, 0, 8, 64, 4, streams, P) == inval          # no ranks
+    assert push(reps, P, P, 0, 16, 0, 8, 64, 4, streams, P) == inval          # self outside the group
+    assert push(reps, P, 0, 60, 16, 0, 8, 64, 4, streams, P) == inval         # rows past the leading dimension
+    assert push(reps, P, 0, -1, 16, 0, 8, 64, 4, streams, P) == inval
+    assert push(reps, P, 0, 0, 16, -1, 8, 64, 4, streams, P) == inval
+    assert push(reps, P, 0, 0, 16, 0, 8, 64, 8, streams, P) == inval          # element size 2 or 4 only
+    assert push(reps, P, 0, 0, 16, 0, 8, 64, 4, None, P) == inval             # no streams
+    assert push(reps, P, 0, 0, 16, 0, 8, 64, 4, streams, 0) == inval
+    ok = cb.CUBLAS_STATUS_SUCCESS
+    assert push(reps, P, 0, 0, 0, 0, 8, 64, 4, streams, P) == ok              # empty block: nothing to copy
+    assert push(reps, P, 0, 0, 16, 0, 0, 64, 4, streams, P) == ok
+    assert push(reps, 1, 0, 0, 16, 0, 8, 64, 4, streams, 1) == ok             # one rank: no peer
