@@ -43,7 +43,9 @@ cublasStatus_t cublasCreate_v2(cublasHandle_t *handle);
  * the streams that used it). */
 cublasStatus_t cublasDestroy_v2(cublasHandle_t handle);
 
-/* replaces cublas.c:248. NULL selects the legacy default stream. */
+/* replaces cublas.c:248. NULL selects the legacy default stream. Outside a stream capture, the first selection of
+ * a stream also makes its pointer-array scratch (64 KB, for batches up to 255 elements), so that such a batch
+ * captured later on that stream runs on the tensor cores. */
 cublasStatus_t cublasSetStream_v2(cublasHandle_t handle, cudaStream_t stream);
 
 /* replaces cublas.c:249. Unlike the reference (which stores and ignores it), the mode is honoured:
@@ -214,8 +216,9 @@ int tb200_noalloc_last_fallback(void);
 
 /* Device scratch allocations this handle has made so far (test hook, the counterpart of the reference's
  * tinycublas_splitk_ws_allocs, cublas.c:91-92). The library allocates scratch only for pointer-array
- * batches on the tensor cores: one buffer per (handle, stream), made at the first such call on that
- * stream outside stream capture and grown when needed; Destroy frees it. */
+ * batches on the tensor cores (and for the opt-in balanced decode kernel): one buffer per (handle, stream),
+ * made when cublasSetStream selects the stream or at the first such call on it, outside stream capture, and
+ * grown when needed; a replaced buffer is kept until Destroy, which frees them all. */
 unsigned tb200_scratch_allocs(cublasHandle_t handle);
 
 /* Last error a kernel of this library recorded on the current device (0 = none): a bounded wait in

@@ -48,7 +48,23 @@ struct tb200_handle {
   struct tb200_ws ws[TB200_WS_SLOTS];
   struct tb200_ws dws[TB200_WS_SLOTS]; /* the balanced decode kernel's workspace, per stream */
   unsigned ws_allocs; /* allocations made, for the tests */
+  /* buffers replaced by a larger one or given up by a stream: launches already queued may still read them, so
+   * they are freed at cublasDestroy (after every stream drains), not on the GEMM path */
+  struct tb200_ws retired[32];
+  int n_retired;
 };
+
+/* keeps a replaced buffer until cublasDestroy; with the list full, waits for its stream and frees it now */
+static void retire(struct tb200_handle *h, struct tb200_ws *w) {
+  if (h->n_retired < (int)(sizeof h->retired / sizeof h->retired[0])) {
+    h->retired[h->n_retired++] = *w;
+  } else {
+    cudaStreamSynchronize(w->stream);
+    cudaFree(w->ptr);
+  }
+  w->ptr = NULL;
+  w->bytes = 0;
+}
 
 /* scratch of at least `bytes` from one of the handle's per-stream slot arrays (`arr`) for its current stream, or
  * NULL (capturing, or out of memory: the caller then takes a path that needs none). zero: a new buffer is cleared
@@ -66,17 +82,10 @@ static void *stream_slot(struct tb200_handle *h, struct tb200_ws *arr, size_t by
   if (slot < 0) {
     for (int i = 0; i < TB200_WS_SLOTS && slot < 0; i++)
       if (!arr[i].ptr) slot = i;
-    if (slot < 0) { /* all slots taken by other streams: retire the first after its stream drains */
-      slot = 0;
-      cudaStreamSynchronize(arr[0].stream);
-    }
+    if (slot < 0) slot = 0; /* all slots taken by other streams: the first one's buffer is retired below */
   }
-  if (arr[slot].ptr) {
-    cudaStreamSynchronize(arr[slot].stream); /* growth: earlier launches on this stream may still read it */
-    cudaFree(arr[slot].ptr);
-    arr[slot].ptr = NULL;
-    arr[slot].bytes = 0;
-  }
+  /* growth, or a slot taken over: launches queued earlier may still read the old buffer */
+  if (arr[slot].ptr) retire(h, &arr[slot]);
   size_t want = bytes < min_bytes ? min_bytes : bytes;
   void *p = NULL;
   if (cudaMalloc(&p, want) != cudaSuccess) {
@@ -454,6 +463,10 @@ cublasStatus_t cublasDestroy_v2(cublasHandle_t handle) {
         cudaFree(h->dws[i].ptr);
       }
     }
+    for (int i = 0; i < h->n_retired; i++) {
+      cudaStreamSynchronize(h->retired[i].stream);
+      cudaFree(h->retired[i].ptr);
+    }
   }
   free(handle);
   return CUBLAS_STATUS_SUCCESS;
@@ -465,7 +478,12 @@ unsigned tb200_scratch_allocs(cublasHandle_t handle) {
 
 cublasStatus_t cublasSetStream_v2(cublasHandle_t handle, cudaStream_t stream) {
   if (!handle) return CUBLAS_STATUS_NOT_INITIALIZED;
-  ((struct tb200_handle *)handle)->stream = stream;
+  struct tb200_handle *h = (struct tb200_handle *)handle;
+  h->stream = stream;
+  /* the stream's pointer-array scratch (64 KB: batches up to 255 elements), made now when this call is outside a
+   * stream capture, so that such a batch captured later on this stream still runs on the tensor cores; nothing is
+   * made during a capture, and a failed allocation only leaves it to the first pointer-array call */
+  (void)handle_scratch(h, tb200_tc_ptr_ws_bytes(1));
   return CUBLAS_STATUS_SUCCESS;
 }
 

@@ -672,6 +672,43 @@ def test_graph_capture_pointer_arrays(lib):
     hh.close()
 
 
+def test_graph_capture_pointer_arrays_first_call(lib):
+    """cublasSetStream made the stream's pointer-array scratch outside the capture, so the first pointer-array
+    call on that stream can be inside one (a warm-up strided GEMM of the same tile sets the kernel's attributes)."""
+    import torch
+    from tests.helpers import storage as st_
+    rng = np.random.default_rng(137)
+    m, n, k, batch = 256, 64, 512, 6
+    A = st_(rng, m * k * batch, O.F16, 0.02)
+    B = st_(rng, k * n * batch, O.F16)
+    dA, dB = dev(A), dev(B)
+    dC = torch.zeros(m * n * batch, device="cuda")
+    tA = ptr_table([dA.data_ptr() + b * m * k * 2 for b in range(batch)])
+    tB = ptr_table([dB.data_ptr() + b * k * n * 2 for b in range(batch)])
+    tC = ptr_table([dC.data_ptr() + b * m * n * 4 for b in range(batch)])
+    s = torch.cuda.Stream()
+    hh = lib.handle()
+    hh.set_stream(s.cuda_stream)
+    assert lib.lib.tb200_scratch_allocs(hh.h) == 1, "cublasSetStream did not make the stream's scratch"
+    with torch.cuda.stream(s):
+        assert hh.gemm_strided_batched_ex(1, 0, m, n, k, 1.0, dA.data_ptr(), cb.CUDA_R_16F, k, m * k, dB.data_ptr(),
+                                          cb.CUDA_R_16F, k, k * n, 0.0, dC.data_ptr(), cb.CUDA_R_32F, m, m * n, batch) == 0
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        assert hh.gemm_batched_ex(1, 0, m, n, k, 1.0, tA.data_ptr(), cb.CUDA_R_16F, k, tB.data_ptr(), cb.CUDA_R_16F, k,
+                                  0.0, tC.data_ptr(), cb.CUDA_R_32F, m, batch) == 0
+    assert lib.lib.tb200_scratch_allocs(hh.h) == 1
+    dC.fill_(float("nan"))
+    g.replay()
+    torch.cuda.synchronize()
+    R, S = O.gemm(1, 0, m, n, k, 1.0, A, O.F16, k, B, O.F16, k, sA=m * k, sB=k * n, batch=batch)
+    got = O.extract(dC.cpu().numpy(), O.F32, m, n, m, sC=m * n, batch=batch)
+    assert_ok(O.check(got, R, S, O.F32), "pointer-array first call inside a capture")
+    del g
+    hh.close()
+
+
 def test_no_device_error_recorded(lib):
     assert lib.device_error() == 0
 
