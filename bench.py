@@ -1059,10 +1059,13 @@ def run(args):
             return runners[i].run(act, stream, comm)
         return runners[i].run(act, stream)
 
-    def step(src, marks=None):
+    def step(src, marks=None, before=None):
         """One step: every projection once, in `order` (the N-sharded ones first, so that their exchange
-        overlaps the rest), then the exchange's completion. marks: {i: (event, event)} recorded around GEMM i."""
+        overlaps the rest), then the exchange's completion. marks: {i: (event, event)} recorded around GEMM i;
+        before: {i: f} called just before GEMM i is enqueued."""
         for i in order:
+            if before is not None and i in before:
+                before[i]()
             if marks is not None and i in marks:
                 marks[i][0].record(stream)
             st = launch(i, src[layers[i]["src"]])
@@ -1161,13 +1164,15 @@ def run(args):
 
     # e2e through the public API with host buffers: each step copies its activations from pinned host
     # memory (double-buffered on a copy stream, overlapping the previous step) and reads back the last
-    # token's logits
+    # token's logits (on the copy stream, after lm_head; the next step's lm_head, which overwrites that C, waits
+    # for the read)
     hx = {"x": acts["x"].cpu().pin_memory(), "h": acts["h"].cpu().pin_memory()}
     dev_bufs = [{"x": torch.empty_like(acts["x"]), "h": torch.empty_like(acts["h"])} for _ in range(2)]
     logits = torch.empty(VOCAB, dtype=torch.float32).pin_memory()
     h2d = torch.cuda.Stream()
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
+    lm_done, read_done = torch.cuda.Event(), torch.cuda.Event()
     n_e2e = max(3, min(args.steps, 100))
 
     def c_of(i):
@@ -1181,10 +1186,19 @@ def run(args):
             dev_bufs[b]["h"].copy_(hx["h"], non_blocking=True)
             ready[b].record(h2d)
         stream.wait_event(ready[b])
-        step(dev_bufs[b])
+        after_lm = lambda: lm_done.record(stream)  # noqa: E731
+        nxt = order[order.index(dom) + 1] if order.index(dom) + 1 < len(order) else None
+        before = {dom: lambda: stream.wait_event(read_done)}  # the previous step's read of this C has finished
+        if nxt is not None:
+            before[nxt] = after_lm
+        step(dev_bufs[b], before=before)
+        if nxt is None:
+            after_lm()
         free[b].record(stream)
-        with torch.cuda.stream(stream):
+        with torch.cuda.stream(h2d):  # lm_head's C is complete after its GEMM (and, at N > 1, the barrier)
+            h2d.wait_event(lm_done if world == 1 else free[b])
             logits.copy_(c_of(dom)[(TOKENS - 1) * VOCAB:TOKENS * VOCAB], non_blocking=True)
+            read_done.record(h2d)
 
     for i in range(3):
         e2e_step(i)
@@ -1197,6 +1211,7 @@ def run(args):
     t_wall = time.perf_counter()
     for i in range(n_e2e):
         e2e_step(i)
+    stream.wait_event(read_done)  # the last step's logits are on the host inside the timed region
     f1.record(stream)
     torch.cuda.synchronize()
     t_wall = time.perf_counter() - t_wall
