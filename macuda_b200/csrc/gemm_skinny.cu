@@ -73,9 +73,26 @@ __global__ void __launch_bounds__(SK_WARPS * 32) tb200_gemm_skinny_kernel(const 
   __shared__ float part[SK_ROWS * 8];  // this CTA's k-slice sums, read by cluster rank 0 (S > 1)
   // launched with programmatic stream serialization: wait for the kernel before this one in the stream to
   // complete before touching memory, then let the next one be scheduled on SMs this grid leaves free
+  const int b = blockIdx.y + z0;
+  if (!g.Aarr) {
+    // this warp's first chunks of A into L2 while the kernel before this one may still be finishing (waited for
+    // below, before any load): prefetches only move lines into L2, the point of coherence, so the loads after
+    // griddep_wait still read what that kernel wrote
+    const int lane_ = threadIdx.x & 31, w_ = threadIdx.x >> 5;
+    const int sl = S > 1 ? (int)(blockIdx.x % (unsigned)S) : 0;
+    const int r = (int)(blockIdx.x / (unsigned)S) * SK_ROWS + (lane_ >> 1);
+    const int nch = g.k >> 5, c0 = (int)((long long)sl * nch / S), c1 = (int)((long long)(sl + 1) * nch / S);
+    if (r < g.m) {
+      const T *row = (const T *)g.A + (long long)b * g.sA + (long long)r * g.lda + (lane_ & 1) * 16;
+#pragma unroll
+      for (int u = 0; u < SK_UNROLL; ++u) {
+        const int j = c0 + w_ + u * SK_WARPS;
+        if (j < c1) prefetch_l2(row + (long long)j * 32);
+      }
+    }
+  }
   griddep_wait();
   griddep_launch_dependents();
-  const int b = blockIdx.y + z0;
   const T *A = g.Aarr ? (const T *)g.Aarr[b] : (const T *)g.A + (long long)b * g.sA;
   const T *B = g.Barr ? (const T *)g.Barr[b] : (const T *)g.B + (long long)b * g.sB;
   const int osz = g.out_type == 0 ? 4 : 2;
