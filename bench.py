@@ -144,6 +144,27 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": smax, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def bind_to_gpu_cpus(torch, dev):
+    """Run this process on the host CPUs local to GPU `dev` (its PCI device's local_cpulist in sysfs), so that the
+    pinned host buffers of the e2e leg sit on the GPU's NUMA node. Returns the CPU list, or None when unknown."""
+    try:
+        pr = torch.cuda.get_device_properties(dev)
+        bdf = "%04x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+        with open(f"/sys/bus/pci/devices/{bdf}/local_cpulist") as f:
+            text = f.read().strip()
+        cpus = set()
+        for part in text.split(","):
+            a, _, b = part.partition("-")
+            cpus.update(range(int(a), int(b or a) + 1))
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return text
+    except Exception:
+        pass
+    return None
+
+
 def make_inputs(torch, rank, world, dtype, seed=1234):
     """Weights (each projection's full matrix, the same on every rank, stored k x m: op T, lda = k; "w" is
     this rank's m/world rows of it) and activations."""
@@ -896,6 +917,8 @@ def run(args):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
+    all_cpus = os.sched_getaffinity(0)
+    host_cpus = bind_to_gpu_cpus(torch, local)
     if world > 1:
         from datetime import timedelta
         # NCCL's initialisation lines (communicator size, ranks, transports) go to stderr, so that the rank count
@@ -1163,13 +1186,13 @@ def run(args):
               for i in range(len(layers))}
 
     # e2e through the public API with host buffers: each step copies its activations from pinned host
-    # memory (double-buffered on a copy stream, overlapping the previous step) and reads back the last
-    # token's logits (on the copy stream, after lm_head; the next step's lm_head, which overwrites that C, waits
-    # for the read)
+    # memory (double-buffered on a host-to-device stream, overlapping the previous step) and reads back the
+    # last token's logits (on a stream of its own, after lm_head, so that the next step's activation copy does
+    # not queue behind it; the next step's lm_head, which overwrites that C, waits for the read)
     hx = {"x": acts["x"].cpu().pin_memory(), "h": acts["h"].cpu().pin_memory()}
     dev_bufs = [{"x": torch.empty_like(acts["x"]), "h": torch.empty_like(acts["h"])} for _ in range(2)]
     logits = torch.empty(VOCAB, dtype=torch.float32).pin_memory()
-    h2d = torch.cuda.Stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
     lm_done, read_done = torch.cuda.Event(), torch.cuda.Event()
@@ -1195,10 +1218,10 @@ def run(args):
         if nxt is None:
             after_lm()
         free[b].record(stream)
-        with torch.cuda.stream(h2d):  # lm_head's C is complete after its GEMM (and, at N > 1, the barrier)
-            h2d.wait_event(lm_done if world == 1 else free[b])
+        with torch.cuda.stream(d2h):  # lm_head's C is complete after its GEMM (and, at N > 1, the barrier)
+            d2h.wait_event(lm_done if world == 1 else free[b])
             logits.copy_(c_of(dom)[(TOKENS - 1) * VOCAB:TOKENS * VOCAB], non_blocking=True)
-            read_done.record(h2d)
+            read_done.record(d2h)
 
     for i in range(3):
         e2e_step(i)
@@ -1222,7 +1245,8 @@ def run(args):
         e2e_ms = float(t.item())
     e2e = {"value": round(STEP_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
            "h2d_bytes_per_step": int(hx["x"].numel() * 2 + hx["h"].numel() * 2), "d2h_bytes_per_step": VOCAB * 4,
-           "ms_per_step": round(e2e_ms, 4), "wall_ms_per_step": round(t_wall * 1e3 / n_e2e, 4), "steps": n_e2e}
+           "ms_per_step": round(e2e_ms, 4), "wall_ms_per_step": round(t_wall * 1e3 / n_e2e, 4), "steps": n_e2e,
+           "host_cpus": host_cpus}
 
     # parity of every projection's C as every rank holds it after the last step (each peer's rows included),
     # against fp64 on sampled rows
@@ -1252,6 +1276,7 @@ def run(args):
     cpu = None
     if rank == 0 and world == 1 and args.impl == "ours" and not args.no_cpu_baseline:
         try:
+            os.sched_setaffinity(0, all_cpus)  # the CPU baseline takes every host core it can
             cpu = run_cpu_baseline()
         except Exception as ex:  # the baseline is reported, never required
             cpu = {"error": str(ex)[:200]}

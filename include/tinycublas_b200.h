@@ -9,8 +9,9 @@
  *   C = alpha * op(A) * op(B) + beta * C, column-major, op(X) = X or X^T.
  *   A, B, C and pointer arrays are caller-owned DEVICE memory; alpha and beta are HOST pointers read
  *   in the compute type (half under CUBLAS_COMPUTE_16F*, float otherwise).
- *   Launches are asynchronous on the handle's stream. No entry point synchronises the host, reads
- *   device memory back, or allocates on the GEMM path, so every call can be captured in a CUDA graph.
+ *   Launches are asynchronous on the handle's stream. No entry point synchronises the host or reads
+ *   device memory back. Device scratch is made only outside stream capture, and only where
+ *   tb200_scratch_allocs says.
  *
  * Status codes:
  *   CUBLAS_STATUS_SUCCESS            launched (or nothing to do: m, n or batch is 0)

@@ -274,28 +274,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
     if (p.c_tma) prefetch_tmap(&tmC);
-    // The first stages of this CTA's first tile of A into L2, while the kernel before this one may still be
-    // finishing (it is waited for below, before any load): only prefetches, which move lines into L2 and nothing
-    // else, so every load after griddep_wait still reads what that kernel wrote. Plain and strided GEMMs only (a
-    // pointer-array element's maps are written by the kernel before this one; a grouped tile needs the offsets).
-    if (p.maps == nullptr && p.groups == 0 && t_first < p.total_tiles) {
-      const TileCoord tc = tile_coord<BN>(p, t_first, nullptr, nullptr);
-      const int mn0 = tc.mt * (TC_BM * CG) + (int)rank * TC_BM;
-      for (int q = 0; q < STAGES && kb_lo + q < kb_hi; ++q) {
-        const int k0 = (kb_lo + q) * p.bk;
-        if (!p.a_mn) {
-          for (int c = 0; c < KC; ++c) {
-            if (p.a_batched) tma_prefetch_3d(&tmA, k0 + c * p.epr, mn0, tc.b);
-            else tma_prefetch_2d(&tmA, k0 + c * p.epr, mn0);
-          }
-        } else {
-          for (int j = 0; j < TC_BM / p.epr; ++j) {
-            if (p.a_batched) tma_prefetch_3d(&tmA, mn0 + j * p.epr, k0, tc.b);
-            else tma_prefetch_2d(&tmA, mn0 + j * p.epr, k0);
-          }
-        }
-      }
-    }
   }
   if (warp == 1) {
     if (CG == 1) {

@@ -199,19 +199,8 @@ __device__ __forceinline__ void tma_load_3d_cg2(void *dst, const void *tmap, uin
       "l"((uint64_t)tmap), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
 }
-// L2 prefetch of a tile through a tensor map (no shared memory, no barrier): the box lands in L2 only. L2 is the
-// point of coherence for the SMs and the TMA, so a load issued later still sees writes that other kernels made
-// after the prefetch.
-__device__ __forceinline__ void tma_prefetch_2d(const void *tmap, int c0, int c1) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"((uint64_t)tmap), "r"(c0),
-               "r"(c1)
-               : "memory");
-}
-__device__ __forceinline__ void tma_prefetch_3d(const void *tmap, int c0, int c1, int c2) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"((uint64_t)tmap), "r"(c0),
-               "r"(c1), "r"(c2)
-               : "memory");
-}
+// L2 prefetch of the line holding p: the line lands in L2 only. L2 is the point of coherence for the SMs, so a
+// load issued later still sees writes that other kernels made after the prefetch.
 __device__ __forceinline__ void prefetch_l2(const void *p) {
   asm volatile("prefetch.global.L2 [%0];" ::"l"((uint64_t)p) : "memory");
 }
