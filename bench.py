@@ -885,16 +885,16 @@ def run_single(args):
 
 # candidate plans at N > 1: which projections are N-sharded and how their rows reach the peers ("ce": the copy
 # engines push them after the GEMM, to every peer at once, overlapping the projections that follow; "ring": the
-# same pushes one peer after another in ring order; "ring2": two such rings at once; "p2p": the GEMM epilogue
-# stores them into the peers' C over NVLink); the others run whole on every rank. A plan uses one copy-engine
-# mode. Each is timed as a whole step on
-# every rank at set-up and the fastest kept. The copy engines win with one peer and lose with more (their
-# pushes to several peers at once ran at 300-400 GB/s in all against 585 GB/s to one), the epilogue stores
-# hold ~550-590 GB/s: so both are candidates, alone and mixed.
+# same pushes one peer after another in ring order; "ring2": two such rings at once; "ring4": the ring, with the
+# GEMM in four column chunks whose pushes start as each is computed; "p2p": the GEMM epilogue stores them into the
+# peers' C over NVLink); the others run whole on every rank. A plan uses one copy-engine mode. Each is timed as a
+# whole step on every rank at set-up and the fastest kept. The copy engines win with one peer and lose with more
+# (their pushes to several peers at once ran at 300-400 GB/s in all against 585-677 GB/s to one; along a ring
+# 472-489 GB/s at P = 8), the epilogue stores hold ~550-590 GB/s: so both are candidates, alone and mixed.
 _ALL = ("q", "k", "v", "o", "gate", "up", "down", "lm_head")
 PLANS = [
     {},
-    {"lm_head": "ce"}, {"lm_head": "ring"}, {"lm_head": "ring2"}, {"lm_head": "p2p"},
+    {"lm_head": "ce"}, {"lm_head": "ring"}, {"lm_head": "ring2"}, {"lm_head": "ring4"}, {"lm_head": "p2p"},
     {"lm_head": "ring", "gate": "ring", "up": "ring"}, {"lm_head": "ring2", "gate": "ring2", "up": "ring2"},
     {"lm_head": "ce", "gate": "ce", "up": "ce"}, {"lm_head": "p2p", "gate": "ce", "up": "ce"},
     {"lm_head": "p2p", "gate": "p2p", "up": "p2p"},
@@ -958,12 +958,15 @@ def run(args):
     order = list(range(len(layers)))
     copies, comm = None, None
     finish = lambda: None  # noqa: E731  completes the step's exchange on the compute stream
+    finish_barrier = False  # whether finish() ends with a barrier of every rank
     if world > 1:
         from macuda_b200.dist import (CopyEngineShardedGemm, CopyStreams, FusedShardedGemm, ReplicatedGemm,
                                       ShardedGemm, pick_fastest, step_barrier)
         if exchange in ("auto", "ce"):
             copies = CopyStreams(world)
-            lanes = {"ce": copies, "ring": CopyStreams(world, lanes=1), "ring2": CopyStreams(world, lanes=2)}
+            ring1 = CopyStreams(world, lanes=1)
+            lanes = {"ce": copies, "ring": ring1, "ring2": CopyStreams(world, lanes=2), "ring4": ring1}
+            chunks_of = {"ring4": 4}  # column chunks of a copy-engine shard's GEMM (1 unless named here)
             plans = [pl for pl in PLANS if exchange == "auto" or all(v in lanes for v in pl.values())]
             if args.shard == "sharded":
                 plans = [{n: ("ce" if exchange == "ce" else "p2p") for n in names}]
@@ -978,7 +981,7 @@ def run(args):
 
             def plan_order(plan):
                 """copy-engine shards first (their copies overlap what follows), then epilogue shards, then whole"""
-                rank_of = {"ce": 0, "ring": 0, "ring2": 0, "p2p": 1}
+                rank_of = {"ce": 0, "ring": 0, "ring2": 0, "ring4": 0, "p2p": 1}
                 return sorted(range(len(layers)), key=lambda i: (rank_of.get(plan.get(names[i]), 2), i))
 
             def runner_of(plan, i):
@@ -995,6 +998,7 @@ def run(args):
                     g = runner_of(plan, i)
                     if g is ce[i]:
                         g.copies = cs
+                        g.chunks = chunks_of.get(plan[names[i]], 1)
                     if g.run(acts[layers[i]["src"]], stream) != 0:
                         raise RuntimeError(f"{names[i]}: GEMM failed")
                 if set(plan.values()) & set(lanes):
@@ -1037,7 +1041,10 @@ def run(args):
             for i in range(len(layers)):
                 if runners[i] is ce[i]:
                     runners[i].copies = copies
+                    runners[i].chunks = chunks_of.get(plan[names[i]], 1)
             if plan:
+                finish_barrier = True
+
                 def finish():
                     if set(plan.values()) & set(lanes):
                         copies.join(stream)
@@ -1058,6 +1065,8 @@ def run(args):
             sharded_set = tuple(n for n, g in zip(names, runners) if g.exchange != "replicated")
             plan_modes = {n: exchange for n in sharded_set}
             if sharded_set:
+                finish_barrier = True
+
                 def finish():
                     step_barrier(stream)  # every peer's stores into this rank's C have landed
         else:  # NCCL all-gather + layout kernel, every projection sharded
@@ -1082,10 +1091,10 @@ def run(args):
             return runners[i].run(act, stream, comm)
         return runners[i].run(act, stream)
 
-    def step(src, marks=None, before=None):
+    def step(src, marks=None, before=None, pre_finish=None):
         """One step: every projection once, in `order` (the N-sharded ones first, so that their exchange
         overlaps the rest), then the exchange's completion. marks: {i: (event, event)} recorded around GEMM i;
-        before: {i: f} called just before GEMM i is enqueued."""
+        before: {i: f} called just before GEMM i is enqueued; pre_finish: called before the completion."""
         for i in order:
             if before is not None and i in before:
                 before[i]()
@@ -1096,6 +1105,8 @@ def run(args):
                 marks[i][1].record(stream)
             if st != 0:
                 raise RuntimeError(f"{names[i]}: status {st}")
+        if pre_finish is not None:
+            pre_finish()
         finish()
 
     # Inside the timed region the only events are the two around the dominant GEMM (lm_head, the roofline
@@ -1187,43 +1198,97 @@ def run(args):
 
     # e2e through the public API with host buffers: each step copies its activations from pinned host
     # memory (double-buffered on a host-to-device stream, overlapping the previous step) and reads back the
-    # last token's logits (on a stream of its own, after lm_head, so that the next step's activation copy does
-    # not queue behind it; the next step's lm_head, which overwrites that C, waits for the read)
-    hx = {"x": acts["x"].cpu().pin_memory(), "h": acts["h"].cpu().pin_memory()}
-    dev_bufs = [{"x": torch.empty_like(acts["x"]), "h": torch.empty_like(acts["h"])} for _ in range(2)]
+    # last token's logits (on a stream of their own, after lm_head, so that the next step's activation copy does
+    # not queue behind it; the next step's lm_head, which overwrites that C, waits for the read). At N > 1 each
+    # rank copies 1/N of the packed activations over its own host link and the copy engines push that slice
+    # into every peer's buffer (CUDA IPC) while the step runs; the step's barrier, which waits for this rank's
+    # pushes, tells every rank that the next step's inputs are whole, and a buffer is refilled only after the
+    # barrier that follows its last reader.
     logits = torch.empty(VOCAB, dtype=torch.float32).pin_memory()
     h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
-    ready = [torch.cuda.Event() for _ in range(2)]
-    free = [torch.cuda.Event() for _ in range(2)]
     lm_done, read_done = torch.cuda.Event(), torch.cuda.Event()
     n_e2e = max(3, min(args.steps, 100))
 
     def c_of(i):
         return layers[i]["c_local"] if world == 1 else runners[i].c
 
+    nxt_of_dom = order[order.index(dom) + 1] if order.index(dom) + 1 < len(order) else None
+    e2e_ipc = []
+    if world == 1:
+        hx = {"x": acts["x"].cpu().pin_memory(), "h": acts["h"].cpu().pin_memory()}
+        dev_bufs = [{"x": torch.empty_like(acts["x"]), "h": torch.empty_like(acts["h"])} for _ in range(2)]
+        ready = [torch.cuda.Event() for _ in range(2)]
+        free = [torch.cuda.Event() for _ in range(2)]
+        h2d_bytes = int(hx["x"].numel() * 2 + hx["h"].numel() * 2)
+
+        def stage(b):
+            with torch.cuda.stream(h2d):
+                h2d.wait_event(free[b])
+                dev_bufs[b]["x"].copy_(hx["x"], non_blocking=True)
+                dev_bufs[b]["h"].copy_(hx["h"], non_blocking=True)
+                ready[b].record(h2d)
+    else:
+        from macuda_b200.dist import CopyStreams, IpcReplicas, _DeviceArray, step_barrier
+        nx, nh = acts["x"].numel(), acts["h"].numel()
+        esz = acts["x"].element_size()
+        chunk = -(-(nx + nh) // world)
+        packed = torch.zeros(world * chunk, dtype=acts["x"].dtype, device="cuda")
+        packed[:nx] = acts["x"].reshape(-1)
+        packed[nx:nx + nh] = acts["h"].reshape(-1)
+        hshard = packed[rank * chunk:(rank + 1) * chunk].cpu().pin_memory()
+        del packed
+        e2e_ipc = [IpcReplicas(lib, world * chunk * esz, rank, world) for _ in range(2)]
+        full = [torch.as_tensor(_DeviceArray(r.own, world * chunk, "<i2"), device="cuda").view(acts["x"].dtype)
+                for r in e2e_ipc]
+        dev_bufs = [{"x": f[:nx].view(acts["x"].shape), "h": f[nx:nx + nh].view(acts["h"].shape)} for f in full]
+        in_lanes = CopyStreams(world, lanes=1)
+        pushed = [torch.cuda.Event() for _ in range(2)]
+        bar_done = torch.cuda.Event()
+        bar_done.record(stream)
+        h2d_bytes = int(chunk * esz)
+
+        def stage(b):
+            with torch.cuda.stream(h2d):
+                h2d.wait_event(bar_done)  # every rank has passed the barrier after buffer b's last reader
+                full[b][rank * chunk:(rank + 1) * chunk].copy_(hshard, non_blocking=True)
+            in_lanes.after(h2d)
+            if lib.lib.tb200_push_block(e2e_ipc[b].array, world, rank, rank * chunk, chunk, 0, 1, world * chunk, esz,
+                                        in_lanes.array, in_lanes.lanes) != 0:
+                raise RuntimeError("tb200_push_block failed")
+            in_lanes.join(h2d)
+            pushed[b].record(h2d)
+
     def e2e_step(i):
         b = i % 2
-        with torch.cuda.stream(h2d):
-            h2d.wait_event(free[b])
-            dev_bufs[b]["x"].copy_(hx["x"], non_blocking=True)
-            dev_bufs[b]["h"].copy_(hx["h"], non_blocking=True)
-            ready[b].record(h2d)
-        stream.wait_event(ready[b])
+        if world == 1:
+            stage(b)
+            stream.wait_event(ready[b])
         after_lm = lambda: lm_done.record(stream)  # noqa: E731
-        nxt = order[order.index(dom) + 1] if order.index(dom) + 1 < len(order) else None
         before = {dom: lambda: stream.wait_event(read_done)}  # the previous step's read of this C has finished
-        if nxt is not None:
-            before[nxt] = after_lm
-        step(dev_bufs[b], before=before)
-        if nxt is None:
-            after_lm()
-        free[b].record(stream)
+        if nxt_of_dom is not None:
+            before[nxt_of_dom] = after_lm
+        if world == 1:
+            step(dev_bufs[b], before=before)
+            if nxt_of_dom is None:
+                after_lm()
+            free[b].record(stream)
+        else:
+            stage(1 - b)  # the next step's inputs, while this step runs
+            step(dev_bufs[b], before=before, pre_finish=lambda: stream.wait_event(pushed[1 - b]))
+            if not finish_barrier:
+                step_barrier(stream)
+            bar_done.record(stream)
         with torch.cuda.stream(d2h):  # lm_head's C is complete after its GEMM (and, at N > 1, the barrier)
-            d2h.wait_event(lm_done if world == 1 else free[b])
+            d2h.wait_event(lm_done if world == 1 else bar_done)
             logits.copy_(c_of(dom)[(TOKENS - 1) * VOCAB:TOKENS * VOCAB], non_blocking=True)
             read_done.record(d2h)
 
-    for i in range(3):
+    if world > 1:  # the first step's inputs, staged before the loop
+        stage(0)
+        stream.wait_event(pushed[0])
+        step_barrier(stream)
+        bar_done.record(stream)
+    for i in range(4):  # an even count: the timed steps go on alternating the two input buffers
         e2e_step(i)
     torch.cuda.synchronize()
     if world > 1:
@@ -1244,9 +1309,16 @@ def run(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
     e2e = {"value": round(STEP_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-           "h2d_bytes_per_step": int(hx["x"].numel() * 2 + hx["h"].numel() * 2), "d2h_bytes_per_step": VOCAB * 4,
+           "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": VOCAB * 4,
            "ms_per_step": round(e2e_ms, 4), "wall_ms_per_step": round(t_wall * 1e3 / n_e2e, 4), "steps": n_e2e,
-           "host_cpus": host_cpus}
+           "host_cpus": host_cpus,
+           "inputs": "all activations from this GPU's pinned host memory" if world == 1 else
+                     f"1/{world} of the activations from each rank's pinned host memory (h2d_bytes_per_step, per "
+                     f"rank), pushed to every peer by the copy engines over NVLink"}
+    if e2e_ipc:
+        del dev_bufs, full
+        for r in e2e_ipc:
+            r.close()
 
     # parity of every projection's C as every rank holds it after the last step (each peer's rows included),
     # against fp64 on sampled rows
@@ -1311,6 +1383,8 @@ def run(args):
         how = {"ce": "N-sharded, rows pushed to every peer at once by the copy engines",
                "ring": "N-sharded, rows pushed by the copy engines to one peer after another (ring order)",
                "ring2": "N-sharded, rows pushed by the copy engines along two rings of peers at once",
+               "ring4": "N-sharded in four column chunks, each chunk's rows pushed by the copy engines in ring order "
+                        "as soon as it is computed",
                "p2p": "N-sharded, rows stored into every peer's C by the GEMM epilogue (P2P)",
                "multicast": "N-sharded, rows stored through an NVLink multicast address by the GEMM epilogue",
                "allgather": "N-sharded, C exchanged by NCCL all-gather + layout kernel"}

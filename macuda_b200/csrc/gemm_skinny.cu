@@ -75,21 +75,21 @@ __global__ void __launch_bounds__(SK_WARPS * 32) tb200_gemm_skinny_kernel(const 
   // complete before touching memory, then let the next one be scheduled on SMs this grid leaves free
   const int b = blockIdx.y + z0;
   if (!g.Aarr && g.k <= 8192) {
-    // this warp's first chunks of A into L2 while the kernel before this one may still be finishing (waited for
-    // below, before any load): prefetches only move lines into L2, the point of coherence, so the loads after
-    // griddep_wait still read what that kernel wrote. Rows of up to 8192 columns only: measured back to back on
-    // one B200, 4096 x 4096 went from 9.0 to 8.5 us with it and 4096 x 14336 from 20.9 to 21.4 us
+    // this warp's chunks of A into L2 while the kernel before this one may still be finishing (waited for below,
+    // before any load): prefetches only move lines into L2, the point of coherence, so the loads after
+    // griddep_wait still read what that kernel wrote. All of them when the weights fit a third of L2, so that
+    // HBM streams them through the previous kernel's tail and the wait; else the first SK_UNROLL. Rows of up to
+    // 8192 columns only: measured back to back on one B200, the first chunks took 4096 x 4096 from 9.0 to 8.5 us
+    // and 4096 x 14336 from 20.9 to 21.4 us
     const int lane_ = threadIdx.x & 31, w_ = threadIdx.x >> 5;
     const int sl = S > 1 ? (int)(blockIdx.x % (unsigned)S) : 0;
     const int r = (int)(blockIdx.x / (unsigned)S) * SK_ROWS + (lane_ >> 1);
     const int nch = g.k >> 5, c0 = (int)((long long)sl * nch / S), c1 = (int)((long long)(sl + 1) * nch / S);
+    const bool whole = (long long)g.m * g.k * (long long)sizeof(T) * g.batch <= (48ll << 20);
+    const int j_end = whole || c0 + w_ + SK_UNROLL * SK_WARPS > c1 ? c1 : c0 + w_ + SK_UNROLL * SK_WARPS;
     if (r < g.m) {
       const T *row = (const T *)g.A + (long long)b * g.sA + (long long)r * g.lda + (lane_ & 1) * 16;
-#pragma unroll
-      for (int u = 0; u < SK_UNROLL; ++u) {
-        const int j = c0 + w_ + u * SK_WARPS;
-        if (j < c1) prefetch_l2(row + (long long)j * 32);
-      }
+      for (int j = c0 + w_; j < j_end; j += SK_WARPS) prefetch_l2(row + (long long)j * 32);
     }
   }
   griddep_wait();
