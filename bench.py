@@ -885,8 +885,9 @@ def run_single(args):
 
 # candidate plans at N > 1: which projections are N-sharded and how their rows reach the peers ("ce": the copy
 # engines push them after the GEMM, to every peer at once, overlapping the projections that follow; "ring": the
-# same pushes one peer after another in ring order; "ring2": two such rings at once; "ring4": the ring, with the
-# GEMM in four column chunks whose pushes start as each is computed; "p2p": the GEMM epilogue stores them into the
+# same pushes one peer after another in ring order; "ring2": two such rings at once; "ringx2": the ring, with the
+# GEMM in two column chunks (256 tokens each: the 256 x 256 pair tile still fits) whose pushes start as each is
+# computed; "p2p": the GEMM epilogue stores them into the
 # peers' C over NVLink); the others run whole on every rank. A plan uses one copy-engine mode. Each is timed as a
 # whole step on every rank at set-up and the fastest kept. The copy engines win with one peer and lose with more
 # (their pushes to several peers at once ran at 300-400 GB/s in all against 585-677 GB/s to one; along a ring
@@ -894,7 +895,7 @@ def run_single(args):
 _ALL = ("q", "k", "v", "o", "gate", "up", "down", "lm_head")
 PLANS = [
     {},
-    {"lm_head": "ce"}, {"lm_head": "ring"}, {"lm_head": "ring2"}, {"lm_head": "ring4"}, {"lm_head": "p2p"},
+    {"lm_head": "ce"}, {"lm_head": "ring"}, {"lm_head": "ring2"}, {"lm_head": "ringx2"}, {"lm_head": "p2p"},
     {"lm_head": "ring", "gate": "ring", "up": "ring"}, {"lm_head": "ring2", "gate": "ring2", "up": "ring2"},
     {"lm_head": "ce", "gate": "ce", "up": "ce"}, {"lm_head": "p2p", "gate": "ce", "up": "ce"},
     {"lm_head": "p2p", "gate": "p2p", "up": "p2p"},
@@ -965,8 +966,8 @@ def run(args):
         if exchange in ("auto", "ce"):
             copies = CopyStreams(world)
             ring1 = CopyStreams(world, lanes=1)
-            lanes = {"ce": copies, "ring": ring1, "ring2": CopyStreams(world, lanes=2), "ring4": ring1}
-            chunks_of = {"ring4": 4}  # column chunks of a copy-engine shard's GEMM (1 unless named here)
+            lanes = {"ce": copies, "ring": ring1, "ring2": CopyStreams(world, lanes=2), "ringx2": ring1}
+            chunks_of = {"ringx2": 2}  # column chunks of a copy-engine shard's GEMM (1 unless named here)
             plans = [pl for pl in PLANS if exchange == "auto" or all(v in lanes for v in pl.values())]
             if args.shard == "sharded":
                 plans = [{n: ("ce" if exchange == "ce" else "p2p") for n in names}]
@@ -981,7 +982,7 @@ def run(args):
 
             def plan_order(plan):
                 """copy-engine shards first (their copies overlap what follows), then epilogue shards, then whole"""
-                rank_of = {"ce": 0, "ring": 0, "ring2": 0, "ring4": 0, "p2p": 1}
+                rank_of = {"ce": 0, "ring": 0, "ring2": 0, "ringx2": 0, "p2p": 1}
                 return sorted(range(len(layers)), key=lambda i: (rank_of.get(plan.get(names[i]), 2), i))
 
             def runner_of(plan, i):
@@ -1288,6 +1289,21 @@ def run(args):
         stream.wait_event(pushed[0])
         step_barrier(stream)
         bar_done.record(stream)
+    # this box's host-to-device rate for one step's worth of this rank's inputs (pinned, one copy, 5 times): the
+    # e2e figure follows it wherever the copies outlast the step
+    probe_src = torch.empty(h2d_bytes, dtype=torch.uint8).pin_memory()
+    probe_dst = torch.empty(h2d_bytes, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
+    p0, p1 = ev(), ev()
+    with torch.cuda.stream(h2d):
+        probe_dst.copy_(probe_src, non_blocking=True)
+        p0.record(h2d)
+        for _ in range(5):
+            probe_dst.copy_(probe_src, non_blocking=True)
+        p1.record(h2d)
+    torch.cuda.synchronize()
+    h2d_gbps = h2d_bytes * 5 / (p0.elapsed_time(p1) * 1e-3) / 1e9
+    del probe_src, probe_dst
     for i in range(4):  # an even count: the timed steps go on alternating the two input buffers
         e2e_step(i)
     torch.cuda.synchronize()
@@ -1311,7 +1327,7 @@ def run(args):
     e2e = {"value": round(STEP_FLOP / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
            "h2d_bytes_per_step": h2d_bytes, "d2h_bytes_per_step": VOCAB * 4,
            "ms_per_step": round(e2e_ms, 4), "wall_ms_per_step": round(t_wall * 1e3 / n_e2e, 4), "steps": n_e2e,
-           "host_cpus": host_cpus,
+           "host_cpus": host_cpus, "h2d_probe_GBps": round(h2d_gbps, 1),
            "inputs": "all activations from this GPU's pinned host memory" if world == 1 else
                      f"1/{world} of the activations from each rank's pinned host memory (h2d_bytes_per_step, per "
                      f"rank), pushed to every peer by the copy engines over NVLink"}
@@ -1383,8 +1399,8 @@ def run(args):
         how = {"ce": "N-sharded, rows pushed to every peer at once by the copy engines",
                "ring": "N-sharded, rows pushed by the copy engines to one peer after another (ring order)",
                "ring2": "N-sharded, rows pushed by the copy engines along two rings of peers at once",
-               "ring4": "N-sharded in four column chunks, each chunk's rows pushed by the copy engines in ring order "
-                        "as soon as it is computed",
+               "ringx2": "N-sharded in two column chunks, each chunk's rows pushed by the copy engines in ring order "
+                         "as soon as it is computed",
                "p2p": "N-sharded, rows stored into every peer's C by the GEMM epilogue (P2P)",
                "multicast": "N-sharded, rows stored through an NVLink multicast address by the GEMM epilogue",
                "allgather": "N-sharded, C exchanged by NCCL all-gather + layout kernel"}

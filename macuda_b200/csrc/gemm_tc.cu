@@ -835,8 +835,8 @@ int launch_bn(const CUtensorMap &ta, const CUtensorMap &tb, const CUtensorMap &t
 
 // tile width BN -> k-chunks per stage: the widest single-CTA tile keeps one chunk (four stages of 48 KB);
 // narrower tiles take two so that each stage carries enough tensor work to cover its issue cost. A pair's
-// 256 x 256 tile has 32 KB per CTA per chunk and keeps one chunk (six stages); its 256 x 128 tile has
-// 24 KB and takes two (four stages of 48 KB).
+// 256 x 256 tile has 32 KB per CTA per chunk and keeps one chunk (six stages; two, in three stages, for launches
+// of three waves or more: launch_tc_impl); its 256 x 128 tile has 24 KB and takes two (four stages of 48 KB).
 constexpr int kc_for(int bn) { return bn >= 256 ? 1 : 2; }
 
 }  // namespace
@@ -886,7 +886,15 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
   memset(&p, 0, sizeof p);
   CUtensorMap ta, tb;
   bool ok;
-  const int kc = cg == 2 && bn == 256 ? 1 : kc_for(bn);
+  // the 256 x 256 pair tile: one 64-deep k-chunk per stage (six stages), or two (three stages: half the MMA
+  // thread's barrier waits and commits per k) for launches of at least three waves. Measured on the B200 against
+  // one chunk, bit-identical results: lm_head 128256 x 512 x 4096 1-1.5 % and 8192^3 4-6 % faster, gate 14336 x
+  // 512 x 4096 (1.5 waves) 2 % slower.
+  const char *ks_env = getenv("TB200_KSPLIT");
+  const long long pair_tiles = (long long)((g->m + 255) / 256) * ((g->n + 255) / 256) * (g->batch > 0 ? g->batch : 1);
+  const bool pair_kc2 = cg == 2 && bn == 256 && pair == 1 && !f32in && !g->gidx && !(ks_env && *ks_env == '1') &&
+                        pair_tiles >= 3LL * (num_sms / 2);
+  const int kc = cg == 2 && bn == 256 ? (pair_kc2 ? 2 : 1) : kc_for(bn);
   // pointer arrays: rank-2 template maps with a placeholder address, re-pointed per element on the device
   const void *baseA = ptr_ws ? (const void *)(uintptr_t)0x10000 : g->A;
   const void *baseB = ptr_ws ? (const void *)(uintptr_t)0x10000 : g->B;
@@ -1022,7 +1030,9 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
     if (bn == 128)
       rc = f32in ? launch_bn<1, 128, 2, 2>(ta, tb, tcm, p, num_sms, s) : launch_bn<0, 128, 2, 2>(ta, tb, tcm, p, num_sms, s);
     else
-      rc = f32in ? launch_bn<1, 256, 1, 2>(ta, tb, tcm, p, num_sms, s) : launch_bn<0, 256, 1, 2>(ta, tb, tcm, p, num_sms, s);
+      rc = f32in      ? launch_bn<1, 256, 1, 2>(ta, tb, tcm, p, num_sms, s)
+           : pair_kc2 ? launch_bn<0, 256, 2, 2>(ta, tb, tcm, p, num_sms, s)
+                      : launch_bn<0, 256, 1, 2>(ta, tb, tcm, p, num_sms, s);
   } else if (f32in) {
     switch (bn) {
       case 32: rc = launch_bn<1, 32, kc_for(32), 1>(ta, tb, tcm, p, num_sms, s); break;

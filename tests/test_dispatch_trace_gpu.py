@@ -42,7 +42,7 @@ EXPECTED = {
     "gate": ("tb200_gemm_tc<f16,BN=256,KC=1,CG=2>", 148),
     "up": ("tb200_gemm_tc<f16,BN=256,KC=1,CG=2>", 148),
     "down": ("tb200_gemm_tc<f16,BN=256,KC=1,CG=2,KS=2>", 128),
-    "lm_head": ("tb200_gemm_tc<f16,BN=256,KC=1,CG=2>", 148),
+    "lm_head": ("tb200_gemm_tc<f16,BN=256,KC=2,CG=2>", 148),  # 1002 pair tiles: two k-chunks a stage
     "decode": ("tb200_gemm_skinny<W=16,U=2,S=1>", 256),
 }
 
