@@ -885,9 +885,8 @@ def run_single(args):
 
 # candidate plans at N > 1: which projections are N-sharded and how their rows reach the peers ("ce": the copy
 # engines push them after the GEMM, to every peer at once, overlapping the projections that follow; "ring": the
-# same pushes one peer after another in ring order; "ring2": two such rings at once; "ringx2": the ring, with the
-# GEMM in two column chunks (256 tokens each: the 256 x 256 pair tile still fits) whose pushes start as each is
-# computed; "p2p": the GEMM epilogue stores them into the
+# same pushes one peer after another in ring order; "ring2": two such rings at once; "p2p": the GEMM
+# epilogue stores them into the
 # peers' C over NVLink); the others run whole on every rank. A plan uses one copy-engine mode. Each is timed as a
 # whole step on every rank at set-up and the fastest kept. The copy engines win with one peer and lose with more
 # (their pushes to several peers at once ran at 300-400 GB/s in all against 585-677 GB/s to one; along a ring
@@ -895,7 +894,7 @@ def run_single(args):
 _ALL = ("q", "k", "v", "o", "gate", "up", "down", "lm_head")
 PLANS = [
     {},
-    {"lm_head": "ce"}, {"lm_head": "ring"}, {"lm_head": "ring2"}, {"lm_head": "ringx2"}, {"lm_head": "p2p"},
+    {"lm_head": "ce"}, {"lm_head": "ring"}, {"lm_head": "ring2"}, {"lm_head": "p2p"},
     {"lm_head": "ring", "gate": "ring", "up": "ring"}, {"lm_head": "ring2", "gate": "ring2", "up": "ring2"},
     {"lm_head": "ce", "gate": "ce", "up": "ce"}, {"lm_head": "p2p", "gate": "ce", "up": "ce"},
     {"lm_head": "p2p", "gate": "p2p", "up": "p2p"},
@@ -965,9 +964,7 @@ def run(args):
                                       ShardedGemm, pick_fastest, step_barrier)
         if exchange in ("auto", "ce"):
             copies = CopyStreams(world)
-            ring1 = CopyStreams(world, lanes=1)
-            lanes = {"ce": copies, "ring": ring1, "ring2": CopyStreams(world, lanes=2), "ringx2": ring1}
-            chunks_of = {"ringx2": 2}  # column chunks of a copy-engine shard's GEMM (1 unless named here)
+            lanes = {"ce": copies, "ring": CopyStreams(world, lanes=1), "ring2": CopyStreams(world, lanes=2)}
             plans = [pl for pl in PLANS if exchange == "auto" or all(v in lanes for v in pl.values())]
             if args.shard == "sharded":
                 plans = [{n: ("ce" if exchange == "ce" else "p2p") for n in names}]
@@ -982,7 +979,7 @@ def run(args):
 
             def plan_order(plan):
                 """copy-engine shards first (their copies overlap what follows), then epilogue shards, then whole"""
-                rank_of = {"ce": 0, "ring": 0, "ring2": 0, "ringx2": 0, "p2p": 1}
+                rank_of = {"ce": 0, "ring": 0, "ring2": 0, "p2p": 1}
                 return sorted(range(len(layers)), key=lambda i: (rank_of.get(plan.get(names[i]), 2), i))
 
             def runner_of(plan, i):
@@ -999,7 +996,6 @@ def run(args):
                     g = runner_of(plan, i)
                     if g is ce[i]:
                         g.copies = cs
-                        g.chunks = chunks_of.get(plan[names[i]], 1)
                     if g.run(acts[layers[i]["src"]], stream) != 0:
                         raise RuntimeError(f"{names[i]}: GEMM failed")
                 if set(plan.values()) & set(lanes):
@@ -1042,7 +1038,6 @@ def run(args):
             for i in range(len(layers)):
                 if runners[i] is ce[i]:
                     runners[i].copies = copies
-                    runners[i].chunks = chunks_of.get(plan[names[i]], 1)
             if plan:
                 finish_barrier = True
 
@@ -1242,7 +1237,10 @@ def run(args):
         full = [torch.as_tensor(_DeviceArray(r.own, world * chunk, "<i2"), device="cuda").view(acts["x"].dtype)
                 for r in e2e_ipc]
         dev_bufs = [{"x": f[:nx].view(acts["x"].shape), "h": f[nx:nx + nh].view(acts["h"].shape)} for f in full]
-        in_lanes = CopyStreams(world, lanes=1)
+        # the plan's copy streams when it has them: the input pushes, enqueued at the start of a step, then run
+        # while the first GEMM computes and before the exchange of its rows; on streams of their own they ran
+        # alongside the exchange and slowed it (copy-engine pushes to several peers at once do not add up)
+        in_lanes = copies if copies is not None else CopyStreams(world, lanes=1)
         pushed = [torch.cuda.Event() for _ in range(2)]
         bar_done = torch.cuda.Event()
         bar_done.record(stream)
@@ -1399,8 +1397,6 @@ def run(args):
         how = {"ce": "N-sharded, rows pushed to every peer at once by the copy engines",
                "ring": "N-sharded, rows pushed by the copy engines to one peer after another (ring order)",
                "ring2": "N-sharded, rows pushed by the copy engines along two rings of peers at once",
-               "ringx2": "N-sharded in two column chunks, each chunk's rows pushed by the copy engines in ring order "
-                         "as soon as it is computed",
                "p2p": "N-sharded, rows stored into every peer's C by the GEMM epilogue (P2P)",
                "multicast": "N-sharded, rows stored through an NVLink multicast address by the GEMM epilogue",
                "allgather": "N-sharded, C exchanged by NCCL all-gather + layout kernel"}

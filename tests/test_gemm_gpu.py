@@ -127,6 +127,18 @@ def test_pair_tile_large_and_batched(lib, h):
     assert_ok(run_and_check(lib, h, m=1000, n=700, k=520, batch=3, seed=18), "batched")
 
 
+@pytest.mark.parametrize("case", [
+    dict(m=30001, n=777, k=4104, mode="ex"),                       # k % 128 = 8: the last stage's second chunk
+    dict(m=8000, n=1000, k=1000, opA=0, opB=1, batch=2),           # lies past k; both operands MN-major
+    dict(m=20000, n=600, k=2000, in_t=O.BF16, out_t=O.F16, alpha=0.5, beta=-1.0, mode="ex"),
+], ids=["ragged-k-tail", "mn-major-batched", "bf16-alpha-beta"])
+def test_pair_tile_two_chunks_per_stage(lib, h, monkeypatch, case):
+    """The 256 x 256 pair tile with two k-chunks per stage (launches of three waves or more: 472, 256 and 237 pair
+    tiles on 74 pairs), against the oracle."""
+    monkeypatch.setenv("TB200_TC_BN", "pair")
+    assert_ok(run_and_check(lib, h, seed=case["m"] + case["k"], sample=160, edges=True, **case), "two chunks a stage")
+
+
 def test_strided_batch_and_broadcast(lib, h):
     # folded-GQA shape family of config 3 (small): KQ-like and KQV-like
     assert_ok(run_and_check(lib, h, m=512, n=256, k=128, batch=4, seed=21), "KQ-like")
