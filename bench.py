@@ -1241,21 +1241,24 @@ def run(args):
         # while the first GEMM computes and before the exchange of its rows; on streams of their own they ran
         # alongside the exchange and slowed it (copy-engine pushes to several peers at once do not add up)
         in_lanes = copies if copies is not None else CopyStreams(world, lanes=1)
-        pushed = [torch.cuda.Event() for _ in range(2)]
         bar_done = torch.cuda.Event()
         bar_done.record(stream)
         h2d_bytes = int(chunk * esz)
 
-        def stage(b):
+        def stage(b):  # this rank's slice from the host, at the start of the step before the one that reads it
             with torch.cuda.stream(h2d):
                 h2d.wait_event(bar_done)  # every rank has passed the barrier after buffer b's last reader
                 full[b][rank * chunk:(rank + 1) * chunk].copy_(hshard, non_blocking=True)
+
+        def push(b):
+            """The slice to every peer, queued on the copy streams after this step's exchange (which is the
+            step's longest path: the pushes ahead of it, waiting for the host copy, delayed it), then the compute
+            stream waits for them before the step's barrier."""
             in_lanes.after(h2d)
             if lib.lib.tb200_push_block(e2e_ipc[b].array, world, rank, rank * chunk, chunk, 0, 1, world * chunk, esz,
                                         in_lanes.array, in_lanes.lanes) != 0:
                 raise RuntimeError("tb200_push_block failed")
-            in_lanes.join(h2d)
-            pushed[b].record(h2d)
+            in_lanes.join(stream)
 
     def e2e_step(i):
         b = i % 2
@@ -1273,7 +1276,7 @@ def run(args):
             free[b].record(stream)
         else:
             stage(1 - b)  # the next step's inputs, while this step runs
-            step(dev_bufs[b], before=before, pre_finish=lambda: stream.wait_event(pushed[1 - b]))
+            step(dev_bufs[b], before=before, pre_finish=lambda: push(1 - b))
             if not finish_barrier:
                 step_barrier(stream)
             bar_done.record(stream)
@@ -1284,7 +1287,7 @@ def run(args):
 
     if world > 1:  # the first step's inputs, staged before the loop
         stage(0)
-        stream.wait_event(pushed[0])
+        push(0)
         step_barrier(stream)
         bar_done.record(stream)
     # this box's host-to-device rate for one step's worth of this rank's inputs (pinned, one copy, 5 times): the
