@@ -146,6 +146,16 @@ def test_strided_batch_and_broadcast(lib, h):
     assert_ok(run_and_check(lib, h, m=256, n=128, k=256, batch=3, sA=0, seed=23), "A broadcast (stride 0)")
 
 
+@pytest.mark.parametrize("store", ["1", "0"])
+def test_strided_batch_store_paths(lib, h, monkeypatch, store):
+    """Strided batches through both epilogues: the per-lane stores (their default) and the rank-3 TMA-store map
+    (TB200_TMA_STORE=1), ragged tiles, f32 and f16 C."""
+    monkeypatch.setenv("TB200_TMA_STORE", store)
+    assert_ok(run_and_check(lib, h, m=1000, n=300, k=136, batch=3, seed=24, edges=True), f"f32 C, store {store}")
+    assert_ok(run_and_check(lib, h, m=520, n=264, k=256, batch=2, out_t=O.F16, seed=25, edges=True),
+              f"f16 C, store {store}")
+
+
 def test_ldc_padding_and_offset_base(lib, h):
     assert_ok(run_and_check(lib, h, m=200, n=72, k=256, ldc=203, c_offset=1, seed=31), "ldc 203, base+4B")
 
