@@ -249,8 +249,8 @@ def run_cpu_baseline():
 
 
 def decode_figures(torch, lib, cb, dtype_code, dtype):
-    """Config 4: n in {1, 2, 4, 8} against the four weight shapes, HBM GB/s of the skinny kernel.
-    Weight copies rotate so that the bytes touched per pass exceed twice L2."""
+    """Config 4: n in {1, 2, 4, 8} against the four weight shapes, HBM GB/s of the skinny kernel (median of three
+    repeats of back-to-back calls). Weight copies rotate so that the bytes touched per pass exceed twice L2."""
     out = {}
     h = lib.handle()
     s = torch.cuda.current_stream()
@@ -269,14 +269,17 @@ def decode_figures(torch, lib, cb, dtype_code, dtype):
                                  dtype_code, k, 0.0, c.data_ptr(), cb.CUDA_R_32F, m, cb.CUBLAS_COMPUTE_32F)
             for i in range(copies):
                 one(i)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            torch.cuda.synchronize()
-            e0.record(s)
-            for i in range(reps):
-                one(i)
-            e1.record(s)
-            torch.cuda.synchronize()
-            us = e0.elapsed_time(e1) * 1e3 / reps
+            times = []
+            for _ in range(3):  # median of three repeats of back-to-back calls
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record(s)
+                for i in range(reps):
+                    one(i)
+                e1.record(s)
+                torch.cuda.synchronize()
+                times.append(e0.elapsed_time(e1) * 1e3 / reps)
+            us = statistics.median(times)
             byts = m * k * 2 + n * k * 2 + m * n * 4
             out[f"{m}x{k}_n{n}"] = {"us": round(us, 2), "GB/s": round(byts / us / 1e3, 1)}
         del ws
