@@ -1240,9 +1240,9 @@ def run(args):
         full = [torch.as_tensor(_DeviceArray(r.own, world * chunk, "<i2"), device="cuda").view(acts["x"].dtype)
                 for r in e2e_ipc]
         dev_bufs = [{"x": f[:nx].view(acts["x"].shape), "h": f[nx:nx + nh].view(acts["h"].shape)} for f in full]
-        # the plan's copy streams when it has them: the input pushes, enqueued at the start of a step, then run
-        # while the first GEMM computes and before the exchange of its rows; on streams of their own they ran
-        # alongside the exchange and slowed it (copy-engine pushes to several peers at once do not add up)
+        # the plan's copy streams when it has them: the input pushes then queue behind the step's exchange on
+        # the same engines instead of running alongside it (on streams of their own they slowed it: copy-engine
+        # pushes to several peers at once do not add up)
         in_lanes = copies if copies is not None else CopyStreams(world, lanes=1)
         bar_done = torch.cuda.Event()
         bar_done.record(stream)
