@@ -108,6 +108,7 @@ struct TcParams {
   // shared memory and one lane stores them as one tiled copy into this GPU's own C (plain GEMMs and strided
   // batches with beta == 0; the map covers m x n (x batch), so rows and columns past the ends are clipped)
   int c_tma, c_batched;
+  int epi_pipe;  // plain f32 per-lane stores in 16-column halves, the next half's TMEM load in flight
   // bounded waits: budget of every pipeline wait in SM cycles (WAIT_BUDGET_CYC unless a test shortens it), and
   // the test-only stall: the MMA thread first waits on a barrier nothing arrives at, so that its wait runs out
   uint64_t wait_budget;
@@ -650,11 +651,40 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
           }
         }
       };
+      if (KS == 1 && p.epi_pipe && !p.c_tma && p.out_type == 0 && p.beta == 0.f && !p.gidx && !p.nrep && !p.mc) {
+        // plain f32 per-lane stores in 16-column halves: the next half's TMEM load is in flight while this half's
+        // stores issue (the same 32 registers as one 32-column chunk)
+        uint32_t ha[16], hb[16];
+        auto store_half = [&](const uint32_t(&h)[16], int hh) {
+          const int col0 = n0 + hh * 16;
+          if (row_ok && col0 < tc.n_end) {
+            const int ncols = tc.n_end - col0 < 16 ? tc.n_end - col0 : 16;
+            float *dst = (float *)Cb + row + (long long)col0 * p.ldc;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              if (j < ncols) dst[(long long)j * p.ldc] = p.alpha * __uint_as_float(h[j]);
+          }
+        };
+        const int h_lo = 2 * (c_lo + g_lo), h_hi = 2 * (c_lo + g_lo + g_n);  // an even count of halves
+        tmem_ld_32x32b_x16(t_chunk0 + (uint32_t)(h_lo * 16), ha);
+        tmem_ld_wait_regs16(ha);
 #pragma unroll 1
-      for (int c = c_lo + g_lo; c < c_lo + g_lo + g_n; ++c) {
-        tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)(c * 32), ra);
-        tmem_ld_wait_regs(ra);
-        store_chunk(ra, c);
+        for (int hh = h_lo; hh < h_hi; hh += 2) {
+          tmem_ld_32x32b_x16(t_chunk0 + (uint32_t)((hh + 1) * 16), hb);
+          store_half(ha, hh);
+          tmem_ld_wait_regs16(hb);
+          const bool more = hh + 2 < h_hi;
+          if (more) tmem_ld_32x32b_x16(t_chunk0 + (uint32_t)((hh + 2) * 16), ha);
+          store_half(hb, hh + 1);
+          if (more) tmem_ld_wait_regs16(ha);
+        }
+      } else {
+#pragma unroll 1
+        for (int c = c_lo + g_lo; c < c_lo + g_lo + g_n; ++c) {
+          tmem_ld_32x32b_x32(t_chunk0 + (uint32_t)(c * 32), ra);
+          tmem_ld_wait_regs(ra);
+          store_chunk(ra, c);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -976,6 +1006,11 @@ static int launch_tc_impl(const tb200_gemm_t *g, int tile_n, int pair, int num_s
     if (!(e && *e == '0') && !ptr_ws && !g->nrep && !g->mc && !g->groups && !g->gidx && g->beta == 0.f && g->C &&
         ((uintptr_t)g->C & 15) == 0 && ((long long)g->ldc * esc) % 16 == 0 && (g->batch == 1 || batched_ok))
       p.c_tma = make_c_map(&tcm, g->out_type, g->C, g->m, g->n, g->ldc, g->batch, g->sC, &p.c_batched) ? 1 : 0;
+    // plain f32 per-lane stores drain TMEM in 16-column halves, the next half's load in flight while this half's
+    // stores issue: config 3's KQ 58.6-58.9 -> 57.1-57.3 us, KQV ~0.5 %, bit-identical C (same-process A/B, three
+    // rounds). TB200_EPI_PIPE=0 keeps the 32-column loop (bisecting; read per call)
+    const char *pipe = getenv("TB200_EPI_PIPE");
+    p.epi_pipe = !(pipe && *pipe == '0');
   }
   // TB200_WAIT_BUDGET_CYC shortens the pipeline waits' budget (tests; read per call); the drain waits after an
   // abort keep theirs. TB200_TEST_STALL=1 plants the MMA thread's wait that nothing completes (tests only).
