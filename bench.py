@@ -1183,8 +1183,11 @@ def run(args):
     roofline = {"bound": "tensor", "achieved": round(dom_tflops, 2), "peak": pk["bf16_tflops"],
                 "unit": "TFLOP/s", "frac": round(dom_tflops / pk["bf16_tflops"], 4), "traffic": traffic,
                 "kernel": "lm_head GEMM (%d x %d x %d)" % (m_run(dom), TOKENS, L["k"]),
-                "peak_source": pk["source"] + " bf16 burst (cuBLAS 8192^3, MEASURED_PEAKS.json): the timed region is "
-                               "%.1f ms long, far from the seconds-long loop of the sustained figure" % (ms * args.steps),
+                "peak_source": ("measured bf16 burst (cuBLAS 8192^3, MEASURED_PEAKS.json)" if pk["source"] == "measured"
+                                else "fallback bf16 burst (1.59 PFLOP/s, an earlier measurement on this pool: "
+                                     "MEASURED_PEAKS.json was absent)") +
+                               ": the timed region is %.1f ms long, far from the seconds-long loop of the sustained "
+                               "figure" % (ms * args.steps),
                 "frac_of_sustained": round(dom_tflops / pk["bf16_tflops_sustained"], 4),
                 "algorithmic_bytes": m_run(dom) * L["k"] * 2 + TOKENS * L["k"] * 2 + m_run(dom) * TOKENS * 4}
 
