@@ -1427,6 +1427,10 @@ def run(args):
                        "parallelism": par_note, "exchange": exchange if world > 1 else None,
                        "l2": "inputs larger than L2 (1.9 GB per step); no flush"},
             "frac_of_peak": round(value / pk["bf16_tflops"], 4),
+            # every fraction of a peak in this line (frac_of_peak, roofline, the configs' frac_of_measured_peak)
+            # divides by these: MEASURED_PEAKS.json's figures, or the profiling recipe's fallback when it is absent
+            "peaks": {"source": pk["source"], "hbm_gbs": pk["hbm_gbs"], "bf16_tflops": pk["bf16_tflops"],
+                      "bf16_tflops_sustained": pk["bf16_tflops_sustained"]},
             "parity": par,
             "roofline": roofline, "shapes": shapes,
             "shapes_note": "per-projection device time from %d further steps after the timed region, events around "
